@@ -1,0 +1,174 @@
+/*
+ * spardab200.h - C ABI of the B200 (sm_100a) forecast-guided block-sparse
+ * attention path.  Plain pointers and sizes only; every tensor is allocated by
+ * the caller, and no entry point allocates device memory.
+ *
+ * Conventions
+ *   - Strides are in ELEMENTS.  The innermost (head_dim) stride is always 1.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *   - Every call returns SD_OK (0) or a negative SD_ERR_* code; sd_strerror()
+ *     turns it into text.  Arguments are validated on the host before launch.
+ *   - Calls are asynchronous with respect to the host (stream-ordered) and
+ *     re-entrant for distinct streams and devices.
+ *   - `err` arguments (nullable) point to one device int32 that a kernel sets
+ *     to a nonzero SD_KERR_* code when a bounded wait gives up; kernels never
+ *     trap.
+ *
+ * Reference interfaces replaced (tyborra/local-research-Small-Language-Model):
+ *   model/forecast.py            KVBlockCompressor.forward, ForecastBlockSelector.forward
+ *   model/attention/sparse.py    gather_kv_blocks, SparseAttention._forward_decode_gather,
+ *                                _forward_masked_sdpa, _forward_chunked_gather
+ *   model/attention/base.py      KVCache.update
+ *   model/attention/async_offload.py  AsyncOffloadedKVCache.async_transfer_selected_blocks,
+ *                                AsyncForecastOffloadAttention.prefetch
+ */
+#ifndef SPARDAB200_H
+#define SPARDAB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SD_API __attribute__((visibility("default")))
+#else
+#define SD_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---- */
+#define SD_OK 0
+#define SD_ERR_INVALID (-1)     /* bad shape, stride, pointer or value */
+#define SD_ERR_UNSUPPORTED (-2) /* valid input outside what the kernels implement */
+#define SD_ERR_CUDA (-3)        /* a CUDA runtime call or launch failed */
+#define SD_ERR_ALIGN (-4)       /* a pointer or stride breaks the 16-byte rule of bulk copies */
+
+/* ---- device-side error words (written to *err) ---- */
+#define SD_KERR_TIMEOUT 1       /* a bounded mbarrier wait expired */
+#define SD_KERR_BOUNDS 2        /* a device-side length was outside the cache capacity */
+
+/* ---- element types ---- */
+#define SD_DTYPE_F32 0
+#define SD_DTYPE_BF16 1
+#define SD_DTYPE_F16 2
+
+/* ---- decode-time causal rules ----
+ * SD_RULE_REFERENCE: the reference's literal rule.  The selector is called
+ *   with one forecast row, so blocks j > 0 // block_size = 0 are masked to -inf
+ *   (model/forecast.py:120-126 called from model/attention/sparse.py:139).
+ * SD_RULE_ABSOLUTE: blocks after the block of the query's absolute position
+ *   are masked (what the reference's masked prefill does for every row).
+ * -inf (and other equal) scores are ordered by ascending block index. */
+#define SD_RULE_REFERENCE 0
+#define SD_RULE_ABSOLUTE 1
+
+SD_API const char *sd_strerror(int code);
+SD_API int sd_version(void);
+/* cudaError_t of the last failing CUDA call made by this library on this thread. */
+SD_API int sd_last_cuda_error(void);
+
+/* K1 - block compressor.  Replaces KVBlockCompressor.forward
+ * (model/forecast.py:57-78).  k: [B,T,H,D] with strides (sb, st, sh); writes
+ * reps: fp32 [B,NB,H,D] contiguous, NB = ceil(T / block_size), each entry the
+ * zero-padded block sum divided by block_size. */
+SD_API int sd_compress_blocks(const void *k, int dtype, int64_t B, int64_t T, int64_t H, int64_t D,
+                       int64_t sb, int64_t st, int64_t sh, int block_size, float *reps,
+                       void *stream);
+
+/* K2 - forecast block selector.  Replaces ForecastBlockSelector.forward
+ * (model/forecast.py:89-130).  forecast: [B,Tq,H,D] (strides f_sb, f_st, f_sh),
+ * reps: fp32 [B,NB,H,D] (strides r_sb, r_sn, r_sh).  scores = f.rep / sqrt(D)
+ * in fp32; if causal, blocks j > (t + q_offset) // block_size are -inf
+ * (q_offset = 0 is the reference).  Writes topk_idx int64 [B,H,Tq,k],
+ * k = min(top_k, NB), sorted by score descending (ties: ascending index), and,
+ * if scores != NULL, scores fp32 [B,H,Tq,NB].  D must be 16..256, a multiple of 4. */
+SD_API int sd_select_blocks(const void *forecast, int f_dtype, int64_t B, int64_t Tq, int64_t H,
+                     int64_t D, int64_t f_sb, int64_t f_st, int64_t f_sh, const float *reps,
+                     int64_t NB, int64_t r_sb, int64_t r_sn, int64_t r_sh, int top_k,
+                     int block_size, int causal, int64_t q_offset, float *scores,
+                     int64_t *topk_idx, void *stream);
+
+/* Top-k of fp32 rows, the ordering half of ForecastBlockSelector.forward
+ * (model/forecast.py:128-129, torch.topk(largest=True, sorted=True)).
+ * scores: [rows, n] with row stride ld; idx: int64 [rows, k]; vals (nullable):
+ * fp32 [rows, k].  Ties (including -inf) in ascending index order. k <= 64. */
+SD_API int sd_topk_rows(const float *scores, int64_t rows, int64_t n, int64_t ld, int k, int64_t *idx,
+                 float *vals, void *stream);
+
+/* K4 - block gather.  Replaces gather_kv_blocks (model/attention/sparse.py:19-62).
+ * k, v: [B,H,T,D] with strides (sb, sh, st); idx: int64 [B,H,S];
+ * k_out, v_out: [B,H,S*block_size,D] contiguous, rows at or past T are zero.
+ * Indices outside [0, ceil(T/block_size)) produce zero rows. */
+SD_API int sd_gather_kv_blocks(const void *k, const void *v, int dtype, int64_t B, int64_t H,
+                        int64_t T, int64_t D, int64_t sb, int64_t sh, int64_t st,
+                        const int64_t *idx, int64_t S, int block_size, void *k_out,
+                        void *v_out, void *stream);
+
+/* K3 - decode selected-set assembly.  Replaces model/attention/sparse.py:108-154
+ * (and the identical blocks of offload.py:175-240): {0, curr} U top-k
+ * (forecast != NULL) or the static window (forecast == NULL), future blocks
+ * cleared, listed in ascending order.  When ceil(L/bs) <= min(NB, top_k+2) every
+ * block is listed (the dense fallback, sparse.py:113-123).
+ * forecast: [B,H,D] (strides f_sb, f_sh), reps fp32 [B,NB,H,D] (strides).
+ * sel: int32 [B,H,ms_cap] (-1 padded), cnt: int32 [B,H].
+ * seq_len_k = L (tokens in the cache, the new one included). */
+SD_API int sd_decode_select(const void *forecast, int f_dtype, int64_t f_sb, int64_t f_sh,
+                     const float *reps, int64_t r_sb, int64_t r_sn, int64_t r_sh, int64_t B,
+                     int64_t H, int64_t D, int64_t seq_len_k, int block_size, int top_k,
+                     int rule, int32_t *sel, int32_t *cnt, int ms_cap, void *stream);
+
+/* K7 - block-sparse GQA decode attention.  Replaces the gather + mask +
+ * repeat_interleave + SDPA of model/attention/sparse.py:156-181.
+ * q: [B,Hq,D] (strides q_sb, q_sh); caches: [B,Hkv,Tcap,D] (strides c_sb, c_sh,
+ * c_st, identical for K and V); sel/cnt as produced by sd_decode_select
+ * (sel row stride ms_cap); keys = tokens of the listed blocks with pos < L.
+ * Query head h reads kv head h / (Hq/Hkv).  out: [B,Hq,D] (strides o_sb, o_sh).
+ * D = 64.  Selected K/V rows are staged into shared memory by bulk (TMA)
+ * copies, which need 16-byte aligned rows. */
+SD_API int sd_decode_attention(const void *q, int dtype, int64_t B, int64_t Hq, int64_t Hkv,
+                        int64_t D, int64_t q_sb, int64_t q_sh, const void *k_cache,
+                        const void *v_cache, int64_t c_sb, int64_t c_sh, int64_t c_st,
+                        int64_t Tcap, const int32_t *sel, const int32_t *cnt, int ms_cap,
+                        int64_t seq_len_k, int block_size, float scale, void *out,
+                        int64_t o_sb, int64_t o_sh, int32_t *err, void *stream);
+
+/* KV-cache append with the compressor fused in.  Replaces KVCache.update
+ * (model/attention/base.py:19-29) for the block-major cache of this library:
+ * k_cache, v_cache [B,H,Tcap,D] contiguous, proto_sum fp32 [B,H,NBcap,D]
+ * contiguous (running block sums; prototype = sum / block_size).
+ * xk, xv: [B,T,H,D] with strides (sb, st, sh); written at positions
+ * start .. start+T-1, then the sums of every touched block are recomputed. */
+SD_API int sd_kv_append(const void *xk, const void *xv, int dtype, int64_t B, int64_t T, int64_t H,
+                 int64_t D, int64_t sb, int64_t st, int64_t sh, void *k_cache, void *v_cache,
+                 float *proto_sum, int64_t Tcap, int64_t NBcap, int64_t start, int block_size,
+                 void *stream);
+
+/* Fused decode layer: RoPE + KV append + compressor update + selection +
+ * block-sparse attention, one CTA per (sequence, kv head).  Replaces
+ * SparseAttention.forward for T == 1 (model/attention/sparse.py:366-410 with
+ * _forward_decode_gather) from the point after the q/k/v projections.
+ * qkv: [B, (Hq+2*Hkv)*D] rows with stride qkv_sb (q | k | v, pre-RoPE).
+ * forecast (nullable): layer L-1's forecast [B,Hkv,D] with row stride f_sb.
+ * rope_cos/sin: fp32 [max_pos, D/2].  cur_len: device int32, tokens cached
+ * before this step (the new token is written at that position).
+ * Caches as in sd_kv_append.  out: [B, Hq*D] rows with stride o_sb.
+ * sel_out/cnt_out (nullable, together): the selected block list of every
+ * (sequence, kv head), int32 [B,Hkv,sel_cap] ascending and -1 padded, and its
+ * length int32 [B,Hkv]; sel_cap >= top_k + 2. */
+SD_API int sd_decode_layer(const void *qkv, int dtype, int64_t qkv_sb, const void *forecast,
+                    int f_dtype, int64_t f_sb, const float *rope_cos, const float *rope_sin,
+                    int64_t max_pos, const int32_t *cur_len, void *k_cache, void *v_cache,
+                    float *proto_sum, int64_t B, int64_t Hq, int64_t Hkv, int64_t D,
+                    int64_t Tcap, int64_t NBcap, int block_size, int top_k, int rule,
+                    float scale, void *out, int64_t o_sb, int32_t *sel_out, int32_t *cnt_out,
+                    int sel_cap, int32_t *err, void *stream);
+
+/* lens[i] += delta for i < n (device int32 array). */
+SD_API int sd_advance_len(int32_t *lens, int n, int delta, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SPARDAB200_H */

@@ -1,0 +1,122 @@
+"""Drop-in attention backend (model/attention/base.py, model/attention/sparse.py)
+whose hot path runs on the sm_100a kernels of libspardab200.so."""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from . import ops
+from .cache import B200KVCache
+from .forecast import ForecastBlockSelector, KVBlockCompressor
+from .rope import apply_rotary_emb
+
+
+class BaseAttention(nn.Module):
+    """model/attention/base.py:35-52: owns wq, wk, wv, wo (same state-dict keys)."""
+
+    def __init__(self, config, layer_idx: int):
+        super().__init__()
+        self.config = config
+        self.layer_idx = layer_idx
+        self.n_head = config.n_head
+        self.n_kv_head = config.n_kv_head
+        self.head_dim = config.head_dim
+        self.n_embd = config.n_embd
+        self.num_queries_per_kv = config.n_head // config.n_kv_head
+        self.wq = nn.Linear(self.n_embd, self.n_head * self.head_dim, bias=False)
+        self.wk = nn.Linear(self.n_embd, self.n_kv_head * self.head_dim, bias=False)
+        self.wv = nn.Linear(self.n_embd, self.n_kv_head * self.head_dim, bias=False)
+        self.wo = nn.Linear(self.n_head * self.head_dim, self.n_embd, bias=False)
+
+
+class B200SparseAttention(BaseAttention):
+    """Forecast-guided block-sparse GQA attention (SparseAttention,
+    model/attention/sparse.py:65-439) on B200 kernels.
+
+    Same constructor, state-dict keys and forward signature as the reference.
+    Decode (T == 1 with a cache) on a B200KVCache runs one fused kernel per
+    layer (RoPE + append + compressor update + selection + attention); any
+    other cache object with the reference's ``update``/``current_len`` API runs
+    the unfused kernels.  ``rule`` picks the decode-time causal rule of the
+    selector (see ops.RULES); the default reproduces the reference.
+    """
+
+    def __init__(self, config, layer_idx: int, mode: Optional[str] = None, rule: Optional[str] = None):
+        super().__init__(config, layer_idx)
+        self.block_size = config.block_size
+        self.top_k_blocks = config.top_k_blocks
+        if mode is not None:
+            self.mode = mode
+        elif config.attention_backend in ("static_sparse", "static"):
+            self.mode = "static"
+        elif getattr(config, "sparse_mode", "forecast") == "static":
+            self.mode = "static"
+        else:
+            self.mode = "forecast"
+        self.rule = rule or getattr(config, "selector_rule", "reference")
+        if self.rule not in ops.RULES:
+            raise ValueError(f"unknown selector rule {self.rule!r}")
+        self.compressor = KVBlockCompressor(self.block_size, self.head_dim, config.forecast_dim)
+        self.selector = ForecastBlockSelector(self.block_size, config.forecast_dim)
+        self._packed = None
+        self._packed_key = None
+        self.last_profile = {}
+
+    # -- fused projection weight [wq; wk; wv], rebuilt when any weight changes
+    def qkv_weight(self) -> torch.Tensor:
+        key = tuple((w.data_ptr(), w._version, w.dtype) for w in (self.wq.weight, self.wk.weight, self.wv.weight))
+        if self._packed is None or self._packed_key != key:
+            with torch.no_grad():
+                self._packed = torch.cat([self.wq.weight, self.wk.weight, self.wv.weight], dim=0).contiguous()
+            self._packed_key = key
+        return self._packed
+
+    def forward(self, x: torch.Tensor, rotary_emb, kv_cache=None, mask: Optional[torch.Tensor] = None,
+                is_causal: bool = True, forecast_vector: Optional[torch.Tensor] = None, **kwargs):
+        if kwargs.get("return_attn_weights", False):
+            raise NotImplementedError("return_attn_weights is a training/test feature of the reference backend")
+        b, t, _ = x.shape
+        if kv_cache is not None and t == 1:
+            if isinstance(kv_cache, B200KVCache):
+                return self._decode_fused(x, rotary_emb, kv_cache, forecast_vector)
+            return self._decode_generic(x, rotary_emb, kv_cache, forecast_vector)
+        return self._prefill(x, rotary_emb, kv_cache, mask, is_causal, forecast_vector, **kwargs)
+
+    def _decode_fused(self, x, rotary_emb, cache: B200KVCache, forecast_vector):
+        b = x.shape[0]
+        if cache.current_len >= cache.tcap:
+            raise ValueError(f"cache full: {cache.current_len} tokens of {cache.tcap}")
+        if rotary_emb.cos.shape[0] < cache.tcap:
+            rotary_emb._extend_cache(cache.tcap, x.device)
+        qkv = F.linear(x.view(b, self.n_embd), self.qkv_weight())
+        if qkv.dtype != cache.k_store.dtype:
+            qkv = qkv.to(cache.k_store.dtype)
+        f = forecast_vector if (self.mode == "forecast" and forecast_vector is not None) else None
+        out = ops.decode_layer(qkv, f, rotary_emb.cos, rotary_emb.sin, cache.len_dev, cache.k_store,
+                               cache.v_store, cache.proto_sum, self.n_head, self.n_kv_head, self.block_size,
+                               self.top_k_blocks, self.rule)
+        cache.advance(1, device=not getattr(cache, "shared_len", False))
+        return self.wo(out.to(x.dtype)).view(b, 1, self.n_embd)
+
+    def _decode_generic(self, x, rotary_emb, cache, forecast_vector):
+        b = x.shape[0]
+        xq = self.wq(x).view(b, 1, self.n_head, self.head_dim)
+        xk = self.wk(x).view(b, 1, self.n_kv_head, self.head_dim)
+        xv = self.wv(x).view(b, 1, self.n_kv_head, self.head_dim)
+        xq, xk = rotary_emb(xq, xk, offset=cache.current_len)
+        k_all, v_all = cache.update(xk, xv)
+        seq_len_k = cache.current_len
+        f = forecast_vector if (self.mode == "forecast" and forecast_vector is not None) else None
+        reps = self.compressor(k_all) if f is not None else None
+        sel, cnt = ops.decode_select(f, reps, seq_len_k, b, self.n_kv_head, self.head_dim, self.block_size,
+                                     self.top_k_blocks, self.rule, device=x.device)
+        out = ops.decode_attention(xq[:, 0], k_all.transpose(1, 2), v_all.transpose(1, 2), sel, cnt, seq_len_k,
+                                   self.block_size)
+        return self.wo(out.reshape(b, 1, self.n_head * self.head_dim).to(x.dtype))
+
+    def _prefill(self, x, rotary_emb, kv_cache, mask, is_causal, forecast_vector, **kwargs):
+        raise NotImplementedError("prefill kernels are not built yet")

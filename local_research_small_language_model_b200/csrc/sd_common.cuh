@@ -1,0 +1,177 @@
+// Shared device/host helpers for the sm_100a kernels of this library.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "spardab200.h"
+
+namespace sd {
+
+// ---------------------------------------------------------------- host side
+void set_cuda_error(cudaError_t e);
+int check_launch();  // SD_OK or SD_ERR_CUDA after a launch
+
+inline bool dtype_ok(int dt) { return dt == SD_DTYPE_F32 || dt == SD_DTYPE_BF16 || dt == SD_DTYPE_F16; }
+inline int dtype_size(int dt) { return dt == SD_DTYPE_F32 ? 4 : 2; }
+inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+// 1/sqrt(D) rounded once to fp32, as a Python float scale is when it multiplies
+// an fp32 tensor (model/forecast.py:115-116).
+float inv_sqrt(int64_t d);
+// Raises a kernel's dynamic shared-memory limit when `bytes` exceeds 48 KB.
+int set_max_smem_raw(const void *func, size_t bytes);
+template <typename K> int set_max_smem(K *func, size_t bytes) {
+  return set_max_smem_raw(reinterpret_cast<const void *>(func), bytes);
+}
+
+// ---------------------------------------------------------------- conversions
+template <typename T> __device__ __forceinline__ float to_f(T x);
+template <> __device__ __forceinline__ float to_f<float>(float x) { return x; }
+template <> __device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 x) { return __bfloat162float(x); }
+template <> __device__ __forceinline__ float to_f<__half>(__half x) { return __half2float(x); }
+
+template <typename T> __device__ __forceinline__ T from_f(float x);
+template <> __device__ __forceinline__ float from_f<float>(float x) { return x; }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
+template <> __device__ __forceinline__ __half from_f<__half>(float x) { return __float2half_rn(x); }
+
+// Round a float to T's precision and back (identity for float).
+template <typename T> __device__ __forceinline__ float round_to(float x) { return to_f<T>(from_f<T>(x)); }
+
+// ---------------------------------------------------------------- PTX wrappers
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+// Make mbarrier initialisation visible to the async (bulk-copy) proxy.
+__device__ __forceinline__ void mbar_init_fence() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Waits for the given phase parity with a wall-clock bound (nanoseconds).
+// Returns false when the bound expired; never spins forever.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity,
+                                                  uint64_t limit_ns = 2000000000ull) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t i = 0; i < (1u << 30); ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 63u) == 0 && global_timer_ns() - t0 > limit_ns) return false;
+  }
+  return false;
+}
+
+// Bulk (TMA, non-tensor) copy global -> shared, completion counted on `bar`.
+// Both addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void *smem_dst, const void *gsrc, uint32_t bytes, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Orders this thread's earlier generic-proxy global writes before later
+// async-proxy (bulk copy) reads issued after a CTA barrier.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// ---------------------------------------------------------------- top-k
+// Total order used everywhere for top-k: larger value first; equal values
+// (including -inf) by ascending index.
+__device__ __forceinline__ bool better(float va, int ia, float vb, int ib) {
+  return va > vb || (va == vb && ia < ib);
+}
+
+// One warp selects the k best of n entries; entry j has value get(j).
+// Writes k (index, value) pairs in order.  Entries are visited without
+// mutation: round r takes the best entry strictly after round r-1's winner in
+// the total order.  NaN values are never selected.
+template <typename Get>
+__device__ __forceinline__ void warp_topk(Get get, int n, int k, int *out_idx, float *out_val) {
+  const int lane = threadIdx.x & 31;
+  float pv = INFINITY;
+  int pi = -1;
+  bool first = true;
+  for (int r = 0; r < k; ++r) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int j = lane; j < n; j += 32) {
+      const float v = get(j);
+      const bool elig = first || (v < pv) || (v == pv && j > pi);
+      if (elig && (bi == 0x7fffffff || better(v, j, bv, bi))) {
+        bv = v;
+        bi = j;
+      }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+      if (oi != 0x7fffffff && (bi == 0x7fffffff || better(ov, oi, bv, bi))) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if (lane == 0) {
+      out_idx[r] = bi == 0x7fffffff ? -1 : bi;
+      if (out_val) out_val[r] = bv;
+    }
+    pv = bv;
+    pi = bi;
+    first = false;
+  }
+}
+
+}  // namespace sd
+
+// Expands BODY with `T` bound to the element type of SD_DTYPE_* code `dt`;
+// returns SD_ERR_INVALID from the enclosing function for unknown codes.
+#define SD_DISPATCH_DTYPE(dt, T, ...)                 \
+  switch (dt) {                                       \
+    case SD_DTYPE_F32: {                              \
+      using T = float;                                \
+      __VA_ARGS__;                                    \
+    } break;                                          \
+    case SD_DTYPE_BF16: {                             \
+      using T = __nv_bfloat16;                        \
+      __VA_ARGS__;                                    \
+    } break;                                          \
+    case SD_DTYPE_F16: {                              \
+      using T = __half;                               \
+      __VA_ARGS__;                                    \
+    } break;                                          \
+    default:                                          \
+      return SD_ERR_INVALID;                          \
+  }

@@ -1,0 +1,493 @@
+// K7 block-sparse GQA decode attention and the fused decode layer
+// (RoPE + KV append + compressor update + selection + attention).
+//
+// Work split: one CTA (4 warps) per (sequence, kv head).  The selected KV
+// blocks are cut into tiles of at most 64 cached rows of ONE block; tiles are
+// staged into shared memory by bulk asynchronous copies (cp.async.bulk, the
+// non-tensor TMA path) into a 4-stage ring completed on mbarriers, so up to
+// 4 tiles (K and V) are in flight per CTA while the previous ones are consumed.
+// Warp w owns rows 16w..16w+15 of every tile and keeps an online-softmax state
+// for all G = Hq/Hkv query heads of the kv head; the four warp states are
+// merged at the end.  Scores are accumulated in fp32 and exponentiated in base 2.
+#include "sd_select_core.cuh"
+
+namespace sd {
+
+constexpr int kD = 64;          // head_dim the attention kernels implement
+constexpr int kRows = 64;       // rows per tile
+constexpr int kStages = 4;
+constexpr int kThreads = 128;
+constexpr int kMaxTiles = 256;
+constexpr float kLog2e = 1.4426950408889634f;
+
+// Per-lane feature layout of the QK^T product: lane l serves key group l>>3
+// and 8 features chosen so that the 8 lanes of a group read one K row with
+// conflict-free 16-byte shared loads.
+template <typename T> struct Feat {
+  static __device__ __forceinline__ int dim(int dc, int i) { return 8 * dc + i; }
+};
+template <> struct Feat<float> {
+  static __device__ __forceinline__ int dim(int dc, int i) { return i < 4 ? 4 * dc + i : 32 + 4 * dc + (i - 4); }
+};
+
+template <typename T> __device__ __forceinline__ void load8(const T *row, int dc, float (&x)[8]) {
+  const uint4 u = *reinterpret_cast<const uint4 *>(row + 8 * dc);
+  const T *e = reinterpret_cast<const T *>(&u);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) x[i] = to_f(e[i]);
+}
+template <> __device__ __forceinline__ void load8<float>(const float *row, int dc, float (&x)[8]) {
+  const float4 a = *reinterpret_cast<const float4 *>(row + 4 * dc);
+  const float4 b = *reinterpret_cast<const float4 *>(row + 32 + 4 * dc);
+  x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+  x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+}
+
+template <typename T> __device__ __forceinline__ float2 load2(const T *row, int lane) {
+  const T *p = row + 2 * lane;
+  return make_float2(to_f(p[0]), to_f(p[1]));
+}
+template <> __device__ __forceinline__ float2 load2<float>(const float *row, int lane) {
+  return *reinterpret_cast<const float2 *>(row + 2 * lane);
+}
+
+// Shared-memory carve-up common to both kernels.
+template <typename T, int G> struct AttnSmem {
+  T *k;            // [kStages][kRows][kD]
+  T *v;            // [kStages][kRows][kD]
+  uint64_t *full;  // [kStages]
+  float *q;        // [G][kD]
+  int *tile_tok;   // [kMaxTiles]
+  int *tile_n;     // [kMaxTiles]
+  float *red;      // [4][G][kD + 2]
+  char *tail;      // kernel-specific
+  static constexpr size_t bytes() {
+    return 2 * sizeof(T) * kStages * kRows * kD + sizeof(uint64_t) * kStages + sizeof(float) * G * kD +
+           2 * sizeof(int) * kMaxTiles + sizeof(float) * 4 * G * (kD + 2);
+  }
+  __device__ explicit AttnSmem(char *base) {
+    k = reinterpret_cast<T *>(base);
+    v = k + kStages * kRows * kD;
+    full = reinterpret_cast<uint64_t *>(v + kStages * kRows * kD);
+    q = reinterpret_cast<float *>(full + kStages);
+    tile_tok = reinterpret_cast<int *>(q + G * kD);
+    tile_n = tile_tok + kMaxTiles;
+    red = reinterpret_cast<float *>(tile_n + kMaxTiles);
+    tail = reinterpret_cast<char *>(red + 4 * G * (kD + 2));
+  }
+};
+
+// Fills the tile table from an ascending block list; returns the tile count.
+// Called by one thread.
+__device__ __forceinline__ int build_tiles(const int *list, int count, int64_t L, int bs, int *tile_tok,
+                                           int *tile_n) {
+  int nt = 0;
+  for (int i = 0; i < count; ++i) {
+    const int64_t j = list[i];
+    if (j < 0 || j * bs >= L) continue;  // invalid or empty block: nothing to stage
+    int64_t n = L - j * bs;
+    if (n > bs) n = bs;
+    for (int64_t r0 = 0; r0 < n && nt < kMaxTiles; r0 += kRows) {
+      tile_tok[nt] = static_cast<int>(j * bs + r0);
+      tile_n[nt] = static_cast<int>(n - r0 < kRows ? n - r0 : kRows);
+      ++nt;
+    }
+  }
+  return nt;
+}
+
+template <typename T, int G>
+__device__ __forceinline__ void issue_tile(AttnSmem<T, G> &S, int t, const T *kb, const T *vb, int64_t c_st) {
+  const int s = t % kStages;
+  const int tok = S.tile_tok[t], n = S.tile_n[t];
+  const uint32_t row_bytes = kD * sizeof(T);
+  mbar_arrive_expect_tx(&S.full[s], 2u * n * row_bytes);
+  T *kd = S.k + s * kRows * kD;
+  T *vd = S.v + s * kRows * kD;
+  if (c_st == kD) {
+    bulk_g2s(kd, kb + static_cast<int64_t>(tok) * kD, n * row_bytes, &S.full[s]);
+    bulk_g2s(vd, vb + static_cast<int64_t>(tok) * kD, n * row_bytes, &S.full[s]);
+  } else {
+    for (int r = 0; r < n; ++r) {
+      bulk_g2s(kd + r * kD, kb + static_cast<int64_t>(tok + r) * c_st, row_bytes, &S.full[s]);
+      bulk_g2s(vd + r * kD, vb + static_cast<int64_t>(tok + r) * c_st, row_bytes, &S.full[s]);
+    }
+  }
+}
+
+// Runs the staged attention over S.tile_* (ntiles) for the G query heads in
+// S.q (fp32).  Writes out[g * o_hs + d] (T).  Returns false (uniformly) when a
+// bounded wait expired; the caller reports it.  All threads call this.
+template <typename T, int G>
+__device__ bool attend_tiles(AttnSmem<T, G> &S, int ntiles, const T *kb, const T *vb, int64_t c_st,
+                             float scale_log2, T *out, int64_t o_hs) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int kg = lane >> 3, dc = lane & 7;
+  if (tid == 0) {
+    for (int t = 0; t < ntiles && t < kStages; ++t) issue_tile<T, G>(S, t, kb, vb, c_st);
+  }
+  float qr[G][8];
+#pragma unroll
+  for (int g = 0; g < G; ++g)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) qr[g][i] = S.q[g * kD + Feat<T>::dim(dc, i)] * scale_log2;
+  float m[G], l[G], acc[G][2];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    m[g] = -INFINITY;
+    l[g] = 0.f;
+    acc[g][0] = acc[g][1] = 0.f;
+  }
+  bool ok = true;
+  int t = 0;
+  for (; t < ntiles; ++t) {
+    const int s = t % kStages;
+    bool got = mbar_wait_bounded(&S.full[s], (t / kStages) & 1);
+    got = __all_sync(0xffffffffu, got);
+    if (got) {
+      const T *ks = S.k + s * kRows * kD;
+      const T *vs = S.v + s * kRows * kD;
+      int nv = S.tile_n[t] - 16 * warp;  // rows of this warp that hold keys
+      nv = nv < 0 ? 0 : (nv > 16 ? 16 : nv);
+      float sc[G][4];
+#pragma unroll
+      for (int it = 0; it < 4; ++it) {
+        const int r = 16 * warp + 4 * it + kg;
+        float x[8];
+        load8<T>(ks + r * kD, dc, x);
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          float p = 0.f;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) p = fmaf(qr[g][i], x[i], p);
+          p += __shfl_xor_sync(0xffffffffu, p, 1);
+          p += __shfl_xor_sync(0xffffffffu, p, 2);
+          p += __shfl_xor_sync(0xffffffffu, p, 4);
+          sc[g][it] = (4 * it + kg < nv) ? p : -INFINITY;
+        }
+      }
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float mt = fmaxf(fmaxf(sc[g][0], sc[g][1]), fmaxf(sc[g][2], sc[g][3]));
+        mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 8));
+        mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16));
+        const float mn = fmaxf(m[g], mt);
+        if (mn == -INFINITY) continue;  // no key seen yet (uniform per warp)
+        const float alpha = exp2f(m[g] - mn);
+        float ps = 0.f;
+#pragma unroll
+        for (int it = 0; it < 4; ++it) {
+          sc[g][it] = exp2f(sc[g][it] - mn);
+          ps += sc[g][it];
+        }
+        ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+        ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+        l[g] = l[g] * alpha + ps;
+        acc[g][0] *= alpha;
+        acc[g][1] *= alpha;
+        m[g] = mn;
+      }
+#pragma unroll
+      for (int kk = 0; kk < 16; ++kk) {
+        if (kk < nv) {
+          const float2 vv = load2<T>(vs + (16 * warp + kk) * kD, lane);
+#pragma unroll
+          for (int g = 0; g < G; ++g) {
+            const float p = __shfl_sync(0xffffffffu, sc[g][kk >> 2], (kk & 3) * 8);
+            if (m[g] != -INFINITY) {
+              acc[g][0] = fmaf(p, vv.x, acc[g][0]);
+              acc[g][1] = fmaf(p, vv.y, acc[g][1]);
+            }
+          }
+        }
+      }
+    }
+    if (__syncthreads_or(!got)) {
+      ok = false;
+      break;
+    }
+    if (tid == 0 && t + kStages < ntiles) issue_tile<T, G>(S, t + kStages, kb, vb, c_st);
+  }
+  if (!ok) {
+    // let the copies still in flight land before the CTA's shared memory is released
+    for (int u = t; u < ntiles && u < t + kStages; ++u) mbar_wait_bounded(&S.full[u % kStages], (u / kStages) & 1);
+    __syncthreads();
+    return false;
+  }
+  // merge the four warp states
+  float *rw = S.red + warp * G * (kD + 2);
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    if (lane == 0) {
+      rw[g * (kD + 2)] = m[g];
+      rw[g * (kD + 2) + 1] = l[g];
+    }
+    rw[g * (kD + 2) + 2 + 2 * lane] = acc[g][0];
+    rw[g * (kD + 2) + 3 + 2 * lane] = acc[g][1];
+  }
+  __syncthreads();
+  for (int e = tid; e < G * kD; e += blockDim.x) {
+    const int g = e / kD, d = e - g * kD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, S.red[(w * G + g) * (kD + 2)]);
+    float den = 0.f, num = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        const float *r = S.red + (w * G + g) * (kD + 2);
+        const float f = exp2f(r[0] - M);
+        den = fmaf(r[1], f, den);
+        num = fmaf(r[2 + d], f, num);
+      }
+    }
+    out[g * o_hs + d] = from_f<T>(den > 0.f ? num / den : 0.f);
+  }
+  return true;
+}
+
+__device__ __forceinline__ void report(int32_t *err, int code) {
+  if (err && threadIdx.x == 0) atomicExch(err, code);
+}
+
+template <typename T, int G>
+__device__ __forceinline__ void init_barriers(AttnSmem<T, G> &S) {
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) mbar_init(&S.full[s], 1);
+    mbar_init_fence();
+  }
+}
+
+// ------------------------------------------------------------ API kernel
+template <typename T, int G>
+__global__ void __launch_bounds__(kThreads)
+    decode_attention_kernel(const T *__restrict__ q, int Hkv, int64_t q_sb, int64_t q_sh, const T *k_cache,
+                            const T *v_cache, int64_t c_sb, int64_t c_sh, int64_t c_st,
+                            const int32_t *__restrict__ sel, const int32_t *__restrict__ cnt, int ms_cap,
+                            int64_t L, int bs, float scale_log2, T *__restrict__ out, int64_t o_sb,
+                            int64_t o_sh, int32_t *err) {
+  extern __shared__ __align__(128) char smem_raw[];
+  AttnSmem<T, G> S(smem_raw);
+  int *list = reinterpret_cast<int *>(S.tail);
+  __shared__ int ntiles;
+  const int b = blockIdx.x / Hkv, h = blockIdx.x - (blockIdx.x / Hkv) * Hkv;
+  init_barriers(S);
+  for (int e = threadIdx.x; e < G * kD; e += blockDim.x) {
+    const int g = e / kD, d = e - g * kD;
+    S.q[e] = to_f(q[b * q_sb + static_cast<int64_t>(h * G + g) * q_sh + d]);
+  }
+  const int32_t *srow = sel + static_cast<int64_t>(blockIdx.x) * ms_cap;
+  int c = cnt[blockIdx.x];
+  c = c < 0 ? 0 : (c > ms_cap ? ms_cap : c);
+  for (int i = threadIdx.x; i < c; i += blockDim.x) list[i] = srow[i];
+  __syncthreads();
+  if (threadIdx.x == 0) ntiles = build_tiles(list, c, L, bs, S.tile_tok, S.tile_n);
+  __syncthreads();
+  const int64_t cb = b * c_sb + h * c_sh;
+  if (!attend_tiles<T, G>(S, ntiles, k_cache + cb, v_cache + cb, c_st, scale_log2,
+                          out + b * o_sb + static_cast<int64_t>(h * G) * o_sh, o_sh))
+    report(err, SD_KERR_TIMEOUT);
+}
+
+// ------------------------------------------------------------ fused layer
+// RoPE of one element with the reference's rounding sequence
+// (model/rope.py:58-63): tables cast to the activation dtype, then
+// x*cos and rotate_half(x)*sin and their sum each rounded to the dtype.
+template <typename T>
+__device__ __forceinline__ float rope_elem(float x, float partner, int d, float c, float s) {
+  const float cc = round_to<T>(c), ss = round_to<T>(s);
+  const float rot = d < kD / 2 ? -partner : partner;
+  const float a = round_to<T>(__fmul_rn(x, cc));
+  const float bq = round_to<T>(__fmul_rn(rot, ss));
+  return round_to<T>(__fadd_rn(a, bq));
+}
+
+template <typename T, typename F, int G>
+__global__ void __launch_bounds__(kThreads)
+    decode_layer_kernel(const T *__restrict__ qkv, int64_t qkv_sb, const F *__restrict__ fc, int64_t f_sb,
+                        const float *__restrict__ rcos, const float *__restrict__ rsin,
+                        const int32_t *__restrict__ cur_len, T *k_cache, T *v_cache, float *proto_sum, int Hkv,
+                        int64_t Tcap, int64_t NBcap, int bs, int top_k, int rule, float sel_scale,
+                        float scale_log2, T *__restrict__ out, int64_t o_sb, int32_t *sel_out,
+                        int32_t *cnt_out, int sel_cap, int32_t *err) {
+  extern __shared__ __align__(128) char smem_raw[];
+  AttnSmem<T, G> S(smem_raw);
+  __shared__ int count, ntiles;
+  const int b = blockIdx.x / Hkv, h = blockIdx.x - (blockIdx.x / Hkv) * Hkv;
+  const int Hq = Hkv * G;
+  const int64_t pos = *cur_len;
+  if (pos < 0 || pos >= Tcap) {  // cache full (or corrupt length): write nothing
+    report(err, SD_KERR_BOUNDS);
+    return;
+  }
+  const int64_t L = pos + 1;
+  const int curr = static_cast<int>(pos / bs);
+  const int nb = curr + 1;
+  const int ms = nb < top_k + 2 ? nb : top_k + 2;
+  float *f_s = reinterpret_cast<float *>(S.tail);  // [kD]
+  float *sc = f_s + kD;                            // [nb]
+  int *list = reinterpret_cast<int *>(sc + nb);    // [max(nb, top_k + 2)]
+  int *tk = list + (nb > top_k + 2 ? nb : top_k + 2);
+  init_barriers(S);
+
+  // -- 1. RoPE, append, compressor running sum
+  const T *row = qkv + b * qkv_sb;
+  const float *cr = rcos + pos * (kD / 2);
+  const float *sr = rsin + pos * (kD / 2);
+  const int64_t bh = static_cast<int64_t>(b) * Hkv + h;
+  if (threadIdx.x < kD) {
+    const int d = threadIdx.x;
+    const T *kr = row + static_cast<int64_t>(Hq + h) * kD;
+    const float x = to_f(kr[d]);
+    const float pr = to_f(kr[d < kD / 2 ? d + kD / 2 : d - kD / 2]);
+    const float y = rope_elem<T>(x, pr, d, cr[d & (kD / 2 - 1)], sr[d & (kD / 2 - 1)]);
+    const int64_t off = (bh * Tcap + pos) * kD + d;
+    k_cache[off] = from_f<T>(y);
+    v_cache[off] = row[static_cast<int64_t>(Hq + Hkv + h) * kD + d];
+    float *ps = proto_sum + (bh * NBcap + curr) * kD + d;
+    *ps = (pos % bs == 0 ? 0.f : *ps) + y;
+    fence_proxy_async_global();
+  } else {
+    for (int e = threadIdx.x - kD; e < G * kD; e += blockDim.x - kD) {
+      const int g = e / kD, d = e - g * kD;
+      const T *qr = row + static_cast<int64_t>(h * G + g) * kD;
+      const float x = to_f(qr[d]);
+      const float pr = to_f(qr[d < kD / 2 ? d + kD / 2 : d - kD / 2]);
+      S.q[e] = rope_elem<T>(x, pr, d, cr[d & (kD / 2 - 1)], sr[d & (kD / 2 - 1)]);
+    }
+  }
+  if (fc != nullptr && threadIdx.x < kD) f_s[threadIdx.x] = to_f(fc[b * f_sb + h * kD + threadIdx.x]);
+  __syncthreads();
+
+  // -- 2. selection over this layer's prototypes (sum / bs)
+  int n_scored = 0;
+  if (fc != nullptr && nb > ms) {
+    n_scored = rule == SD_RULE_REFERENCE ? 1 : nb;
+    score_blocks(proto_sum + bh * NBcap * kD, kD, kD, f_s, n_scored, sel_scale, sc);
+    __syncthreads();
+  }
+  build_decode_list(fc != nullptr, sc, n_scored, nb, curr, top_k, ms, tk, list, &count);
+  if (threadIdx.x == 0) ntiles = build_tiles(list, count, L, bs, S.tile_tok, S.tile_n);
+  if (sel_out) {
+    for (int i = threadIdx.x; i < sel_cap; i += blockDim.x) sel_out[bh * sel_cap + i] = i < count ? list[i] : -1;
+    if (threadIdx.x == 0) cnt_out[bh] = count;
+  }
+  __syncthreads();
+
+  // -- 3. attention over the selected blocks
+  const T *kb = k_cache + bh * Tcap * kD;
+  const T *vb = v_cache + bh * Tcap * kD;
+  if (!attend_tiles<T, G>(S, ntiles, kb, vb, kD, scale_log2, out + b * o_sb + static_cast<int64_t>(h * G) * kD,
+                          kD))
+    report(err, SD_KERR_TIMEOUT);
+}
+
+template <typename T, int G> int launch_decode_attention(const void *q, int64_t B, int64_t Hkv, int64_t q_sb,
+                                                         int64_t q_sh, const void *kc, const void *vc,
+                                                         int64_t c_sb, int64_t c_sh, int64_t c_st,
+                                                         const int32_t *sel, const int32_t *cnt, int ms_cap,
+                                                         int64_t L, int bs, float scale, void *out, int64_t o_sb,
+                                                         int64_t o_sh, int32_t *err, cudaStream_t s) {
+  const size_t smem = AttnSmem<T, G>::bytes() + sizeof(int) * ms_cap + 128;
+  auto kern = decode_attention_kernel<T, G>;
+  if (set_max_smem(kern, smem) != SD_OK) return SD_ERR_CUDA;
+  kern<<<static_cast<unsigned>(B * Hkv), kThreads, smem, s>>>(
+      static_cast<const T *>(q), (int)Hkv, q_sb, q_sh, static_cast<const T *>(kc), static_cast<const T *>(vc), c_sb,
+      c_sh, c_st, sel, cnt, ms_cap, L, bs, scale * kLog2e, static_cast<T *>(out), o_sb, o_sh, err);
+  return check_launch();
+}
+
+template <typename T, typename F, int G>
+int launch_decode_layer(const void *qkv, int64_t qkv_sb, const void *fc, int64_t f_sb, const float *rc,
+                        const float *rs, const int32_t *cur_len, void *kc, void *vc, float *ps, int64_t B,
+                        int64_t Hkv, int64_t Tcap, int64_t NBcap, int bs, int top_k, int rule, float scale,
+                        void *out, int64_t o_sb, int32_t *sel_out, int32_t *cnt_out, int sel_cap, int32_t *err,
+                        cudaStream_t s) {
+  const int64_t lst = NBcap > top_k + 2 ? NBcap : top_k + 2;
+  const size_t smem =
+      AttnSmem<T, G>::bytes() + sizeof(float) * (kD + NBcap) + sizeof(int) * (lst + top_k) + 128;
+  auto kern = decode_layer_kernel<T, F, G>;
+  if (set_max_smem(kern, smem) != SD_OK) return SD_ERR_CUDA;
+  kern<<<static_cast<unsigned>(B * Hkv), kThreads, smem, s>>>(
+      static_cast<const T *>(qkv), qkv_sb, static_cast<const F *>(fc), f_sb, rc, rs, cur_len,
+      static_cast<T *>(kc), static_cast<T *>(vc), ps, (int)Hkv, Tcap, NBcap, bs, top_k, rule,
+      scale / static_cast<float>(bs), scale * kLog2e, static_cast<T *>(out), o_sb, sel_out, cnt_out, sel_cap, err);
+  return check_launch();
+}
+
+}  // namespace sd
+
+#define SD_DISPATCH_G(G, ...)                          \
+  switch (G) {                                         \
+    case 1: { constexpr int GG = 1; __VA_ARGS__; } break; \
+    case 2: { constexpr int GG = 2; __VA_ARGS__; } break; \
+    case 3: { constexpr int GG = 3; __VA_ARGS__; } break; \
+    case 4: { constexpr int GG = 4; __VA_ARGS__; } break; \
+    case 6: { constexpr int GG = 6; __VA_ARGS__; } break; \
+    case 8: { constexpr int GG = 8; __VA_ARGS__; } break; \
+    default: return SD_ERR_UNSUPPORTED;                \
+  }
+
+extern "C" int sd_decode_attention(const void *q, int dtype, int64_t B, int64_t Hq, int64_t Hkv, int64_t D,
+                                   int64_t q_sb, int64_t q_sh, const void *k_cache, const void *v_cache,
+                                   int64_t c_sb, int64_t c_sh, int64_t c_st, int64_t Tcap, const int32_t *sel,
+                                   const int32_t *cnt, int ms_cap, int64_t seq_len_k, int block_size, float scale,
+                                   void *out, int64_t o_sb, int64_t o_sh, int32_t *err, void *stream) {
+  if (!q || !k_cache || !v_cache || !sel || !cnt || !out) return SD_ERR_INVALID;
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || seq_len_k <= 0 || seq_len_k > Tcap || block_size <= 0 ||
+      ms_cap <= 0)
+    return SD_ERR_INVALID;
+  if (D != sd::kD || B * Hkv > 0x7fffffff) return SD_ERR_UNSUPPORTED;
+  if (static_cast<int64_t>(ms_cap) * ((block_size + sd::kRows - 1) / sd::kRows) > sd::kMaxTiles)
+    return SD_ERR_UNSUPPORTED;
+  const int es = sd::dtype_size(dtype);
+  if (!sd::aligned16(k_cache) || !sd::aligned16(v_cache) || (c_sb * es) % 16 || (c_sh * es) % 16 ||
+      (c_st * es) % 16)
+    return SD_ERR_ALIGN;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int G = static_cast<int>(Hq / Hkv);
+  SD_DISPATCH_DTYPE(dtype, E, {
+    SD_DISPATCH_G(G, return sd::launch_decode_attention<E, GG>(q, B, Hkv, q_sb, q_sh, k_cache, v_cache, c_sb,
+                                                                c_sh, c_st, sel, cnt, ms_cap, seq_len_k,
+                                                                block_size, scale, out, o_sb, o_sh, err, s));
+  });
+  return SD_OK;
+}
+
+extern "C" int sd_decode_layer(const void *qkv, int dtype, int64_t qkv_sb, const void *forecast, int f_dtype,
+                               int64_t f_sb, const float *rope_cos, const float *rope_sin, int64_t max_pos,
+                               const int32_t *cur_len, void *k_cache, void *v_cache, float *proto_sum, int64_t B,
+                               int64_t Hq, int64_t Hkv, int64_t D, int64_t Tcap, int64_t NBcap, int block_size,
+                               int top_k, int rule, float scale, void *out, int64_t o_sb, int32_t *sel_out,
+                               int32_t *cnt_out, int sel_cap, int32_t *err, void *stream) {
+  if (!qkv || !rope_cos || !rope_sin || !cur_len || !k_cache || !v_cache || !proto_sum || !out)
+    return SD_ERR_INVALID;
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || block_size <= 0 || top_k <= 0 || Tcap <= 0 || NBcap <= 0 ||
+      max_pos < Tcap)
+    return SD_ERR_INVALID;
+  if (rule != SD_RULE_REFERENCE && rule != SD_RULE_ABSOLUTE) return SD_ERR_INVALID;
+  if (NBcap * block_size < Tcap) return SD_ERR_INVALID;
+  if ((sel_out == nullptr) != (cnt_out == nullptr) || (sel_out && sel_cap < top_k + 2)) return SD_ERR_INVALID;
+  if (D != sd::kD || top_k > 64 || NBcap > 16384 || B * Hkv > 0x7fffffff) return SD_ERR_UNSUPPORTED;
+  if (static_cast<int64_t>(top_k + 2) * ((block_size + sd::kRows - 1) / sd::kRows) > sd::kMaxTiles)
+    return SD_ERR_UNSUPPORTED;
+  if (!sd::aligned16(k_cache) || !sd::aligned16(v_cache) || !sd::aligned16(proto_sum)) return SD_ERR_ALIGN;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int G = static_cast<int>(Hq / Hkv);
+  const int fdt = forecast ? f_dtype : dtype;
+  SD_DISPATCH_DTYPE(dtype, E, {
+    if (fdt == dtype) {
+      SD_DISPATCH_G(G, return sd::launch_decode_layer<E, E, GG>(qkv, qkv_sb, forecast, f_sb, rope_cos, rope_sin,
+                                                                cur_len, k_cache, v_cache, proto_sum, B, Hkv,
+                                                                Tcap, NBcap, block_size, top_k, rule, scale, out,
+                                                                o_sb, sel_out, cnt_out, sel_cap, err, s));
+    } else if (fdt == SD_DTYPE_F32) {
+      SD_DISPATCH_G(G, return sd::launch_decode_layer<E, float, GG>(
+                           qkv, qkv_sb, forecast, f_sb, rope_cos, rope_sin, cur_len, k_cache, v_cache, proto_sum,
+                           B, Hkv, Tcap, NBcap, block_size, top_k, rule, scale, out, o_sb, sel_out, cnt_out, sel_cap, err, s));
+    } else {
+      return SD_ERR_UNSUPPORTED;
+    }
+  });
+  return SD_OK;
+}

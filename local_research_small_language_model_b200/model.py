@@ -1,0 +1,260 @@
+"""SparDA model driver on the B200 attention backend.
+
+The caller side of the hot path: SparDAResearchModel (model/model.py:14-191)
+and TransformerBlock (model/transformer.py:54-131) with the reference's module
+tree and state-dict keys, so reference checkpoints load unchanged, wired to
+B200SparseAttention.  Embedding, RMSNorm, SwiGLU and the tied head stay on
+PyTorch/cuBLAS.  ``DecodeEngine`` captures a whole greedy decode step (all
+layers, LM head and argmax) in one CUDA graph.
+"""
+
+from __future__ import annotations
+
+from typing import Dict, List, Optional
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from . import ops
+from .attention import B200SparseAttention
+from .cache import B200KVCache
+from .config import ModelConfig
+from .forecast import ForecastProjection
+from .rope import RotaryEmbedding
+
+
+class RMSNorm(nn.Module):
+    """model/norm.py:7-21."""
+
+    def __init__(self, dim: int, eps: float = 1e-6):
+        super().__init__()
+        self.eps = eps
+        self.weight = nn.Parameter(torch.ones(dim))
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        xf = x.float()
+        return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps)).type_as(x) * self.weight
+
+
+class TiedEmbedding(nn.Module):
+    """model/embeddings.py:8-32."""
+
+    def __init__(self, vocab_size: int, n_embd: int, initializer_range: float = 0.02):
+        super().__init__()
+        self.vocab_size = vocab_size
+        self.n_embd = n_embd
+        self.weight = nn.Parameter(torch.empty(vocab_size, n_embd))
+        nn.init.normal_(self.weight, mean=0.0, std=initializer_range)
+
+    def embed(self, ids: torch.Tensor) -> torch.Tensor:
+        return F.embedding(ids, self.weight)
+
+    def project(self, h: torch.Tensor) -> torch.Tensor:
+        return F.linear(h, self.weight)
+
+
+class SwiGLU(nn.Module):
+    """model/transformer.py:18-31."""
+
+    def __init__(self, n_embd: int, ffn_dim: int):
+        super().__init__()
+        self.w_gate = nn.Linear(n_embd, ffn_dim, bias=False)
+        self.w_up = nn.Linear(n_embd, ffn_dim, bias=False)
+        self.w_down = nn.Linear(ffn_dim, n_embd, bias=False)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return self.w_down(F.silu(self.w_gate(x)) * self.w_up(x))
+
+
+class TransformerBlock(nn.Module):
+    """model/transformer.py:54-131 with the B200 attention backend.
+
+    Decode on a B200KVCache uses one GEMM for [wq; wk; wv; wf] (the forecast
+    of layer L is computed from the same normalised input as L's q/k/v,
+    transformer.py:104-107) followed by the fused decode kernel."""
+
+    def __init__(self, config: ModelConfig, layer_idx: int):
+        super().__init__()
+        self.config = config
+        self.layer_idx = layer_idx
+        self.attn_norm = RMSNorm(config.n_embd, eps=config.norm_eps)
+        self.attention = B200SparseAttention(config, layer_idx)
+        self.forecast = ForecastProjection(config)
+        self.ffn_norm = RMSNorm(config.n_embd, eps=config.norm_eps)
+        self.ffn = SwiGLU(config.n_embd, config.ffn_dim)
+        self._packed = None
+        self._packed_key = None
+        # optional instrumentation of the fused decode kernel: {"start", "end"}
+        # timing events (external=True so they survive graph capture) and
+        # {"sel", "cnt"} buffers receiving the selected block lists
+        self.probe = None
+
+    def packed_weight(self) -> torch.Tensor:
+        ws = (self.attention.wq.weight, self.attention.wk.weight, self.attention.wv.weight, self.forecast.wf.weight)
+        key = tuple((w.data_ptr(), w._version, w.dtype) for w in ws)
+        if self._packed is None or self._packed_key != key:
+            with torch.no_grad():
+                self._packed = torch.cat(ws, dim=0).contiguous()
+            self._packed_key = key
+        return self._packed
+
+    def forward(self, x, rotary_emb, kv_cache=None, mask=None, is_causal=True, prev_layer_forecast=None,
+                next_layer_block=None, next_kv_cache=None):
+        normed = self.attn_norm(x)
+        b, t, c = x.shape
+        if isinstance(kv_cache, B200KVCache) and t == 1:
+            a = self.attention
+            proj = F.linear(normed.view(b, c), self.packed_weight())
+            nq = (a.n_head + 2 * a.n_kv_head) * a.head_dim
+            current_forecast = proj[:, nq:].view(b, 1, self.config.forecast_heads, self.config.forecast_dim)
+            if kv_cache.current_len >= kv_cache.tcap:
+                raise ValueError(f"cache full: {kv_cache.current_len} tokens of {kv_cache.tcap}")
+            if rotary_emb.cos.shape[0] < kv_cache.tcap:
+                rotary_emb._extend_cache(kv_cache.tcap, x.device)
+            f = prev_layer_forecast if (a.mode == "forecast" and prev_layer_forecast is not None) else None
+            probe = self.probe
+            if probe is not None:
+                probe["start"].record()
+            out = ops.decode_layer(proj[:, :nq], f, rotary_emb.cos, rotary_emb.sin, kv_cache.len_dev,
+                                   kv_cache.k_store, kv_cache.v_store, kv_cache.proto_sum, a.n_head, a.n_kv_head,
+                                   a.block_size, a.top_k_blocks, a.rule,
+                                   sel_out=probe["sel"] if probe is not None else None,
+                                   cnt_out=probe["cnt"] if probe is not None else None)
+            if probe is not None:
+                probe["end"].record()
+            kv_cache.advance(1, device=not getattr(kv_cache, "shared_len", False))
+            x = x + a.wo(out).view(b, 1, c)
+        else:
+            current_forecast = self.forecast(normed)
+            if next_layer_block is not None and next_kv_cache is not None and \
+                    hasattr(next_layer_block.attention, "prefetch"):
+                next_layer_block.attention.prefetch(forecast_vector=current_forecast, offload_cache=next_kv_cache)
+            x = x + self.attention(normed, rotary_emb=rotary_emb, kv_cache=kv_cache, mask=mask,
+                                   is_causal=is_causal, forecast_vector=prev_layer_forecast)
+        x = x + self.ffn(self.ffn_norm(x))
+        return x, current_forecast
+
+
+class SparDAB200Model(nn.Module):
+    """model/model.py:14-157 with B200 attention."""
+
+    def __init__(self, config: ModelConfig):
+        super().__init__()
+        self.config = config
+        self.embeddings = TiedEmbedding(config.vocab_size, config.n_embd, config.initializer_range)
+        self.rotary_emb = RotaryEmbedding(config.head_dim, config.context_length, config.rope_theta)
+        self.layers = nn.ModuleList([TransformerBlock(config, i) for i in range(config.n_layer)])
+        self.final_norm = RMSNorm(config.n_embd, eps=config.norm_eps)
+        self.apply(self._init_weights)
+        self._lens: Optional[torch.Tensor] = None
+
+    def _init_weights(self, module: nn.Module):
+        if isinstance(module, nn.Linear):
+            nn.init.normal_(module.weight, mean=0.0, std=self.config.initializer_range)
+        elif isinstance(module, nn.Embedding):
+            nn.init.normal_(module.weight, mean=0.0, std=self.config.initializer_range)
+
+    def allocate_caches(self, batch: int, max_seq_len: int, dtype: Optional[torch.dtype] = None,
+                        device=None) -> List[B200KVCache]:
+        """One B200KVCache per layer, sharing one device length array so a
+        decode step bumps all lengths with a single launch."""
+        cfg = self.config
+        device = device or self.embeddings.weight.device
+        dtype = dtype or self.embeddings.weight.dtype
+        self._lens = torch.zeros(cfg.n_layer, dtype=torch.int32, device=device)
+        caches = []
+        for i in range(cfg.n_layer):
+            c = B200KVCache(batch, max_seq_len, cfg.n_kv_head, cfg.head_dim, device, dtype, cfg.block_size,
+                            len_dev=self._lens[i:i + 1])
+            c.shared_len = True
+            caches.append(c)
+        self.rotary_emb._extend_cache(caches[0].tcap, device)
+        return caches
+
+    def forward(self, input_ids: torch.Tensor, targets: Optional[torch.Tensor] = None,
+                kv_caches: Optional[List] = None, return_forecasts: bool = False) -> Dict[str, torch.Tensor]:
+        b, t = input_ids.shape
+        x = self.embeddings.embed(input_ids)
+        forecasts = []
+        prev = None
+        for i, layer in enumerate(self.layers):
+            cache = kv_caches[i] if kv_caches is not None else None
+            nxt = self.layers[i + 1] if i + 1 < len(self.layers) else None
+            ncache = kv_caches[i + 1] if (kv_caches is not None and i + 1 < len(kv_caches)) else None
+            x, cur = layer(x=x, rotary_emb=self.rotary_emb, kv_cache=cache, mask=None, is_causal=True,
+                           prev_layer_forecast=prev, next_layer_block=nxt, next_kv_cache=ncache)
+            if return_forecasts:
+                forecasts.append(cur)
+            prev = cur
+        if kv_caches is not None and t == 1 and getattr(kv_caches[0], "shared_len", False) and \
+                kv_caches[0].len_dev.data_ptr() == self._lens.data_ptr():
+            ops.advance_len(self._lens, 1)
+        logits = self.embeddings.project(self.final_norm(x))
+        out = {"logits": logits}
+        if return_forecasts:
+            out["forecasts"] = forecasts
+        if targets is not None:
+            out["loss"] = F.cross_entropy(logits.view(-1, self.config.vocab_size), targets.view(-1),
+                                          ignore_index=-100)
+        return out
+
+
+class DecodeEngine:
+    """Greedy decode step of a SparDAB200Model captured in one CUDA graph.
+
+    ``ids`` (device, [B,1] int64) feeds the step; the graph writes the argmax
+    tokens to ``next_ids`` and copies them into ``ids`` so replays chain.
+    Cache lengths live on the device; the engine keeps the host copies in step.
+    """
+
+    def __init__(self, model: SparDAB200Model, caches: List[B200KVCache], batch: int):
+        self.model, self.caches, self.batch = model, caches, batch
+        dev = model.embeddings.weight.device
+        self.ids = torch.zeros(batch, 1, dtype=torch.long, device=dev)
+        self.next_ids = torch.zeros(batch, 1, dtype=torch.long, device=dev)
+        self.graph = None
+
+    def _body(self):
+        out = self.model(self.ids, kv_caches=self.caches)
+        self.next_ids.copy_(out["logits"][:, -1:, :].argmax(dim=-1))
+        self.ids.copy_(self.next_ids)
+
+    def _snapshot(self):
+        bs = self.caches[0].block_size
+        j = self.caches[0].current_len // bs
+        return [c.proto_sum[:, :, j].clone() for c in self.caches], j
+
+    def _restore(self, snap):
+        rows, j = snap
+        for c, r in zip(self.caches, rows):
+            c.proto_sum[:, :, j].copy_(r)
+            c.current_len -= 1
+        self.model._lens.sub_(1)
+
+    @torch.no_grad()
+    def capture(self) -> None:
+        """Warm-up (whose cache writes are rolled back) and graph capture."""
+        snap = self._snapshot()
+        saved = self.ids.clone()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            self._body()
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        self._restore(snap)
+        self.ids.copy_(saved)
+        self.graph = torch.cuda.CUDAGraph()
+        host_lens = [c.current_len for c in self.caches]
+        with torch.cuda.graph(self.graph):
+            self._body()
+        for c, n in zip(self.caches, host_lens):  # capture ran no kernels
+            c.current_len = n
+        torch.cuda.synchronize()
+
+    def step(self) -> torch.Tensor:
+        self.graph.replay()
+        for c in self.caches:
+            c.current_len += 1
+        return self.next_ids

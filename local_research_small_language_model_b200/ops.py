@@ -1,0 +1,240 @@
+"""Torch-tensor wrappers over the C ABI.  Every op requires CUDA tensors: there
+is no CPU path.  Each wrapper validates shapes, allocates its outputs with the
+caching allocator and launches on the current CUDA stream."""
+
+from __future__ import annotations
+
+import math
+from typing import Optional, Tuple
+
+import torch
+
+from . import _lib as L
+
+_DT = {torch.float32: L.SD_DTYPE_F32, torch.bfloat16: L.SD_DTYPE_BF16, torch.float16: L.SD_DTYPE_F16}
+RULES = {"reference": L.SD_RULE_REFERENCE, "absolute": L.SD_RULE_ABSOLUTE}
+
+_err_bufs = {}
+
+
+def dtype_code(t: torch.Tensor) -> int:
+    try:
+        return _DT[t.dtype]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {t.dtype}; expected float32, bfloat16 or float16") from None
+
+
+def _cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("the B200 kernels need CUDA tensors (this library has no CPU path)")
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _inner1(t: torch.Tensor) -> torch.Tensor:
+    return t if t.stride(-1) == 1 else t.contiguous()
+
+
+def error_buffer(device) -> torch.Tensor:
+    """Per-device int32 word the kernels set when a bounded wait expires."""
+    device = torch.device(device)
+    key = device.index if device.index is not None else torch.cuda.current_device()
+    buf = _err_bufs.get(key)
+    if buf is None:
+        buf = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", key))
+        _err_bufs[key] = buf
+    return buf
+
+
+def check_device_errors(device=None) -> None:
+    """Synchronises and raises if any kernel reported a device-side timeout."""
+    device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    buf = error_buffer(device)
+    if int(buf.item()) != 0:
+        code = int(buf.item())
+        buf.zero_()
+        raise L.SparDAError(f"a kernel gave up a bounded wait (device error code {code})")
+
+
+def num_blocks(t: int, bs: int) -> int:
+    return (t + bs - 1) // bs
+
+
+# ---------------------------------------------------------------- K1 compressor
+def compress_blocks(k: torch.Tensor, block_size: int) -> torch.Tensor:
+    """KVBlockCompressor.forward (model/forecast.py:57-78): k [B,T,H,D] ->
+    fp32 prototypes [B,N_b,H,D] (zero-padded block sum / block_size)."""
+    _cuda(k)
+    k = _inner1(k)
+    b, t, h, d = k.shape
+    reps = torch.empty(b, num_blocks(t, block_size), h, d, dtype=torch.float32, device=k.device)
+    L.call("sd_compress_blocks", k.data_ptr(), dtype_code(k), b, t, h, d, k.stride(0), k.stride(1), k.stride(2),
+           block_size, reps.data_ptr(), _stream(k))
+    return reps
+
+
+# ---------------------------------------------------------------- K2 selector
+def select_blocks(forecast: torch.Tensor, reps: torch.Tensor, top_k: int, block_size: int,
+                  is_causal: bool = True, q_offset: int = 0,
+                  return_scores: bool = True) -> Tuple[Optional[torch.Tensor], torch.Tensor]:
+    """ForecastBlockSelector.forward (model/forecast.py:89-130) in fp32.
+    forecast [B,Tq,H,D], reps [B,N_b,H,D] -> (scores [B,H,Tq,N_b] fp32, idx [B,H,Tq,k] int64)."""
+    _cuda(forecast, reps)
+    b, tq, h, d = forecast.shape
+    if reps.shape[0] != b or reps.shape[2] != h or reps.shape[3] != d:
+        raise AssertionError(f"Mismatch: forecast_heads ({h}) != n_kv_head ({reps.shape[2]})")
+    forecast = _inner1(forecast)
+    reps = _inner1(reps.float())
+    nb = reps.shape[1]
+    k = min(top_k, nb)
+    scores = torch.empty(b, h, tq, nb, dtype=torch.float32, device=forecast.device) if return_scores else None
+    idx = torch.empty(b, h, tq, k, dtype=torch.int64, device=forecast.device)
+    L.call("sd_select_blocks", forecast.data_ptr(), dtype_code(forecast), b, tq, h, d, forecast.stride(0),
+           forecast.stride(1), forecast.stride(2), reps.data_ptr(), nb, reps.stride(0), reps.stride(1),
+           reps.stride(2), top_k, block_size, int(bool(is_causal)), int(q_offset),
+           scores.data_ptr() if scores is not None else None, idx.data_ptr(), _stream(forecast))
+    return scores, idx
+
+
+def topk_rows(scores: torch.Tensor, k: int) -> Tuple[torch.Tensor, torch.Tensor]:
+    """torch.topk(scores, k, dim=-1) (largest, sorted) with ties in ascending index order."""
+    _cuda(scores)
+    s = _inner1(scores.float())
+    n = s.shape[-1]
+    flat = s.reshape(-1, n)
+    idx = torch.empty(flat.shape[0], k, dtype=torch.int64, device=s.device)
+    vals = torch.empty(flat.shape[0], k, dtype=torch.float32, device=s.device)
+    L.call("sd_topk_rows", flat.data_ptr(), flat.shape[0], n, flat.stride(0), k, idx.data_ptr(), vals.data_ptr(),
+           _stream(s))
+    return vals.view(*s.shape[:-1], k), idx.view(*s.shape[:-1], k)
+
+
+# ---------------------------------------------------------------- K4 gather
+def gather_kv_blocks(k: torch.Tensor, v: torch.Tensor, block_indices: torch.Tensor,
+                     block_size: int) -> Tuple[torch.Tensor, torch.Tensor]:
+    """gather_kv_blocks (model/attention/sparse.py:19-62): k, v [B,H,T,D],
+    indices [B,H,S] -> [B,H,S*block_size,D]."""
+    _cuda(k, v, block_indices)
+    if k.stride() != v.stride() or k.dtype != v.dtype:
+        k, v = k.contiguous(), v.contiguous()
+    k, v = _inner1(k), _inner1(v)
+    if k.stride() != v.stride():
+        k, v = k.contiguous(), v.contiguous()
+    b, h, t, d = k.shape
+    idx = block_indices.to(torch.int64).contiguous()
+    s = idx.shape[-1]
+    ko = torch.empty(b, h, s * block_size, d, dtype=k.dtype, device=k.device)
+    vo = torch.empty_like(ko)
+    L.call("sd_gather_kv_blocks", k.data_ptr(), v.data_ptr(), dtype_code(k), b, h, t, d, k.stride(0), k.stride(1),
+           k.stride(2), idx.data_ptr(), s, block_size, ko.data_ptr(), vo.data_ptr(), _stream(k))
+    return ko, vo
+
+
+# ---------------------------------------------------------------- K3 + K7 decode
+def decode_select(forecast: Optional[torch.Tensor], reps: Optional[torch.Tensor], seq_len_k: int, batch: int,
+                  n_kv_head: int, head_dim: int, block_size: int, top_k: int,
+                  rule: str = "reference", device=None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Selected-block list of a decode step (model/attention/sparse.py:108-154).
+    forecast [B,1,H,D] or [B,H,D] (or None: static window); reps [B,N_b,H,D] fp32.
+    Returns sel int32 [B,H,MS] (ascending, -1 padded) and cnt int32 [B,H]."""
+    nb = num_blocks(seq_len_k, block_size)
+    ms = min(nb, top_k + 2)
+    dev = forecast.device if forecast is not None else (reps.device if reps is not None else device)
+    _cuda(forecast, reps)
+    sel = torch.empty(batch, n_kv_head, ms, dtype=torch.int32, device=dev)
+    cnt = torch.empty(batch, n_kv_head, dtype=torch.int32, device=dev)
+    if forecast is not None:
+        f = _inner1(forecast.reshape(batch, n_kv_head, head_dim) if forecast.dim() == 4 else forecast)
+        r = _inner1(reps.float())
+        fargs = (f.data_ptr(), dtype_code(f), f.stride(0), f.stride(1))
+        rargs = (r.data_ptr(), r.stride(0), r.stride(1), r.stride(2))
+    else:
+        fargs = (None, L.SD_DTYPE_F32, 0, 0)
+        rargs = (None, 0, 0, 0)
+    L.call("sd_decode_select", *fargs, *rargs, batch, n_kv_head, head_dim, seq_len_k, block_size, top_k,
+           RULES[rule], sel.data_ptr(), cnt.data_ptr(), ms, torch.cuda.current_stream(dev).cuda_stream)
+    return sel, cnt
+
+
+def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, sel: torch.Tensor,
+                     cnt: torch.Tensor, seq_len_k: int, block_size: int,
+                     scale: Optional[float] = None) -> torch.Tensor:
+    """Block-sparse GQA decode attention (model/attention/sparse.py:156-181).
+    q [B,Hq,D]; caches [B,Hkv,Tcap,D] views (any strides with inner 1, same for K
+    and V); sel/cnt from decode_select.  Returns [B,Hq,D] in q's dtype."""
+    _cuda(q, k_cache, v_cache, sel, cnt)
+    b, hq, d = q.shape
+    hkv, tcap = k_cache.shape[1], k_cache.shape[2]
+    if k_cache.stride() != v_cache.stride():
+        raise ValueError("K and V caches must share strides")
+    q = _inner1(q)
+    if q.dtype != k_cache.dtype:
+        q = q.to(k_cache.dtype)
+    sel = sel.to(torch.int32).contiguous()
+    cnt = cnt.to(torch.int32).contiguous()
+    out = torch.empty(b, hq, d, dtype=k_cache.dtype, device=q.device)
+    sc = 1.0 / math.sqrt(d) if scale is None else scale
+    L.call("sd_decode_attention", q.data_ptr(), dtype_code(k_cache), b, hq, hkv, d, q.stride(0), q.stride(1),
+           k_cache.data_ptr(), v_cache.data_ptr(), k_cache.stride(0), k_cache.stride(1), k_cache.stride(2), tcap,
+           sel.data_ptr(), cnt.data_ptr(), sel.shape[-1], seq_len_k, block_size, sc, out.data_ptr(), out.stride(0),
+           out.stride(1), error_buffer(q.device).data_ptr(), _stream(q))
+    return out
+
+
+def kv_append(xk: torch.Tensor, xv: torch.Tensor, k_store: torch.Tensor, v_store: torch.Tensor,
+              proto_sum: torch.Tensor, start: int, block_size: int) -> None:
+    """Writes xk, xv [B,T,H,D] into the head-major stores [B,H,Tcap,D] at
+    positions start.. and refreshes the block sums [B,H,NBcap,D] they touch."""
+    _cuda(xk, xv, k_store, v_store, proto_sum)
+    if xk.stride() != xv.stride():
+        xk, xv = xk.contiguous(), xv.contiguous()
+    xk, xv = _inner1(xk.to(k_store.dtype)), _inner1(xv.to(v_store.dtype))
+    if xk.stride() != xv.stride():
+        xk, xv = xk.contiguous(), xv.contiguous()
+    b, t, h, d = xk.shape
+    L.call("sd_kv_append", xk.data_ptr(), xv.data_ptr(), dtype_code(k_store), b, t, h, d, xk.stride(0),
+           xk.stride(1), xk.stride(2), k_store.data_ptr(), v_store.data_ptr(), proto_sum.data_ptr(),
+           k_store.shape[2], proto_sum.shape[2], start, block_size, _stream(xk))
+
+
+def decode_layer(qkv: torch.Tensor, forecast: Optional[torch.Tensor], rope_cos: torch.Tensor,
+                 rope_sin: torch.Tensor, cur_len: torch.Tensor, k_store: torch.Tensor, v_store: torch.Tensor,
+                 proto_sum: torch.Tensor, n_head: int, n_kv_head: int, block_size: int, top_k: int,
+                 rule: str = "reference", scale: Optional[float] = None,
+                 out: Optional[torch.Tensor] = None, sel_out: Optional[torch.Tensor] = None,
+                 cnt_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Fused decode layer: RoPE + append + compressor update + selection +
+    attention (model/attention/sparse.py:366-410 + :99-183 for T == 1).
+    qkv [B,(Hq+2Hkv)*D] (pre-RoPE projections), forecast [B,Hkv,D] or None.
+    sel_out [B,Hkv,cap] / cnt_out [B,Hkv] int32 (optional) receive each
+    (sequence, kv head)'s selected block list.  Returns [B,Hq*D]."""
+    _cuda(qkv, forecast, rope_cos, rope_sin, cur_len, k_store, v_store, proto_sum)
+    b = qkv.shape[0]
+    d = k_store.shape[-1]
+    qkv = _inner1(qkv)
+    if out is None:
+        out = torch.empty(b, n_head * d, dtype=k_store.dtype, device=qkv.device)
+    if forecast is not None:
+        f = forecast.reshape(b, n_kv_head * d)
+        f = _inner1(f)
+        fargs = (f.data_ptr(), dtype_code(f), f.stride(0))
+    else:
+        fargs = (None, dtype_code(k_store), 0)
+    sc = 1.0 / math.sqrt(d) if scale is None else scale
+    L.call("sd_decode_layer", qkv.data_ptr(), dtype_code(qkv), qkv.stride(0), *fargs, rope_cos.data_ptr(),
+           rope_sin.data_ptr(), rope_cos.shape[0], cur_len.data_ptr(), k_store.data_ptr(), v_store.data_ptr(),
+           proto_sum.data_ptr(), b, n_head, n_kv_head, d, k_store.shape[2], proto_sum.shape[2], block_size, top_k,
+           RULES[rule], sc, out.data_ptr(), out.stride(0),
+           sel_out.data_ptr() if sel_out is not None else None,
+           cnt_out.data_ptr() if cnt_out is not None else None,
+           sel_out.shape[-1] if sel_out is not None else 0,
+           error_buffer(qkv.device).data_ptr(), _stream(qkv))
+    return out
+
+
+def advance_len(lens: torch.Tensor, delta: int = 1) -> None:
+    _cuda(lens)
+    L.call("sd_advance_len", lens.data_ptr(), lens.numel(), delta, _stream(lens))

@@ -1,0 +1,104 @@
+"""Drop-in boundary checks that need no GPU: the C ABI loads and exports every
+declared symbol, host-side validation rejects bad arguments before any launch,
+and the module tree / state-dict keys are the reference's."""
+
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+import local_research_small_language_model_b200 as sd
+from local_research_small_language_model_b200 import _lib
+from local_research_small_language_model_b200.model import SparDAB200Model
+from oracle.synthetic import SmallModelConfig, state_shapes
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    txt = open(os.path.join(REPO, "include", "spardab200.h")).read()
+    return sorted(set(re.findall(r"SD_API\s+(?:const\s+char\s*\*|int)\s*(sd_\w+)\s*\(", txt)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = sd.load_library()
+    decl = declared_symbols()
+    assert len(decl) >= 12
+    for name in decl:
+        assert hasattr(lib, name), name
+    assert sorted(_lib.exported_symbols()) == decl
+    assert lib.sd_version() >= 1
+
+
+def test_strerror_texts():
+    lib = sd.load_library()
+    for code in (0, -1, -2, -3, -4):
+        assert lib.sd_strerror(code)
+    assert lib.sd_strerror(-99) == b"unknown error"
+
+
+def test_host_validation_rejects_bad_arguments():
+    """Null pointers and bad shapes are refused before any CUDA call."""
+    lib = sd.load_library()
+    assert lib.sd_compress_blocks(None, 1, 1, 64, 4, 64, 0, 0, 0, 64, None, None) == -1
+    assert lib.sd_topk_rows(None, 1, 8, 8, 4, None, None, None) == -1
+    assert lib.sd_decode_attention(None, 1, 1, 12, 4, 64, 0, 0, None, None, 0, 0, 0, 64, None, None, 10, 1, 64,
+                                   0.125, None, 0, 0, None, None) == -1
+    # unsupported head_dim with otherwise valid-looking (non-null) pointers
+    p = ctypes.c_void_p(16)
+    assert lib.sd_decode_attention(p, 1, 1, 12, 4, 32, 0, 0, p, p, 0, 0, 0, 64, p, p, 10, 1, 64, 0.125, p, 0, 0,
+                                   None, None) == -2
+    assert lib.sd_decode_select(None, 0, 0, 0, None, 0, 0, 0, 1, 4, 64, 100, 64, 8, 7, p, p, 10, None) == -1
+
+
+def test_ops_refuse_cpu_tensors():
+    k = torch.zeros(1, 64, 4, 64)
+    with pytest.raises(ValueError, match="CUDA"):
+        sd.ops.compress_blocks(k, 64)
+    with pytest.raises(ValueError, match="CUDA"):
+        sd.KVBlockCompressor(64, 64, 64)(k)
+
+
+def test_model_state_dict_matches_reference_layout():
+    m = SparDAB200Model(sd.ModelConfig(block_size=64, top_k_blocks=8))
+    assert sum(p.numel() for p in m.parameters()) == 102_451_968  # reference tests/test_model.py:9-28
+    sc = SmallModelConfig(vocab_size=32000, n_layer=12)
+    ref = state_shapes(sc)
+    got = {k: tuple(v.shape) for k, v in m.state_dict().items()}
+    assert got == ref
+
+
+def test_install_swaps_attention_modules():
+    cfg = sd.ModelConfig(n_layer=2, block_size=64, top_k_blocks=8)
+    m = SparDAB200Model(cfg)
+    w = m.layers[1].attention.wq.weight.clone()
+    sd.install(m, rule="absolute")
+    assert isinstance(m.layers[1].attention, sd.B200SparseAttention)
+    assert m.layers[1].attention.rule == "absolute"
+    assert torch.equal(m.layers[1].attention.wq.weight, w)
+
+
+def test_install_into_reference_model():
+    """The reference's own model accepts the backend (module swap; CPU only,
+    so no forward).  Skipped where the reference checkout is absent."""
+    ref = "/root/reference"
+    if not os.path.isdir(os.path.join(ref, "model")):
+        pytest.skip("reference checkout not present")
+    import sys
+    sys.path.insert(0, ref)
+    from model.config import ModelConfig as RC
+    from model.model import SparDAResearchModel
+    r = SparDAResearchModel(RC(n_layer=2, block_size=64, top_k_blocks=8, attention_backend="sparse"))
+    before = {k: v.clone() for k, v in r.state_dict().items()}
+    sd.install(r)
+    after = r.state_dict()
+    assert set(before) == set(after)
+    for k in before:
+        assert torch.equal(before[k], after[k]), k
+
+
+def test_selector_rule_validation():
+    with pytest.raises(ValueError):
+        sd.B200SparseAttention(sd.ModelConfig(), 1, rule="bogus")
