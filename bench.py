@@ -53,6 +53,8 @@ def parse():
     ap.add_argument("--cpu-seqs", type=int, default=2)
     ap.add_argument("--cpu-budget-s", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=12,
+                    help="layers of the model (12 = the benchmark model; fewer only for small profiler captures)")
     return ap.parse_args()
 
 
@@ -193,7 +195,8 @@ def run_b200(args, rank, world, local):
     torch.cuda.set_device(dev)
     torch.manual_seed(1234 + rank)
     B, ctx, W = args.batch, args.ctx, args.window
-    cfg = ModelConfig(block_size=64, top_k_blocks=8, context_length=4096, selector_rule=args.rule)
+    cfg = ModelConfig(block_size=64, top_k_blocks=8, context_length=4096, selector_rule=args.rule,
+                      n_layer=args.layers)
     model = SparDAB200Model(cfg).to(dev, torch.bfloat16).eval()
     caches = model.allocate_caches(B, ctx + W + 64)
     gen = torch.Generator(device=dev)

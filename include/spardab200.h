@@ -165,6 +165,18 @@ SD_API int sd_decode_layer(const void *qkv, int dtype, int64_t qkv_sb, const voi
                     float scale, void *out, int64_t o_sb, int32_t *sel_out, int32_t *cnt_out,
                     int sel_cap, int32_t *err, void *stream);
 
+/* RMSNorm of `rows` rows of C values (row strides x_rs, o_rs), computed as
+ * model/norm.py:15-21 does: normalised in fp32, cast to the activation dtype,
+ * then multiplied by the gain w [C] in that dtype. */
+SD_API int sd_rmsnorm(const void *x, int dtype, int64_t rows, int64_t C, int64_t x_rs, const void *w,
+                      float eps, void *out, int64_t o_rs, void *stream);
+
+/* SwiGLU gate of model/transformer.py:30-31 on a fused [gate | up] projection:
+ * gu rows hold 2F values (row stride g_rs); out[r, c] = silu(gate) * up, each
+ * op rounded to the activation dtype as the reference's separate ops are. */
+SD_API int sd_silu_mul(const void *gu, int dtype, int64_t rows, int64_t F, int64_t g_rs, void *out,
+                       int64_t o_rs, void *stream);
+
 /* lens[i] += delta for i < n (device int32 array). */
 SD_API int sd_advance_len(int32_t *lens, int n, int delta, void *stream);
 

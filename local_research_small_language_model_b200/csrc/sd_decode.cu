@@ -4,8 +4,10 @@
 // Work split: one CTA (4 warps) per (sequence, kv head).  The selected KV
 // blocks are cut into tiles of at most 64 cached rows of ONE block; tiles are
 // staged into shared memory by bulk asynchronous copies (cp.async.bulk, the
-// non-tensor TMA path) into a 4-stage ring completed on mbarriers, so up to
-// 4 tiles (K and V) are in flight per CTA while the previous ones are consumed.
+// non-tensor TMA path) into a 6-stage ring completed on mbarriers, so up to
+// 6 tiles (K and V) are in flight per CTA while the previous ones are consumed.
+// The fused kernel issues the sink and current blocks (always attended) before
+// it scores the prototypes, so those copies overlap the selection.
 // Warp w owns rows 16w..16w+15 of every tile and keeps an online-softmax state
 // for all G = Hq/Hkv query heads of the kv head; the four warp states are
 // merged at the end.  Scores are accumulated in fp32 and exponentiated in base 2.
@@ -15,7 +17,7 @@ namespace sd {
 
 constexpr int kD = 64;          // head_dim the attention kernels implement
 constexpr int kRows = 64;       // rows per tile
-constexpr int kStages = 4;
+constexpr int kStages = 6;
 constexpr int kThreads = 128;
 constexpr int kMaxTiles = 256;
 constexpr float kLog2e = 1.4426950408889634f;
@@ -77,21 +79,26 @@ template <typename T, int G> struct AttnSmem {
   }
 };
 
-// Fills the tile table from an ascending block list; returns the tile count.
-// Called by one thread.
+// Appends the tiles (<= kRows cached rows each) of block j to the tile table.
+__device__ __forceinline__ int add_block_tiles(int64_t j, int64_t L, int bs, int *tile_tok, int *tile_n, int nt) {
+  if (j < 0 || j * bs >= L) return nt;  // invalid or empty block: nothing to stage
+  int64_t n = L - j * bs;
+  if (n > bs) n = bs;
+  for (int64_t r0 = 0; r0 < n && nt < kMaxTiles; r0 += kRows) {
+    tile_tok[nt] = static_cast<int>(j * bs + r0);
+    tile_n[nt] = static_cast<int>(n - r0 < kRows ? n - r0 : kRows);
+    ++nt;
+  }
+  return nt;
+}
+
+// Appends the tiles of every listed block except skip_a / skip_b, starting at
+// table index nt; returns the new tile count.  Called by one thread.
 __device__ __forceinline__ int build_tiles(const int *list, int count, int64_t L, int bs, int *tile_tok,
-                                           int *tile_n) {
-  int nt = 0;
+                                           int *tile_n, int nt = 0, int skip_a = -1, int skip_b = -1) {
   for (int i = 0; i < count; ++i) {
-    const int64_t j = list[i];
-    if (j < 0 || j * bs >= L) continue;  // invalid or empty block: nothing to stage
-    int64_t n = L - j * bs;
-    if (n > bs) n = bs;
-    for (int64_t r0 = 0; r0 < n && nt < kMaxTiles; r0 += kRows) {
-      tile_tok[nt] = static_cast<int>(j * bs + r0);
-      tile_n[nt] = static_cast<int>(n - r0 < kRows ? n - r0 : kRows);
-      ++nt;
-    }
+    if (list[i] == skip_a || list[i] == skip_b) continue;
+    nt = add_block_tiles(list[i], L, bs, tile_tok, tile_n, nt);
   }
   return nt;
 }
@@ -116,15 +123,16 @@ __device__ __forceinline__ void issue_tile(AttnSmem<T, G> &S, int t, const T *kb
 }
 
 // Runs the staged attention over S.tile_* (ntiles) for the G query heads in
-// S.q (fp32).  Writes out[g * o_hs + d] (T).  Returns false (uniformly) when a
+// S.q (fp32).  Tiles 0..pre_issued-1 (pre_issued <= kStages) were already
+// issued by thread 0.  Writes out[g * o_hs + d] (T).  Returns false (uniformly) when a
 // bounded wait expired; the caller reports it.  All threads call this.
 template <typename T, int G>
-__device__ bool attend_tiles(AttnSmem<T, G> &S, int ntiles, const T *kb, const T *vb, int64_t c_st,
-                             float scale_log2, T *out, int64_t o_hs) {
+__device__ bool attend_tiles(AttnSmem<T, G> &S, int ntiles, int pre_issued, const T *kb, const T *vb,
+                             int64_t c_st, float scale_log2, T *out, int64_t o_hs) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int kg = lane >> 3, dc = lane & 7;
   if (tid == 0) {
-    for (int t = 0; t < ntiles && t < kStages; ++t) issue_tile<T, G>(S, t, kb, vb, c_st);
+    for (int t = pre_issued; t < ntiles && t < kStages; ++t) issue_tile<T, G>(S, t, kb, vb, c_st);
   }
   float qr[G][8];
 #pragma unroll
@@ -284,7 +292,7 @@ __global__ void __launch_bounds__(kThreads)
   if (threadIdx.x == 0) ntiles = build_tiles(list, c, L, bs, S.tile_tok, S.tile_n);
   __syncthreads();
   const int64_t cb = b * c_sb + h * c_sh;
-  if (!attend_tiles<T, G>(S, ntiles, k_cache + cb, v_cache + cb, c_st, scale_log2,
+  if (!attend_tiles<T, G>(S, ntiles, 0, k_cache + cb, v_cache + cb, c_st, scale_log2,
                           out + b * o_sb + static_cast<int64_t>(h * G) * o_sh, o_sh))
     report(err, SD_KERR_TIMEOUT);
 }
@@ -359,6 +367,19 @@ __global__ void __launch_bounds__(kThreads)
   if (fc != nullptr && threadIdx.x < kD) f_s[threadIdx.x] = to_f(fc[b * f_sb + h * kD + threadIdx.x]);
   __syncthreads();
 
+  // the sink block and the current block are always attended: stage them now,
+  // so their copies overlap the prototype scoring
+  const T *kb = k_cache + bh * Tcap * kD;
+  const T *vb = v_cache + bh * Tcap * kD;
+  __shared__ int pre;
+  if (threadIdx.x == 0) {
+    int nt = add_block_tiles(0, L, bs, S.tile_tok, S.tile_n, 0);
+    if (curr != 0) nt = add_block_tiles(curr, L, bs, S.tile_tok, S.tile_n, nt);
+    pre = nt < kStages ? nt : kStages;
+    for (int t = 0; t < pre; ++t) issue_tile<T, G>(S, t, kb, vb, kD);
+    ntiles = nt;
+  }
+
   // -- 2. selection over this layer's prototypes (sum / bs)
   int n_scored = 0;
   if (fc != nullptr && nb > ms) {
@@ -367,7 +388,7 @@ __global__ void __launch_bounds__(kThreads)
     __syncthreads();
   }
   build_decode_list(fc != nullptr, sc, n_scored, nb, curr, top_k, ms, tk, list, &count);
-  if (threadIdx.x == 0) ntiles = build_tiles(list, count, L, bs, S.tile_tok, S.tile_n);
+  if (threadIdx.x == 0) ntiles = build_tiles(list, count, L, bs, S.tile_tok, S.tile_n, ntiles, 0, curr);
   if (sel_out) {
     for (int i = threadIdx.x; i < sel_cap; i += blockDim.x) sel_out[bh * sel_cap + i] = i < count ? list[i] : -1;
     if (threadIdx.x == 0) cnt_out[bh] = count;
@@ -375,9 +396,7 @@ __global__ void __launch_bounds__(kThreads)
   __syncthreads();
 
   // -- 3. attention over the selected blocks
-  const T *kb = k_cache + bh * Tcap * kD;
-  const T *vb = v_cache + bh * Tcap * kD;
-  if (!attend_tiles<T, G>(S, ntiles, kb, vb, kD, scale_log2, out + b * o_sb + static_cast<int64_t>(h * G) * kD,
+  if (!attend_tiles<T, G>(S, ntiles, pre, kb, vb, kD, scale_log2, out + b * o_sb + static_cast<int64_t>(h * G) * kD,
                           kD))
     report(err, SD_KERR_TIMEOUT);
 }

@@ -1,0 +1,77 @@
+// Row kernels of the decode step around the attention path: RMSNorm
+// (model/norm.py:15-21) and the SwiGLU gate (model/transformer.py:30-31),
+// each one launch instead of the several elementwise ops of the reference.
+#include "sd_common.cuh"
+
+namespace sd {
+
+// out = T(T(x * rsqrt(mean(x^2) + eps)) * w): the reference normalises in fp32,
+// casts back to the activation dtype, then multiplies by the gain in that dtype.
+template <typename T>
+__global__ void rmsnorm_kernel(const T *__restrict__ x, int64_t x_rs, const T *__restrict__ w, int C, float eps,
+                               T *__restrict__ out, int64_t o_rs) {
+  const T *xr = x + blockIdx.x * x_rs;
+  T *orow = out + blockIdx.x * o_rs;
+  float ss = 0.f;
+  for (int c = threadIdx.x; c < C; c += blockDim.x) {
+    const float v = to_f(xr[c]);
+    ss = fmaf(v, v, ss);
+  }
+  __shared__ float red[32];
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  const float r = rsqrtf(red[0] / static_cast<float>(C) + eps);
+  for (int c = threadIdx.x; c < C; c += blockDim.x) {
+    const float n = round_to<T>(to_f(xr[c]) * r);
+    orow[c] = from_f<T>(n * to_f(w[c]));
+  }
+}
+
+// gu rows hold [gate | up] (2F values); out = T(T(silu(gate)) * up).
+template <typename T>
+__global__ void silu_mul_kernel(const T *__restrict__ gu, int64_t g_rs, int F, T *__restrict__ out,
+                                int64_t o_rs) {
+  const T *g = gu + blockIdx.y * g_rs;
+  T *o = out + blockIdx.y * o_rs;
+  for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < F; c += gridDim.x * blockDim.x) {
+    const float a = to_f(g[c]);
+    const float s = round_to<T>(a / (1.0f + expf(-a)));
+    o[c] = from_f<T>(s * to_f(g[F + c]));
+  }
+}
+
+}  // namespace sd
+
+extern "C" int sd_rmsnorm(const void *x, int dtype, int64_t rows, int64_t C, int64_t x_rs, const void *w,
+                          float eps, void *out, int64_t o_rs, void *stream) {
+  if (!x || !w || !out || rows <= 0 || C <= 0) return SD_ERR_INVALID;
+  if (rows > 0x7fffffff) return SD_ERR_UNSUPPORTED;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int threads = C >= 1024 ? 1024 : static_cast<int>(((C + 31) / 32) * 32);
+  SD_DISPATCH_DTYPE(dtype, E,
+                    sd::rmsnorm_kernel<E><<<static_cast<unsigned>(rows), threads, 0, s>>>(
+                        static_cast<const E *>(x), x_rs, static_cast<const E *>(w), (int)C, eps,
+                        static_cast<E *>(out), o_rs));
+  return sd::check_launch();
+}
+
+extern "C" int sd_silu_mul(const void *gu, int dtype, int64_t rows, int64_t F, int64_t g_rs, void *out,
+                           int64_t o_rs, void *stream) {
+  if (!gu || !out || rows <= 0 || F <= 0) return SD_ERR_INVALID;
+  if (rows > 65535) return SD_ERR_UNSUPPORTED;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const unsigned gx = static_cast<unsigned>((F + 255) / 256 < 8 ? (F + 255) / 256 : 8);
+  SD_DISPATCH_DTYPE(dtype, E,
+                    sd::silu_mul_kernel<E><<<dim3(gx, static_cast<unsigned>(rows)), 256, 0, s>>>(
+                        static_cast<const E *>(gu), g_rs, (int)F, static_cast<E *>(out), o_rs));
+  return sd::check_launch();
+}

@@ -16,7 +16,36 @@ __device__ __forceinline__ void score_blocks(const float *__restrict__ reps, int
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   const int half = lane >> 4, l16 = lane & 15;
   const int nvec = D >> 2;
-  // two blocks per warp per step, each read by a half-warp as float4 chunks
+  if (D == 64) {
+    // 16 prototype rows per warp per step: each half-warp reads 8 rows (one
+    // float4 per lane per row), all loads issued before any reduction so a
+    // warp keeps 8 independent DRAM requests in flight
+    constexpr int U = 8;
+    const float4 q = reinterpret_cast<const float4 *>(f)[l16];
+    for (int j0 = 2 * U * warp; j0 < n_scored; j0 += 2 * U * nwarps) {
+      float4 r[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int j = j0 + 2 * u + half;
+        r[u] = j < n_scored ? reinterpret_cast<const float4 *>(reps + static_cast<int64_t>(j) * r_sn)[l16]
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        float acc = 0.f;
+        acc = fmaf(q.x, r[u].x, acc);
+        acc = fmaf(q.y, r[u].y, acc);
+        acc = fmaf(q.z, r[u].z, acc);
+        acc = fmaf(q.w, r[u].w, acc);
+#pragma unroll
+        for (int off = 8; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+        const int j = j0 + 2 * u + half;
+        if (l16 == 0 && j < n_scored) scores[j] = acc * mul;
+      }
+    }
+    return;
+  }
+  // generic D: two blocks per warp per step, each read by a half-warp as float4 chunks
   for (int j0 = 2 * warp; j0 < n_scored; j0 += 2 * nwarps) {
     const int j = j0 + half;
     float acc = 0.f;

@@ -33,6 +33,9 @@ class RMSNorm(nn.Module):
         self.weight = nn.Parameter(torch.ones(dim))
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if x.is_cuda and x.dtype == self.weight.dtype:
+            c = x.shape[-1]
+            return ops.rmsnorm(x.reshape(-1, c), self.weight, self.eps).view(x.shape)
         xf = x.float()
         return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.eps)).type_as(x) * self.weight
 
@@ -99,13 +102,26 @@ class TransformerBlock(nn.Module):
             self._packed_key = key
         return self._packed
 
+    def packed_ffn_weight(self) -> torch.Tensor:
+        ws = (self.ffn.w_gate.weight, self.ffn.w_up.weight)
+        key = tuple((w.data_ptr(), w._version, w.dtype) for w in ws)
+        if getattr(self, "_ffn_packed", None) is None or self._ffn_key != key:
+            with torch.no_grad():
+                self._ffn_packed = torch.cat(ws, dim=0).contiguous()
+            self._ffn_key = key
+        return self._ffn_packed
+
     def forward(self, x, rotary_emb, kv_cache=None, mask=None, is_causal=True, prev_layer_forecast=None,
                 next_layer_block=None, next_kv_cache=None):
-        normed = self.attn_norm(x)
         b, t, c = x.shape
         if isinstance(kv_cache, B200KVCache) and t == 1:
+            # decode step: 8 launches per layer (norm, [wq;wk;wv;wf] GEMM, fused
+            # attention kernel, wo GEMM with the residual add folded into addmm,
+            # norm, [w_gate;w_up] GEMM, SwiGLU gate kernel, w_down addmm)
             a = self.attention
-            proj = F.linear(normed.view(b, c), self.packed_weight())
+            x2 = x.view(b, c)
+            normed = self.attn_norm(x2)
+            proj = F.linear(normed, self.packed_weight())
             nq = (a.n_head + 2 * a.n_kv_head) * a.head_dim
             current_forecast = proj[:, nq:].view(b, 1, self.config.forecast_heads, self.config.forecast_dim)
             if kv_cache.current_len >= kv_cache.tcap:
@@ -124,8 +140,12 @@ class TransformerBlock(nn.Module):
             if probe is not None:
                 probe["end"].record()
             kv_cache.advance(1, device=not getattr(kv_cache, "shared_len", False))
-            x = x + a.wo(out).view(b, 1, c)
+            x2 = torch.addmm(x2, out, a.wo.weight.t())
+            gu = F.linear(self.ffn_norm(x2), self.packed_ffn_weight())
+            x2 = torch.addmm(x2, ops.silu_mul(gu), self.ffn.w_down.weight.t())
+            return x2.view(b, 1, c), current_forecast
         else:
+            normed = self.attn_norm(x)
             current_forecast = self.forecast(normed)
             if next_layer_block is not None and next_kv_cache is not None and \
                     hasattr(next_layer_block.attention, "prefetch"):

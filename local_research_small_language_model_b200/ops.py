@@ -235,6 +235,28 @@ def decode_layer(qkv: torch.Tensor, forecast: Optional[torch.Tensor], rope_cos: 
     return out
 
 
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
+    """RMSNorm (model/norm.py:15-21) over the last dim of a 2-D [rows, C] tensor."""
+    _cuda(x, weight)
+    x = _inner1(x)
+    w = weight.to(x.dtype).contiguous()
+    out = torch.empty(x.shape, dtype=x.dtype, device=x.device)
+    L.call("sd_rmsnorm", x.data_ptr(), dtype_code(x), x.shape[0], x.shape[1], x.stride(0), w.data_ptr(), eps,
+           out.data_ptr(), out.stride(0), _stream(x))
+    return out
+
+
+def silu_mul(gu: torch.Tensor) -> torch.Tensor:
+    """silu(gate) * up for gu = [gate | up] rows [rows, 2F] -> [rows, F]."""
+    _cuda(gu)
+    gu = _inner1(gu)
+    f = gu.shape[1] // 2
+    out = torch.empty(gu.shape[0], f, dtype=gu.dtype, device=gu.device)
+    L.call("sd_silu_mul", gu.data_ptr(), dtype_code(gu), gu.shape[0], f, gu.stride(0), out.data_ptr(),
+           out.stride(0), _stream(gu))
+    return out
+
+
 def advance_len(lens: torch.Tensor, delta: int = 1) -> None:
     _cuda(lens)
     L.call("sd_advance_len", lens.data_ptr(), lens.numel(), delta, _stream(lens))

@@ -310,3 +310,24 @@ def test_decode_layer_rope_bitexact_bf16(dev):
     xk = qkv[:, hq * 64:(hq + hkv) * 64].view(b, 1, hkv, 64)
     _, kr = apply_rotary_emb(xq, xk, cos.to(dev), sin.to(dev), offset=300)
     assert torch.equal(cache.k_store[:, :, 300], kr[:, 0])
+
+
+# ------------------------------------------------------------------ decode-step row kernels
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
+def test_rmsnorm_matches_reference_formula(dev, dt):
+    """model/norm.py:15-21: fp32 normalisation, cast, gain multiply in dtype."""
+    x = t(normal((64, 768), seed=1), dev, dt)
+    w = t(1.0 + 0.1 * normal((768,), seed=2), dev, dt)
+    ref = (x.float() * torch.rsqrt(x.float().pow(2).mean(-1, keepdim=True) + 1e-6)).type_as(x) * w
+    got = ops.rmsnorm(x, w, 1e-6)
+    tol = 1e-6 if dt == torch.float32 else 8e-3  # one bf16 ulp of the normalised value
+    torch.testing.assert_close(got.float(), ref.float(), rtol=tol, atol=tol)
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
+def test_silu_mul_matches_reference_formula(dev, dt):
+    """model/transformer.py:30-31 on a fused [gate | up] projection."""
+    gu = t(normal((64, 4096), seed=3), dev, dt)
+    ref = torch.nn.functional.silu(gu[:, :2048]) * gu[:, 2048:]
+    torch.testing.assert_close(ops.silu_mul(gu).float(), ref.float(), rtol=1e-5 if dt == torch.float32 else 8e-3,
+                               atol=1e-6 if dt == torch.float32 else 8e-3)
