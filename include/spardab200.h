@@ -165,6 +165,48 @@ SD_API int sd_decode_layer(const void *qkv, int dtype, int64_t qkv_sb, const voi
                     float scale, void *out, int64_t o_sb, int32_t *sel_out, int32_t *cnt_out,
                     int sel_cap, int32_t *err, void *stream);
 
+/* ---- prefill block-list modes (sd_prefill_lists) ----
+ * One list per (sequence, kv head, 64-token query block qb), ascending:
+ *   DENSE            blocks 0..qb (sparse.py:201-224, layer 0 / no forecast / N_b <= 2)
+ *   MASKED_FORECAST  {0, qb} U every row's top-k (sparse.py:226-247); the
+ *                    attention kernel then applies each row's own membership
+ *   MASKED_STATIC    {0} U {qb-top_k .. qb} (sparse.py:249-251)
+ *   CHUNKED_FORECAST {0, qb} U union of the rows' non-causal top-k, future
+ *                    blocks cleared, cut to min(N_b, top_k+2) blocks by keeping
+ *                    0 and qb, then the blocks most rows picked (ties: lower
+ *                    index) (sparse.py:303-333; the reference keeps an
+ *                    unspecified subset of that size)
+ *   CHUNKED_STATIC   {0} U {qb-top_k+1 .. qb} (sparse.py:324-328) */
+#define SD_LIST_DENSE 0
+#define SD_LIST_MASKED_FORECAST 1
+#define SD_LIST_MASKED_STATIC 2
+#define SD_LIST_CHUNKED_FORECAST 3
+#define SD_LIST_CHUNKED_STATIC 4
+
+/* Builds the prefill block lists.  topk: int64 [B,H,T,kk] selector indices
+ * (needed by the *_FORECAST modes).  causal = 0 keeps future blocks for the
+ * masked modes (is_causal=False); chunked modes always clear them.  lists:
+ * int32 [B,H,ceil(T/64),lcap] (-1 padded), counts: int32 [B,H,ceil(T/64)].
+ * block_size must be 64. */
+SD_API int sd_prefill_lists(int mode, int causal, int64_t B, int64_t H, int64_t T, int block_size, int top_k,
+                            const int64_t *topk, int kk, int32_t *lists, int32_t *counts, int lcap,
+                            void *stream);
+
+/* Block-sparse GQA prefill attention over the lists of sd_prefill_lists on
+ * CUDA cores (fp32 math): the fp32 path, and the cross-check of the
+ * tensor-core kernel.  Replaces the mask construction + repeat_interleave +
+ * SDPA of model/attention/sparse.py:255-282 and :334-360.
+ * q: [B,T,Hq,D] (strides q_sb, q_st, q_sh); k, v: [B,Hkv,T,D] (strides c_sb,
+ * c_sh, c_st); topk (nullable): the MASKED_FORECAST rows' top-k, for per-row
+ * membership; causal: key pos <= query pos.  out: [B,T,Hq,D] (strides o_sb,
+ * o_st, o_sh).  D = 64, block_size = 64. */
+SD_API int sd_prefill_attention(const void *q, int dtype, int64_t B, int64_t T, int64_t Hq, int64_t Hkv,
+                                int64_t D, int64_t q_sb, int64_t q_st, int64_t q_sh, const void *k,
+                                const void *v, int64_t c_sb, int64_t c_sh, int64_t c_st,
+                                const int32_t *lists, const int32_t *counts, int lcap, const int64_t *topk,
+                                int kk, int block_size, int causal, float scale, void *out, int64_t o_sb,
+                                int64_t o_st, int64_t o_sh, void *stream);
+
 /* RMSNorm of `rows` rows of C values (row strides x_rs, o_rs), computed as
  * model/norm.py:15-21 does: normalised in fp32, cast to the activation dtype,
  * then multiplied by the gain w [C] in that dtype. */
