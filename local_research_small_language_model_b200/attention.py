@@ -119,4 +119,50 @@ class B200SparseAttention(BaseAttention):
         return self.wo(out.reshape(b, 1, self.n_head * self.head_dim).to(x.dtype))
 
     def _prefill(self, x, rotary_emb, kv_cache, mask, is_causal, forecast_vector, **kwargs):
-        raise NotImplementedError("prefill kernels are not built yet")
+        """Sequence prefill (sparse.py:412-439): the masked path for T <= 8192,
+        the chunked path above (or when ``use_chunked_gather`` is passed)."""
+        if mask is not None:
+            raise NotImplementedError("explicit additive masks are not supported by the B200 backend")
+        b, t, _ = x.shape
+        xq = self.wq(x).view(b, t, self.n_head, self.head_dim)
+        xk = self.wk(x).view(b, t, self.n_kv_head, self.head_dim)
+        xv = self.wv(x).view(b, t, self.n_kv_head, self.head_dim)
+        offset = kv_cache.current_len if kv_cache is not None else 0
+        if offset:
+            # the reference uses seq_len for both queries and keys here
+            # (sparse.py:413-430), so a prompt cannot extend a filled cache
+            raise NotImplementedError("prefill into a non-empty cache")
+        xq, xk = rotary_emb(xq, xk, offset=0)
+        if kv_cache is not None:
+            k_all, v_all = kv_cache.update(xk, xv)
+            if isinstance(kv_cache, B200KVCache):
+                kh, vh = kv_cache.k_store[:, :, :t], kv_cache.v_store[:, :, :t]
+            else:
+                kh, vh = k_all.transpose(1, 2), v_all.transpose(1, 2)
+        else:
+            kh, vh = xk.transpose(1, 2), xv.transpose(1, 2)
+        bs, kk = self.block_size, self.top_k_blocks
+        nb = ops.num_blocks(t, bs)
+        f = forecast_vector if (self.mode == "forecast" and forecast_vector is not None) else None
+        topk = None
+        if kwargs.get("use_chunked_gather", t > 8192):
+            causal = True  # the chunked path always clears future blocks (sparse.py:330-346)
+            if f is not None:
+                _, topk = self.selector(f, self.compressor(xk), kk, is_causal=False)
+                mode = "chunked_forecast"
+            else:
+                mode = "chunked_static"
+            row_topk = None
+        else:
+            causal = is_causal
+            if nb <= 2 or (self.mode == "forecast" and (f is None or self.layer_idx == 0)):
+                mode = "dense"
+            elif self.mode == "forecast":
+                _, topk = self.selector(f, self.compressor(xk), kk, is_causal=is_causal)
+                mode = "masked_forecast"
+            else:
+                mode = "masked_static"
+            row_topk = topk
+        lists, counts = ops.prefill_lists(mode, b, self.n_kv_head, t, bs, kk, topk, causal, device=x.device)
+        out = ops.prefill_attention(xq, kh, vh, lists, counts, bs, row_topk, causal)
+        return self.wo(out.reshape(b, t, self.n_head * self.head_dim).to(x.dtype))

@@ -154,6 +154,43 @@ __device__ __forceinline__ void warp_topk(Get get, int n, int k, int *out_idx, f
   }
 }
 
+// Like warp_topk, but candidate c has value val(c) and block index idx(c),
+// which both orders ties and is written out.  Used to merge per-warp top-k
+// lists; idx values must be distinct.
+template <typename Val, typename Idx>
+__device__ __forceinline__ void warp_topk_kv(Val val, Idx idx, int n, int k, int *out_idx) {
+  const int lane = threadIdx.x & 31;
+  float pv = INFINITY;
+  int pi = -1;
+  bool first = true;
+  for (int r = 0; r < k; ++r) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int c = lane; c < n; c += 32) {
+      const float v = val(c);
+      const int j = idx(c);
+      const bool elig = first || (v < pv) || (v == pv && j > pi);
+      if (elig && (bi == 0x7fffffff || better(v, j, bv, bi))) {
+        bv = v;
+        bi = j;
+      }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+      if (oi != 0x7fffffff && (bi == 0x7fffffff || better(ov, oi, bv, bi))) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if (lane == 0) out_idx[r] = bi == 0x7fffffff ? -1 : bi;
+    pv = bv;
+    pi = bi;
+    first = false;
+  }
+}
+
 }  // namespace sd
 
 // Expands BODY with `T` bound to the element type of SD_DTYPE_* code `dt`;

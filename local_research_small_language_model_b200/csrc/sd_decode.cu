@@ -2,16 +2,26 @@
 // (RoPE + KV append + compressor update + selection + attention).
 //
 // Work split: one CTA (4 warps) per (sequence, kv head).  The selected KV
-// blocks are cut into tiles of at most 64 cached rows of ONE block; tiles are
-// staged into shared memory by bulk asynchronous copies (cp.async.bulk, the
-// non-tensor TMA path) into a 6-stage ring completed on mbarriers, so up to
-// 6 tiles (K and V) are in flight per CTA while the previous ones are consumed.
+// blocks are cut into tiles of at most 64 cached rows of ONE block, staged into
+// shared memory through a 6-stage ring completed on mbarriers, so up to 6
+// tiles (K and V) are in flight per CTA while earlier ones are consumed.
+//
+// Two staging/compute paths:
+//   * 16-bit caches whose rows are contiguous (the block-major cache of this
+//     library): each tile is one TMA tensor copy (cp.async.bulk.tensor, 128-byte
+//     swizzle) per K and V; warp w takes keys 16w..16w+15 of a tile and runs
+//     QK^T and PV as mma.sync m16n8k16 with the G query heads as the rows of
+//     the A operand (ldmatrix on the swizzled tile is bank-conflict free);
+//   * fp32 caches (exact fp32 parity) and strided 16-bit caches: bulk copies of
+//     rows and the same split of keys over warps on CUDA cores.
+// Each warp keeps an online-softmax state (fp32, base-2 exponent) for all G
+// heads; the four warp states are merged at the end.
 // The fused kernel issues the sink and current blocks (always attended) before
 // it scores the prototypes, so those copies overlap the selection.
-// Warp w owns rows 16w..16w+15 of every tile and keeps an online-softmax state
-// for all G = Hq/Hkv query heads of the kv head; the four warp states are
-// merged at the end.  Scores are accumulated in fp32 and exponentiated in base 2.
+#include <type_traits>
+
 #include "sd_select_core.cuh"
+#include "sd_tma.cuh"
 
 namespace sd {
 
@@ -19,12 +29,16 @@ constexpr int kD = 64;          // head_dim the attention kernels implement
 constexpr int kRows = 64;       // rows per tile
 constexpr int kStages = 6;
 constexpr int kThreads = 128;
+constexpr int kWarps = kThreads / 32;
 constexpr int kMaxTiles = 256;
 constexpr float kLog2e = 1.4426950408889634f;
 
-// Per-lane feature layout of the QK^T product: lane l serves key group l>>3
-// and 8 features chosen so that the 8 lanes of a group read one K row with
-// conflict-free 16-byte shared loads.
+template <typename T> __host__ __device__ constexpr bool is16() { return sizeof(T) == 2; }
+
+// ---------------------------------------------------------------- CUDA-core helpers
+// Per-lane feature layout of the CUDA-core QK^T product: lane l serves key
+// group l>>3 and 8 features chosen so that the 8 lanes of a group read one K
+// row with conflict-free 16-byte shared loads.
 template <typename T> struct Feat {
   static __device__ __forceinline__ int dim(int dc, int i) { return 8 * dc + i; }
 };
@@ -53,7 +67,9 @@ template <> __device__ __forceinline__ float2 load2<float>(const float *row, int
   return *reinterpret_cast<const float2 *>(row + 2 * lane);
 }
 
-// Shared-memory carve-up common to both kernels.
+// ---------------------------------------------------------------- shared memory
+// Carve-up common to both kernels.  The stage buffers come first so that they
+// sit on the 1024-byte boundary the 128-byte TMA swizzle needs.
 template <typename T, int G> struct AttnSmem {
   T *k;            // [kStages][kRows][kD]
   T *v;            // [kStages][kRows][kD]
@@ -61,13 +77,14 @@ template <typename T, int G> struct AttnSmem {
   float *q;        // [G][kD]
   int *tile_tok;   // [kMaxTiles]
   int *tile_n;     // [kMaxTiles]
-  float *red;      // [4][G][kD + 2]
+  float *red;      // [kWarps][G][kD + 2]
   char *tail;      // kernel-specific
   static constexpr size_t bytes() {
     return 2 * sizeof(T) * kStages * kRows * kD + sizeof(uint64_t) * kStages + sizeof(float) * G * kD +
-           2 * sizeof(int) * kMaxTiles + sizeof(float) * 4 * G * (kD + 2);
+           2 * sizeof(int) * kMaxTiles + sizeof(float) * kWarps * G * (kD + 2);
   }
-  __device__ explicit AttnSmem(char *base) {
+  __device__ explicit AttnSmem(char *raw) {
+    char *base = raw + ((1024u - (smem_u32(raw) & 1023u)) & 1023u);
     k = reinterpret_cast<T *>(base);
     v = k + kStages * kRows * kD;
     full = reinterpret_cast<uint64_t *>(v + kStages * kRows * kD);
@@ -75,9 +92,10 @@ template <typename T, int G> struct AttnSmem {
     tile_tok = reinterpret_cast<int *>(q + G * kD);
     tile_n = tile_tok + kMaxTiles;
     red = reinterpret_cast<float *>(tile_n + kMaxTiles);
-    tail = reinterpret_cast<char *>(red + 4 * G * (kD + 2));
+    tail = reinterpret_cast<char *>(red + kWarps * G * (kD + 2));
   }
 };
+constexpr size_t kAlignSlack = 1024;
 
 // Appends the tiles (<= kRows cached rows each) of block j to the tile table.
 __device__ __forceinline__ int add_block_tiles(int64_t j, int64_t L, int bs, int *tile_tok, int *tile_n, int nt) {
@@ -103,36 +121,90 @@ __device__ __forceinline__ int build_tiles(const int *list, int count, int64_t L
   return nt;
 }
 
-template <typename T, int G>
-__device__ __forceinline__ void issue_tile(AttnSmem<T, G> &S, int t, const T *kb, const T *vb, int64_t c_st) {
-  const int s = t % kStages;
-  const int tok = S.tile_tok[t], n = S.tile_n[t];
-  const uint32_t row_bytes = kD * sizeof(T);
-  mbar_arrive_expect_tx(&S.full[s], 2u * n * row_bytes);
-  T *kd = S.k + s * kRows * kD;
-  T *vd = S.v + s * kRows * kD;
-  if (c_st == kD) {
-    bulk_g2s(kd, kb + static_cast<int64_t>(tok) * kD, n * row_bytes, &S.full[s]);
-    bulk_g2s(vd, vb + static_cast<int64_t>(tok) * kD, n * row_bytes, &S.full[s]);
-  } else {
-    for (int r = 0; r < n; ++r) {
-      bulk_g2s(kd + r * kD, kb + static_cast<int64_t>(tok + r) * c_st, row_bytes, &S.full[s]);
-      bulk_g2s(vd + r * kD, vb + static_cast<int64_t>(tok + r) * c_st, row_bytes, &S.full[s]);
+// ---------------------------------------------------------------- staging
+// Bulk (non-tensor TMA) copies of a tile's rows: one copy when rows are
+// contiguous, one per row otherwise.  Rows land unswizzled.
+template <typename T> struct BulkLoader {
+  const T *kb, *vb;
+  int64_t c_st;
+  __device__ void operator()(T *kd, T *vd, int tok, int n, uint64_t *bar) const {
+    const uint32_t row_bytes = kD * sizeof(T);
+    mbar_arrive_expect_tx(bar, 2u * n * row_bytes);
+    if (c_st == kD) {
+      bulk_g2s(kd, kb + static_cast<int64_t>(tok) * kD, n * row_bytes, bar);
+      bulk_g2s(vd, vb + static_cast<int64_t>(tok) * kD, n * row_bytes, bar);
+    } else {
+      for (int r = 0; r < n; ++r) {
+        bulk_g2s(kd + r * kD, kb + static_cast<int64_t>(tok + r) * c_st, row_bytes, bar);
+        bulk_g2s(vd + r * kD, vb + static_cast<int64_t>(tok + r) * c_st, row_bytes, bar);
+      }
     }
+  }
+};
+
+// TMA tensor copies of a whole 64-row box (rows past the map's extent are
+// zero-filled; rows past the tile's valid count are masked by the consumer).
+struct TmaLoader {
+  const CUtensorMap *mk, *mv;
+  int h, b;
+  template <typename T> __device__ void operator()(T *kd, T *vd, int tok, int, uint64_t *bar) const {
+    mbar_arrive_expect_tx(bar, 2u * kRows * kD * sizeof(T));
+    tma_load_4d(kd, mk, 0, tok, h, b, bar);
+    tma_load_4d(vd, mv, 0, tok, h, b, bar);
+  }
+};
+
+template <typename T, int G, typename Ld>
+__device__ __forceinline__ void issue_tile(AttnSmem<T, G> &S, int t, const Ld &ld) {
+  const int s = t % kStages;
+  ld(S.k + s * kRows * kD, S.v + s * kRows * kD, S.tile_tok[t], S.tile_n[t], &S.full[s]);
+}
+
+// Merges the per-warp states written to S.red and stores out[g*o_hs + d].
+template <typename T, int G>
+__device__ __forceinline__ void combine_store(AttnSmem<T, G> &S, T *out, int64_t o_hs) {
+  for (int e = threadIdx.x; e < G * kD; e += blockDim.x) {
+    const int g = e / kD, d = e - g * kD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, S.red[(w * G + g) * (kD + 2)]);
+    float den = 0.f, num = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) {
+        const float *r = S.red + (w * G + g) * (kD + 2);
+        const float f = exp2f(r[0] - M);
+        den = fmaf(r[1], f, den);
+        num = fmaf(r[2 + d], f, num);
+      }
+    }
+    out[g * o_hs + d] = from_f<T>(den > 0.f ? num / den : 0.f);
   }
 }
 
-// Runs the staged attention over S.tile_* (ntiles) for the G query heads in
-// S.q (fp32).  Tiles 0..pre_issued-1 (pre_issued <= kStages) were already
-// issued by thread 0.  Writes out[g * o_hs + d] (T).  Returns false (uniformly) when a
-// bounded wait expired; the caller reports it.  All threads call this.
+// Waits for tile t; returns the uniform "all threads got it" verdict through
+// the CTA barrier at the end of the tile (see the loops below).
+__device__ __forceinline__ bool wait_tile(uint64_t *full, int t) {
+  bool got = mbar_wait_bounded(&full[t % kStages], (t / kStages) & 1);
+  return __all_sync(0xffffffffu, got);
+}
+
+// After a bounded wait expired: let the copies still in flight land before
+// the CTA's shared memory is released.
 template <typename T, int G>
-__device__ bool attend_tiles(AttnSmem<T, G> &S, int ntiles, int pre_issued, const T *kb, const T *vb,
-                             int64_t c_st, float scale_log2, T *out, int64_t o_hs) {
+__device__ __forceinline__ void drain(AttnSmem<T, G> &S, int t, int ntiles) {
+  for (int u = t; u < ntiles && u < t + kStages; ++u) mbar_wait_bounded(&S.full[u % kStages], (u / kStages) & 1);
+  __syncthreads();
+}
+
+// ---------------------------------------------------------------- CUDA-core path
+template <typename T, int G, typename Ld>
+__device__ bool attend_simt(AttnSmem<T, G> &S, int ntiles, int pre_issued, const Ld &ld, float scale_log2, T *out,
+                            int64_t o_hs) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int kg = lane >> 3, dc = lane & 7;
   if (tid == 0) {
-    for (int t = pre_issued; t < ntiles && t < kStages; ++t) issue_tile<T, G>(S, t, kb, vb, c_st);
+    for (int t = pre_issued; t < ntiles && t < kStages; ++t) issue_tile(S, t, ld);
   }
   float qr[G][8];
 #pragma unroll
@@ -146,12 +218,10 @@ __device__ bool attend_tiles(AttnSmem<T, G> &S, int ntiles, int pre_issued, cons
     l[g] = 0.f;
     acc[g][0] = acc[g][1] = 0.f;
   }
-  bool ok = true;
   int t = 0;
   for (; t < ntiles; ++t) {
     const int s = t % kStages;
-    bool got = mbar_wait_bounded(&S.full[s], (t / kStages) & 1);
-    got = __all_sync(0xffffffffu, got);
+    const bool got = wait_tile(S.full, t);
     if (got) {
       const T *ks = S.k + s * kRows * kD;
       const T *vs = S.v + s * kRows * kD;
@@ -211,18 +281,11 @@ __device__ bool attend_tiles(AttnSmem<T, G> &S, int ntiles, int pre_issued, cons
       }
     }
     if (__syncthreads_or(!got)) {
-      ok = false;
-      break;
+      drain(S, t, ntiles);
+      return false;
     }
-    if (tid == 0 && t + kStages < ntiles) issue_tile<T, G>(S, t + kStages, kb, vb, c_st);
+    if (tid == 0 && t + kStages < ntiles) issue_tile(S, t + kStages, ld);
   }
-  if (!ok) {
-    // let the copies still in flight land before the CTA's shared memory is released
-    for (int u = t; u < ntiles && u < t + kStages; ++u) mbar_wait_bounded(&S.full[u % kStages], (u / kStages) & 1);
-    __syncthreads();
-    return false;
-  }
-  // merge the four warp states
   float *rw = S.red + warp * G * (kD + 2);
 #pragma unroll
   for (int g = 0; g < G; ++g) {
@@ -234,23 +297,117 @@ __device__ bool attend_tiles(AttnSmem<T, G> &S, int ntiles, int pre_issued, cons
     rw[g * (kD + 2) + 3 + 2 * lane] = acc[g][1];
   }
   __syncthreads();
-  for (int e = tid; e < G * kD; e += blockDim.x) {
-    const int g = e / kD, d = e - g * kD;
-    float M = -INFINITY;
+  combine_store(S, out, o_hs);
+  return true;
+}
+
+// ---------------------------------------------------------------- tensor-core path
+// Warp w, per tile: S[heads x 16 keys] = Q K^T as 2 n-tiles x 4 k-steps of
+// m16n8k16 (A rows = the G heads, zero-padded to 16), softmax on the fp32
+// accumulators (a quad of lanes holds one head's 16 scores), then
+// O[heads x 64] += P V as 8 n-tiles x 1 k-step, P reused from the accumulator
+// registers as the A operand.  K fragments come from ldmatrix, V fragments
+// from ldmatrix.trans, both on the 128-byte-swizzled TMA tiles.
+template <typename T, int G>
+__device__ bool attend_mma(AttnSmem<T, G> &S, int ntiles, int pre_issued, const TmaLoader &ld, float scale_log2,
+                           T *out, int64_t o_hs) {
+  static_assert(G <= 8, "query heads per kv head must fit the 16 rows of the A operand");
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int grp = lane >> 2, tig = lane & 3;
+  if (tid == 0) {
+    for (int t = pre_issued; t < ntiles && t < kStages; ++t) issue_tile(S, t, ld);
+  }
+  uint32_t qa[4][2];
 #pragma unroll
-    for (int w = 0; w < 4; ++w) M = fmaxf(M, S.red[(w * G + g) * (kD + 2)]);
-    float den = 0.f, num = 0.f;
-    if (M != -INFINITY) {
+  for (int ks = 0; ks < 4; ++ks) {
+    const float *qr = S.q + (grp < G ? grp : 0) * kD + 16 * ks + 2 * tig;
+    const float z = grp < G ? 1.f : 0.f;
+    qa[ks][0] = pack2<T>(qr[0] * z, qr[1] * z);
+    qa[ks][1] = pack2<T>(qr[8] * z, qr[9] * z);
+  }
+  float o[8][4];
 #pragma unroll
-      for (int w = 0; w < 4; ++w) {
-        const float *r = S.red + (w * G + g) * (kD + 2);
-        const float f = exp2f(r[0] - M);
-        den = fmaf(r[1], f, den);
-        num = fmaf(r[2 + d], f, num);
+  for (int n = 0; n < 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  float m = -INFINITY, l = 0.f;
+  int t = 0;
+  for (; t < ntiles; ++t) {
+    const int s = t % kStages;
+    const bool got = wait_tile(S.full, t);
+    int nv = S.tile_n[t] - 16 * warp;
+    nv = nv < 0 ? 0 : (nv > 16 ? 16 : nv);
+    if (got && nv > 0) {
+      const uint32_t kbase = smem_u32(S.k + s * kRows * kD);
+      const uint32_t vbase = smem_u32(S.v + s * kRows * kD);
+      float sc[2][4];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+        const int key = 16 * warp + 8 * nt + (lane & 7);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(kbase + sw128(key, lane >> 3), b0, b1, b2, b3);
+        mma16816<T>(sc[nt], {qa[0][0], 0u, qa[0][1], 0u}, b0, b1);
+        mma16816<T>(sc[nt], {qa[1][0], 0u, qa[1][1], 0u}, b2, b3);
+        ldsm_x4(kbase + sw128(key, 4 + (lane >> 3)), b0, b1, b2, b3);
+        mma16816<T>(sc[nt], {qa[2][0], 0u, qa[2][1], 0u}, b0, b1);
+        mma16816<T>(sc[nt], {qa[3][0], 0u, qa[3][1], 0u}, b2, b3);
+      }
+      float v[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int kl = 8 * (i >> 1) + 2 * tig + (i & 1);  // key within the warp's 16
+        v[i] = kl < nv ? sc[i >> 1][i & 1] * scale_log2 : -INFINITY;
+      }
+      float mt = fmaxf(fmaxf(v[0], v[1]), fmaxf(v[2], v[3]));
+      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 1));
+      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 2));
+      const float mn = fmaxf(m, mt);  // finite: every warp slice with nv > 0 has a key
+      const float alpha = exp2f(m - mn);
+      float p[4], ps = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        p[i] = exp2f(v[i] - mn);
+        ps += p[i];
+      }
+      ps += __shfl_xor_sync(0xffffffffu, ps, 1);
+      ps += __shfl_xor_sync(0xffffffffu, ps, 2);
+      l = l * alpha + ps;
+      m = mn;
+#pragma unroll
+      for (int n = 0; n < 8; ++n) {
+        o[n][0] *= alpha;
+        o[n][1] *= alpha;
+      }
+      const uint32_t pa[4] = {pack2<T>(p[0], p[1]), 0u, pack2<T>(p[2], p[3]), 0u};
+      const int vkey = 16 * warp + (lane & 7) + ((lane >> 3) & 1) * 8;
+#pragma unroll
+      for (int qd = 0; qd < 4; ++qd) {
+        uint32_t r0, r1, r2, r3;
+        ldsm_x4_t(vbase + sw128(vkey, 2 * qd + (lane >> 4)), r0, r1, r2, r3);
+        mma16816<T>(o[2 * qd], pa, r0, r1);
+        mma16816<T>(o[2 * qd + 1], pa, r2, r3);
       }
     }
-    out[g * o_hs + d] = from_f<T>(den > 0.f ? num / den : 0.f);
+    if (__syncthreads_or(!got)) {
+      drain(S, t, ntiles);
+      return false;
+    }
+    if (tid == 0 && t + kStages < ntiles) issue_tile(S, t + kStages, ld);
   }
+  float *rw = S.red + warp * G * (kD + 2);
+  if (grp < G) {
+    float *r = rw + grp * (kD + 2);
+    if (tig == 0) {
+      r[0] = m;
+      r[1] = l;
+    }
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+      r[2 + 8 * n + 2 * tig] = o[n][0];
+      r[3 + 8 * n + 2 * tig] = o[n][1];
+    }
+  }
+  __syncthreads();
+  combine_store(S, out, o_hs);
   return true;
 }
 
@@ -267,14 +424,15 @@ __device__ __forceinline__ void init_barriers(AttnSmem<T, G> &S) {
 }
 
 // ------------------------------------------------------------ API kernel
-template <typename T, int G>
+template <typename T, int G, bool kTma>
 __global__ void __launch_bounds__(kThreads)
     decode_attention_kernel(const T *__restrict__ q, int Hkv, int64_t q_sb, int64_t q_sh, const T *k_cache,
                             const T *v_cache, int64_t c_sb, int64_t c_sh, int64_t c_st,
+                            const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                             const int32_t *__restrict__ sel, const int32_t *__restrict__ cnt, int ms_cap,
                             int64_t L, int bs, float scale_log2, T *__restrict__ out, int64_t o_sb,
                             int64_t o_sh, int32_t *err) {
-  extern __shared__ __align__(128) char smem_raw[];
+  extern __shared__ __align__(1024) char smem_raw[];
   AttnSmem<T, G> S(smem_raw);
   int *list = reinterpret_cast<int *>(S.tail);
   __shared__ int ntiles;
@@ -291,10 +449,17 @@ __global__ void __launch_bounds__(kThreads)
   __syncthreads();
   if (threadIdx.x == 0) ntiles = build_tiles(list, c, L, bs, S.tile_tok, S.tile_n);
   __syncthreads();
-  const int64_t cb = b * c_sb + h * c_sh;
-  if (!attend_tiles<T, G>(S, ntiles, 0, k_cache + cb, v_cache + cb, c_st, scale_log2,
-                          out + b * o_sb + static_cast<int64_t>(h * G) * o_sh, o_sh))
-    report(err, SD_KERR_TIMEOUT);
+  T *o = out + b * o_sb + static_cast<int64_t>(h * G) * o_sh;
+  bool ok;
+  if constexpr (kTma) {
+    const TmaLoader ld{&tmk, &tmv, h, b};
+    ok = attend_mma<T, G>(S, ntiles, 0, ld, scale_log2, o, o_sh);
+  } else {
+    const int64_t cb = b * c_sb + h * c_sh;
+    const BulkLoader<T> ld{k_cache + cb, v_cache + cb, c_st};
+    ok = attend_simt<T, G>(S, ntiles, 0, ld, scale_log2, o, o_sh);
+  }
+  if (!ok) report(err, SD_KERR_TIMEOUT);
 }
 
 // ------------------------------------------------------------ fused layer
@@ -316,11 +481,12 @@ __global__ void __launch_bounds__(kThreads)
                         const float *__restrict__ rcos, const float *__restrict__ rsin,
                         const int32_t *__restrict__ cur_len, T *k_cache, T *v_cache, float *proto_sum, int Hkv,
                         int64_t Tcap, int64_t NBcap, int bs, int top_k, int rule, float sel_scale,
-                        float scale_log2, T *__restrict__ out, int64_t o_sb, int32_t *sel_out,
-                        int32_t *cnt_out, int sel_cap, int32_t *err) {
-  extern __shared__ __align__(128) char smem_raw[];
+                        float scale_log2, const __grid_constant__ CUtensorMap tmk,
+                        const __grid_constant__ CUtensorMap tmv, T *__restrict__ out, int64_t o_sb,
+                        int32_t *sel_out, int32_t *cnt_out, int sel_cap, int32_t *err) {
+  extern __shared__ __align__(1024) char smem_raw[];
   AttnSmem<T, G> S(smem_raw);
-  __shared__ int count, ntiles;
+  __shared__ int count, ntiles, pre;
   const int b = blockIdx.x / Hkv, h = blockIdx.x - (blockIdx.x / Hkv) * Hkv;
   const int Hq = Hkv * G;
   const int64_t pos = *cur_len;
@@ -371,12 +537,19 @@ __global__ void __launch_bounds__(kThreads)
   // so their copies overlap the prototype scoring
   const T *kb = k_cache + bh * Tcap * kD;
   const T *vb = v_cache + bh * Tcap * kD;
-  __shared__ int pre;
+  const BulkLoader<T> bulk{kb, vb, kD};
+  const TmaLoader tma{&tmk, &tmv, h, b};
   if (threadIdx.x == 0) {
     int nt = add_block_tiles(0, L, bs, S.tile_tok, S.tile_n, 0);
     if (curr != 0) nt = add_block_tiles(curr, L, bs, S.tile_tok, S.tile_n, nt);
     pre = nt < kStages ? nt : kStages;
-    for (int t = 0; t < pre; ++t) issue_tile<T, G>(S, t, kb, vb, kD);
+    for (int t = 0; t < pre; ++t) {
+      if constexpr (is16<T>()) {
+        issue_tile(S, t, tma);
+      } else {
+        issue_tile(S, t, bulk);
+      }
+    }
     ntiles = nt;
   }
 
@@ -396,23 +569,63 @@ __global__ void __launch_bounds__(kThreads)
   __syncthreads();
 
   // -- 3. attention over the selected blocks
-  if (!attend_tiles<T, G>(S, ntiles, pre, kb, vb, kD, scale_log2, out + b * o_sb + static_cast<int64_t>(h * G) * kD,
-                          kD))
-    report(err, SD_KERR_TIMEOUT);
+  T *o = out + b * o_sb + static_cast<int64_t>(h * G) * kD;
+  bool ok;
+  if constexpr (is16<T>()) {
+    ok = attend_mma<T, G>(S, ntiles, pre, tma, scale_log2, o, kD);
+  } else {
+    ok = attend_simt<T, G>(S, ntiles, pre, bulk, scale_log2, o, kD);
+  }
+  if (!ok) report(err, SD_KERR_TIMEOUT);
 }
 
-template <typename T, int G> int launch_decode_attention(const void *q, int64_t B, int64_t Hkv, int64_t q_sb,
-                                                         int64_t q_sh, const void *kc, const void *vc,
-                                                         int64_t c_sb, int64_t c_sh, int64_t c_st,
-                                                         const int32_t *sel, const int32_t *cnt, int ms_cap,
-                                                         int64_t L, int bs, float scale, void *out, int64_t o_sb,
-                                                         int64_t o_sh, int32_t *err, cudaStream_t s) {
-  const size_t smem = AttnSmem<T, G>::bytes() + sizeof(int) * ms_cap + 128;
-  auto kern = decode_attention_kernel<T, G>;
-  if (set_max_smem(kern, smem) != SD_OK) return SD_ERR_CUDA;
-  kern<<<static_cast<unsigned>(B * Hkv), kThreads, smem, s>>>(
-      static_cast<const T *>(q), (int)Hkv, q_sb, q_sh, static_cast<const T *>(kc), static_cast<const T *>(vc), c_sb,
-      c_sh, c_st, sel, cnt, ms_cap, L, bs, scale * kLog2e, static_cast<T *>(out), o_sb, o_sh, err);
+// Tensor maps for a [B][H][T][64] 16-bit cache pair; zeroed maps for fp32.
+template <typename T>
+int make_maps(CUtensorMap *mk, CUtensorMap *mv, const void *kc, const void *vc, int64_t B, int64_t H, int64_t T_,
+              int64_t st, int64_t sh, int64_t sb) {
+  memset(mk, 0, sizeof(CUtensorMap));
+  memset(mv, 0, sizeof(CUtensorMap));
+  if constexpr (!is16<T>()) {
+    return SD_OK;
+  } else {
+    const int dt = std::is_same<T, __nv_bfloat16>::value ? SD_DTYPE_BF16 : SD_DTYPE_F16;
+    int r = encode_rows_map(mk, kc, dt, kD, T_, H, B, st, sh, sb, kRows);
+    if (r == SD_OK) r = encode_rows_map(mv, vc, dt, kD, T_, H, B, st, sh, sb, kRows);
+    return r;
+  }
+}
+
+template <typename T, int G>
+int launch_decode_attention(const void *q, int64_t B, int64_t Hkv, int64_t q_sb, int64_t q_sh, const void *kc,
+                            const void *vc, int64_t c_sb, int64_t c_sh, int64_t c_st, int64_t Tcap,
+                            const int32_t *sel, const int32_t *cnt, int ms_cap, int64_t L, int bs, float scale,
+                            void *out, int64_t o_sb, int64_t o_sh, int32_t *err, cudaStream_t s) {
+  const size_t smem = AttnSmem<T, G>::bytes() + sizeof(int) * ms_cap + kAlignSlack;
+  // the tensor-core path needs contiguous rows laid out [B][H][T] in memory order
+  const bool tma = is16<T>() && c_st == kD && c_sh >= Tcap * kD && c_sb >= Hkv * c_sh;
+  CUtensorMap mk, mv;
+  int r = tma ? make_maps<T>(&mk, &mv, kc, vc, B, Hkv, Tcap, c_st, c_sh, c_sb)
+              : make_maps<float>(&mk, &mv, kc, vc, B, Hkv, Tcap, c_st, c_sh, c_sb);
+  if (r != SD_OK) return r;
+  const dim3 grid(static_cast<unsigned>(B * Hkv));
+  if constexpr (is16<T>()) {
+    if (tma) {
+      auto kern = decode_attention_kernel<T, G, true>;
+      if (set_max_smem(kern, smem) != SD_OK) return SD_ERR_CUDA;
+      kern<<<grid, kThreads, smem, s>>>(static_cast<const T *>(q), (int)Hkv, q_sb, q_sh,
+                                        static_cast<const T *>(kc), static_cast<const T *>(vc), c_sb, c_sh, c_st, mk,
+                                        mv, sel, cnt, ms_cap, L, bs, scale * kLog2e, static_cast<T *>(out), o_sb,
+                                        o_sh, err);
+      return check_launch();
+    }
+  }
+  {
+    auto kern = decode_attention_kernel<T, G, false>;
+    if (set_max_smem(kern, smem) != SD_OK) return SD_ERR_CUDA;
+    kern<<<grid, kThreads, smem, s>>>(static_cast<const T *>(q), (int)Hkv, q_sb, q_sh, static_cast<const T *>(kc),
+                                      static_cast<const T *>(vc), c_sb, c_sh, c_st, mk, mv, sel, cnt, ms_cap, L, bs,
+                                      scale * kLog2e, static_cast<T *>(out), o_sb, o_sh, err);
+  }
   return check_launch();
 }
 
@@ -424,27 +637,31 @@ int launch_decode_layer(const void *qkv, int64_t qkv_sb, const void *fc, int64_t
                         cudaStream_t s) {
   const int64_t lst = NBcap > top_k + 2 ? NBcap : top_k + 2;
   const size_t smem =
-      AttnSmem<T, G>::bytes() + sizeof(float) * (kD + NBcap) + sizeof(int) * (lst + top_k) + 128;
+      AttnSmem<T, G>::bytes() + sizeof(float) * (kD + NBcap) + sizeof(int) * (lst + top_k) + kAlignSlack;
+  CUtensorMap mk, mv;
+  const int r = make_maps<T>(&mk, &mv, kc, vc, B, Hkv, Tcap, kD, Tcap * kD, Hkv * Tcap * kD);
+  if (r != SD_OK) return r;
   auto kern = decode_layer_kernel<T, F, G>;
   if (set_max_smem(kern, smem) != SD_OK) return SD_ERR_CUDA;
   kern<<<static_cast<unsigned>(B * Hkv), kThreads, smem, s>>>(
       static_cast<const T *>(qkv), qkv_sb, static_cast<const F *>(fc), f_sb, rc, rs, cur_len,
       static_cast<T *>(kc), static_cast<T *>(vc), ps, (int)Hkv, Tcap, NBcap, bs, top_k, rule,
-      scale / static_cast<float>(bs), scale * kLog2e, static_cast<T *>(out), o_sb, sel_out, cnt_out, sel_cap, err);
+      scale / static_cast<float>(bs), scale * kLog2e, mk, mv, static_cast<T *>(out), o_sb, sel_out, cnt_out,
+      sel_cap, err);
   return check_launch();
 }
 
 }  // namespace sd
 
-#define SD_DISPATCH_G(G, ...)                          \
-  switch (G) {                                         \
+#define SD_DISPATCH_G(G, ...)                             \
+  switch (G) {                                            \
     case 1: { constexpr int GG = 1; __VA_ARGS__; } break; \
     case 2: { constexpr int GG = 2; __VA_ARGS__; } break; \
     case 3: { constexpr int GG = 3; __VA_ARGS__; } break; \
     case 4: { constexpr int GG = 4; __VA_ARGS__; } break; \
     case 6: { constexpr int GG = 6; __VA_ARGS__; } break; \
     case 8: { constexpr int GG = 8; __VA_ARGS__; } break; \
-    default: return SD_ERR_UNSUPPORTED;                \
+    default: return SD_ERR_UNSUPPORTED;                   \
   }
 
 extern "C" int sd_decode_attention(const void *q, int dtype, int64_t B, int64_t Hq, int64_t Hkv, int64_t D,
@@ -456,7 +673,7 @@ extern "C" int sd_decode_attention(const void *q, int dtype, int64_t B, int64_t 
   if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || seq_len_k <= 0 || seq_len_k > Tcap || block_size <= 0 ||
       ms_cap <= 0)
     return SD_ERR_INVALID;
-  if (D != sd::kD || B * Hkv > 0x7fffffff) return SD_ERR_UNSUPPORTED;
+  if (D != sd::kD || B * Hkv > 0x7fffffff || B > 0x7fffffff / 2) return SD_ERR_UNSUPPORTED;
   if (static_cast<int64_t>(ms_cap) * ((block_size + sd::kRows - 1) / sd::kRows) > sd::kMaxTiles)
     return SD_ERR_UNSUPPORTED;
   const int es = sd::dtype_size(dtype);
@@ -466,8 +683,8 @@ extern "C" int sd_decode_attention(const void *q, int dtype, int64_t B, int64_t 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int G = static_cast<int>(Hq / Hkv);
   SD_DISPATCH_DTYPE(dtype, E, {
-    SD_DISPATCH_G(G, return sd::launch_decode_attention<E, GG>(q, B, Hkv, q_sb, q_sh, k_cache, v_cache, c_sb,
-                                                                c_sh, c_st, sel, cnt, ms_cap, seq_len_k,
+    SD_DISPATCH_G(G, return sd::launch_decode_attention<E, GG>(q, B, Hkv, q_sb, q_sh, k_cache, v_cache, c_sb, c_sh,
+                                                                c_st, Tcap, sel, cnt, ms_cap, seq_len_k,
                                                                 block_size, scale, out, o_sb, o_sh, err, s));
   });
   return SD_OK;
@@ -503,7 +720,8 @@ extern "C" int sd_decode_layer(const void *qkv, int dtype, int64_t qkv_sb, const
     } else if (fdt == SD_DTYPE_F32) {
       SD_DISPATCH_G(G, return sd::launch_decode_layer<E, float, GG>(
                            qkv, qkv_sb, forecast, f_sb, rope_cos, rope_sin, cur_len, k_cache, v_cache, proto_sum,
-                           B, Hkv, Tcap, NBcap, block_size, top_k, rule, scale, out, o_sb, sel_out, cnt_out, sel_cap, err, s));
+                           B, Hkv, Tcap, NBcap, block_size, top_k, rule, scale, out, o_sb, sel_out, cnt_out,
+                           sel_cap, err, s));
     } else {
       return SD_ERR_UNSUPPORTED;
     }

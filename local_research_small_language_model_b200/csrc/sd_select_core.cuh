@@ -79,8 +79,36 @@ __device__ __forceinline__ void build_decode_list(bool use_forecast, const float
     return;
   }
   const int kk = top_k < nb ? top_k : nb;
-  if (use_forecast && threadIdx.x < 32) {
-    warp_topk([&](int j) { return j < n_scored ? scores[j] : -INFINITY; }, nb, kk, topk_tmp, nullptr);
+  if (use_forecast) {
+    // every warp takes the top-kk of a contiguous slice of blocks, then warp 0
+    // merges the slices' candidates under the same total order
+    __shared__ int cand_i[256];
+    __shared__ float cand_v[256];
+    const int nw = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    auto score = [&](int j) { return j < n_scored ? scores[j] : -INFINITY; };
+    if (nw * kk <= 256 && nb >= 4 * 32) {
+      const int seg = (nb + nw - 1) / nw;
+      const int lo = warp * seg, len = lo < nb ? (nb - lo < seg ? nb - lo : seg) : 0;
+      int *ci = cand_i + warp * kk;
+      if (len >= kk) {
+        warp_topk([&](int j) { return score(lo + j); }, len, kk, ci, nullptr);
+        __syncwarp();
+        for (int r = lane; r < kk; r += 32) {
+          ci[r] += lo;
+          cand_v[warp * kk + r] = score(ci[r]);
+        }
+      } else {  // short slice: take it whole, pad with entries that never win
+        for (int r = lane; r < kk; r += 32) {
+          ci[r] = r < len ? lo + r : 0x70000000 + warp * 64 + r;
+          cand_v[warp * kk + r] = r < len ? score(lo + r) : -INFINITY;
+        }
+      }
+      __syncthreads();
+      if (warp == 0)
+        warp_topk_kv([&](int c) { return cand_v[c]; }, [&](int c) { return cand_i[c]; }, nw * kk, kk, topk_tmp);
+    } else if (threadIdx.x < 32) {
+      warp_topk(score, nb, kk, topk_tmp, nullptr);
+    }
   }
   __syncthreads();
   if (threadIdx.x == 0) {

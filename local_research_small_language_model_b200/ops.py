@@ -235,6 +235,58 @@ def decode_layer(qkv: torch.Tensor, forecast: Optional[torch.Tensor], rope_cos: 
     return out
 
 
+# ---------------------------------------------------------------- prefill
+LIST_MODES = {"dense": 0, "masked_forecast": 1, "masked_static": 2, "chunked_forecast": 3, "chunked_static": 4}
+
+
+def prefill_lists(mode: str, batch: int, n_kv_head: int, seq_len: int, block_size: int, top_k: int,
+                  topk: Optional[torch.Tensor] = None, causal: bool = True, device=None
+                  ) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Per-(sequence, kv head, 64-token query block) block lists of the prefill
+    paths (model/attention/sparse.py:185-364); see SD_LIST_* in the C header.
+    topk [B,H,T,k] int64 for the *_forecast modes.  Returns (lists [B,H,NQ,cap]
+    int32 ascending and -1 padded, counts [B,H,NQ] int32)."""
+    nb = num_blocks(seq_len, block_size)
+    cap = min(nb, top_k + 2) if mode.startswith("chunked") else (nb if mode != "masked_static" else top_k + 2)
+    dev = topk.device if topk is not None else device
+    lists = torch.empty(batch, n_kv_head, nb, cap, dtype=torch.int32, device=dev)
+    counts = torch.empty(batch, n_kv_head, nb, dtype=torch.int32, device=dev)
+    if topk is not None:
+        _cuda(topk)
+        topk = topk.to(torch.int64).contiguous()
+    L.call("sd_prefill_lists", LIST_MODES[mode], int(bool(causal)), batch, n_kv_head, seq_len, block_size, top_k,
+           topk.data_ptr() if topk is not None else None, topk.shape[-1] if topk is not None else 0,
+           lists.data_ptr(), counts.data_ptr(), cap, torch.cuda.current_stream(dev).cuda_stream)
+    return lists, counts
+
+
+def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, lists: torch.Tensor, counts: torch.Tensor,
+                      block_size: int, topk: Optional[torch.Tensor] = None, causal: bool = True,
+                      scale: Optional[float] = None) -> torch.Tensor:
+    """Block-sparse GQA prefill attention over prefill_lists' lists.
+    q [B,T,Hq,D]; k, v [B,Hkv,T,D] views (same strides); topk [B,H,T,k] for
+    per-row membership (masked forecast mode).  Returns [B,T,Hq,D]."""
+    _cuda(q, k, v, lists, counts, topk)
+    b, t, hq, d = q.shape
+    hkv = k.shape[1]
+    if k.stride() != v.stride():
+        k, v = k.contiguous(), v.contiguous()
+    q, k, v = _inner1(q), _inner1(k), _inner1(v)
+    if k.stride() != v.stride():
+        k, v = k.contiguous(), v.contiguous()
+    if q.dtype != k.dtype:
+        q = q.to(k.dtype)
+    out = torch.empty(b, t, hq, d, dtype=k.dtype, device=q.device)
+    tk = topk.to(torch.int64).contiguous() if topk is not None else None
+    sc = 1.0 / math.sqrt(d) if scale is None else scale
+    L.call("sd_prefill_attention", q.data_ptr(), dtype_code(k), b, t, hq, hkv, d, q.stride(0), q.stride(1),
+           q.stride(2), k.data_ptr(), v.data_ptr(), k.stride(0), k.stride(1), k.stride(2), lists.data_ptr(),
+           counts.data_ptr(), lists.shape[-1], tk.data_ptr() if tk is not None else None,
+           tk.shape[-1] if tk is not None else 0, block_size, int(bool(causal)), sc, out.data_ptr(), out.stride(0),
+           out.stride(1), out.stride(2), _stream(q))
+    return out
+
+
 def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
     """RMSNorm (model/norm.py:15-21) over the last dim of a 2-D [rows, C] tensor."""
     _cuda(x, weight)
