@@ -66,6 +66,36 @@ __device__ __forceinline__ void score_blocks(const float *__restrict__ reps, int
   }
 }
 
+// The union {0, curr} U top-k (use_forecast) or {0} U the static window
+// ending at curr, future blocks cleared (sparse.py:126-151), written to
+// list in ascending order; returns its length.  One thread.
+__device__ __forceinline__ int assemble_decode_list(bool use_forecast, const int *topk, int kk, int nb, int curr,
+                                                    int top_k, int *list) {
+  int n = 0;
+  auto add = [&](int j) {
+    if (j < 0 || j > curr) return;  // future blocks are cleared (sparse.py:150-151)
+    int p = n;
+    for (int i = 0; i < n; ++i) {
+      if (list[i] == j) return;
+      if (list[i] > j) {
+        p = i;
+        break;
+      }
+    }
+    for (int i = n; i > p; --i) list[i] = list[i - 1];
+    list[p] = j;
+    ++n;
+  };
+  add(0);
+  add(curr);
+  if (use_forecast) {
+    for (int i = 0; i < kk; ++i) add(topk[i] < nb - 1 ? topk[i] : nb - 1);
+  } else {
+    for (int j = curr - top_k + 1 > 0 ? curr - top_k + 1 : 0; j <= curr; ++j) add(j);
+  }
+  return n;
+}
+
 // Builds the ascending selected-block list into list[0..*count).  `scores`
 // holds the scores of blocks 0..n_scored-1; blocks n_scored..nb-1 count as -inf.
 // topk_tmp needs room for top_k ints.  Must be called by all threads.
@@ -111,31 +141,7 @@ __device__ __forceinline__ void build_decode_list(bool use_forecast, const float
     }
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int n = 0;
-    auto add = [&](int j) {
-      if (j < 0 || j > curr) return;  // future blocks are cleared (sparse.py:150-151)
-      int p = n;
-      for (int i = 0; i < n; ++i) {
-        if (list[i] == j) return;
-        if (list[i] > j) {
-          p = i;
-          break;
-        }
-      }
-      for (int i = n; i > p; --i) list[i] = list[i - 1];
-      list[p] = j;
-      ++n;
-    };
-    add(0);
-    add(curr);
-    if (use_forecast) {
-      for (int i = 0; i < kk; ++i) add(topk_tmp[i] < nb - 1 ? topk_tmp[i] : nb - 1);
-    } else {
-      for (int j = curr - top_k + 1 > 0 ? curr - top_k + 1 : 0; j <= curr; ++j) add(j);
-    }
-    *count = n;
-  }
+  if (threadIdx.x == 0) *count = assemble_decode_list(use_forecast, topk_tmp, kk, nb, curr, top_k, list);
   __syncthreads();
 }
 
