@@ -80,6 +80,10 @@ template <> __device__ __forceinline__ float2 load2<float>(const float *row, int
 // ---------------------------------------------------------------- shared memory
 // Carve-up common to both kernels.  The stage buffers come first so that they
 // sit on the 1024-byte boundary the 128-byte TMA swizzle needs.
+// Every region is rounded up to 128 bytes, so each one (and the tail, which
+// holds rows read with 16-byte vector loads) starts 128-byte aligned.
+__host__ __device__ constexpr size_t round128(size_t n) { return (n + 127) & ~static_cast<size_t>(127); }
+
 template <typename T, int G, int NS> struct AttnSmem {
   T *k;            // [NS][kRows][kD]
   T *v;            // [NS][kRows][kD]
@@ -89,20 +93,22 @@ template <typename T, int G, int NS> struct AttnSmem {
   int *tile_n;     // [kMaxTiles]
   float *red;      // [kWarps][G][kD + 2]
   char *tail;      // kernel-specific
-  static constexpr size_t bytes() {
-    return 2 * sizeof(T) * NS * kRows * kD + sizeof(uint64_t) * NS + sizeof(float) * G * kD +
-           2 * sizeof(int) * kMaxTiles + sizeof(float) * kWarps * G * (kD + 2);
-  }
+  static constexpr size_t kKV = round128(sizeof(T) * NS * kRows * kD);
+  static constexpr size_t kFull = round128(sizeof(uint64_t) * NS);
+  static constexpr size_t kQ = round128(sizeof(float) * G * kD);
+  static constexpr size_t kTiles = round128(sizeof(int) * kMaxTiles);
+  static constexpr size_t kRed = round128(sizeof(float) * kWarps * G * (kD + 2));
+  static constexpr size_t bytes() { return 2 * kKV + kFull + kQ + 2 * kTiles + kRed; }
   __device__ explicit AttnSmem(char *raw) {
     char *base = raw + ((1024u - (smem_u32(raw) & 1023u)) & 1023u);
     k = reinterpret_cast<T *>(base);
-    v = k + NS * kRows * kD;
-    full = reinterpret_cast<uint64_t *>(v + NS * kRows * kD);
-    q = reinterpret_cast<float *>(full + NS);
-    tile_tok = reinterpret_cast<int *>(q + G * kD);
-    tile_n = tile_tok + kMaxTiles;
-    red = reinterpret_cast<float *>(tile_n + kMaxTiles);
-    tail = reinterpret_cast<char *>(red + kWarps * G * (kD + 2));
+    v = reinterpret_cast<T *>(base + kKV);
+    full = reinterpret_cast<uint64_t *>(base + 2 * kKV);
+    q = reinterpret_cast<float *>(base + 2 * kKV + kFull);
+    tile_tok = reinterpret_cast<int *>(base + 2 * kKV + kFull + kQ);
+    tile_n = reinterpret_cast<int *>(base + 2 * kKV + kFull + kQ + kTiles);
+    red = reinterpret_cast<float *>(base + 2 * kKV + kFull + kQ + 2 * kTiles);
+    tail = base + bytes();
   }
 };
 constexpr size_t kAlignSlack = 1024;
