@@ -225,6 +225,8 @@ def run_b200(args, rank, world, local):
     for layer in model.layers:
         p = {"start": torch.cuda.Event(enable_timing=True, external=True),
              "end": torch.cuda.Event(enable_timing=True, external=True),
+             "cstart": torch.cuda.Event(enable_timing=True, external=True),
+             "cend": torch.cuda.Event(enable_timing=True, external=True),
              "sel": torch.full((B, 4, 16), -1, dtype=torch.int32, device=dev),
              "cnt": torch.zeros(B, 4, dtype=torch.int32, device=dev)}
         layer.probe = p
@@ -296,26 +298,33 @@ def run_b200(args, rank, world, local):
 
         # ---- roofline of the fused decode kernel (instrumented graph)
         k_ms, k_bytes, k_launch = 0.0, 0.0, 0
+        c_ms, c_bytes, c_launch = 0.0, 0.0, 0
+        np_ = __import__("numpy")
         for i in range(args.probe_steps):
             inst.step()
             torch.cuda.synchronize()
             L = caches[0].current_len  # tokens after the step (the new one included)
+            nb = (L + 63) // 64
             for li, p in enumerate(probes):
                 k_ms += p["start"].elapsed_time(p["end"])
                 k_launch += 1
                 sel = p["sel"].cpu().numpy()
                 cnt = p["cnt"].cpu().numpy()
                 rows = 0
-                for (b_, h_), c_ in __import__("numpy").ndenumerate(cnt):
+                for (b_, h_), c_ in np_.ndenumerate(cnt):
                     for j in sel[b_, h_, :c_]:
                         rows += min(64, L - int(j) * 64)
-                nb = (L + 63) // 64
-                n_scored = 0 if li == 0 else (nb if args.rule == "absolute" else 1) * B * 4
                 k_bytes += (rows * 64 * 2 * 2            # selected K and V rows (bf16)
-                            + n_scored * 64 * 4          # fp32 prototype rows scored
+                            + B * 4 * 64 * 4             # the current block's running sum, scored in-kernel
                             + B * (1280 + 256 + 768) * 2  # q|k|v in, forecast in, attention out
                             + B * 4 * 64 * 2 * 2         # new K and V rows written
-                            + B * 4 * 64 * 4 * 2)        # running block sum read + write
+                            + B * 4 * 64 * 4 * 2         # running block sum read + write
+                            + B * 4 * 8 * 8)             # candidates read
+                if li + 1 < len(probes):  # this block launched layer li+1's candidates
+                    c_ms += p["cstart"].elapsed_time(p["cend"])
+                    c_launch += 1
+                    n_sc = (nb - 1) if args.rule == "absolute" else 1
+                    c_bytes += B * 4 * (n_sc * 64 * 4 + 64 * 2 + 8 * 8)  # fp32 sums scored, forecast, output
             if (i + 1) % W == 0:
                 rewind(W)
         rewind(caches[0].current_len - ctx)
@@ -326,6 +335,8 @@ def run_b200(args, rank, world, local):
     hbm, src = read_peaks()
     avg_launch_s = k_ms / 1000.0 / k_launch
     bytes_per_launch = k_bytes / k_launch
+    c_avg_s = c_ms / 1000.0 / max(c_launch, 1)
+    c_gbs = (c_bytes / max(c_launch, 1)) / c_avg_s / 1e9 if c_launch else None
     achieved = bytes_per_launch / avg_launch_s / 1e9
     result = {
         "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -341,13 +352,22 @@ def run_b200(args, rank, world, local):
                          "exceeds the 126 MB L2"},
         "e2e": {"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": B * 8, "d2h_bytes_per_step": B * 8,
                 "steps": ke, "note": "pinned host token ids in, argmax ids out and read on the host every step"},
-        "gpu_launches": args.steps * (cfg.n_layer + 1),
+        # per step: fused decode (12) + side-stream candidates (11) + RMSNorm (25)
+        # + SwiGLU gate (12) + length bump (1) kernels of libspardab200.so
+        "gpu_launches": args.steps * (cfg.n_layer + (cfg.n_layer - 1) + (2 * cfg.n_layer + 1) + cfg.n_layer + 1),
         "roofline": {"bound": "hbm", "kernel": "sd::decode_layer_kernel<bf16,bf16,3>",
                      "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(achieved / hbm, 4), "peak_source": src,
                      "traffic": read_traffic("decode_layer"),
                      "bytes_per_launch": round(bytes_per_launch), "avg_launch_us": round(avg_launch_s * 1e6, 3),
-                     "launches_sampled": k_launch},
+                     "launches_sampled": k_launch,
+                     "selector_kernel": {"kernel": "sd::decode_candidates_kernel<bf16> (side stream)",
+                                         "achieved": round(c_gbs, 1) if c_gbs else None, "unit": "GB/s",
+                                         "frac": round(c_gbs / hbm, 4) if c_gbs else None,
+                                         "bytes_per_launch": round(c_bytes / max(c_launch, 1)),
+                                         "avg_launch_us": round(c_avg_s * 1e6, 3), "launches_sampled": c_launch},
+                     "path": {"achieved": round((k_bytes + c_bytes) / ((k_ms + c_ms) / 1000.0) / 1e9, 1),
+                              "note": "decode + candidate kernels' algorithmic bytes over their summed time"}},
         "clocks": clock_info,
     }
     return result

@@ -154,6 +154,9 @@ SD_API int sd_kv_append(const void *xk, const void *xv, int dtype, int64_t B, in
  * rope_cos/sin: fp32 [max_pos, D/2].  cur_len: device int32, tokens cached
  * before this step (the new token is written at that position).
  * Caches as in sd_kv_append.  out: [B, Hq*D] rows with stride o_sb.
+ * cand_idx/cand_val (nullable, together): candidates from
+ * sd_decode_candidates for this step; without them the kernel scores every
+ * prototype itself (same result).
  * sel_out/cnt_out (nullable, together): the selected block list of every
  * (sequence, kv head), int32 [B,Hkv,sel_cap] ascending and -1 padded, and its
  * length int32 [B,Hkv]; sel_cap >= top_k + 2. */
@@ -162,8 +165,23 @@ SD_API int sd_decode_layer(const void *qkv, int dtype, int64_t qkv_sb, const voi
                     int64_t max_pos, const int32_t *cur_len, void *k_cache, void *v_cache,
                     float *proto_sum, int64_t B, int64_t Hq, int64_t Hkv, int64_t D,
                     int64_t Tcap, int64_t NBcap, int block_size, int top_k, int rule,
-                    float scale, void *out, int64_t o_sb, int32_t *sel_out, int32_t *cnt_out,
-                    int sel_cap, int32_t *err, void *stream);
+                    float scale, void *out, int64_t o_sb, const int32_t *cand_idx,
+                    const float *cand_val, int32_t *sel_out, int32_t *cnt_out, int sel_cap,
+                    int32_t *err, void *stream);
+
+/* Forecast candidates for the next decode step of one layer, computed ahead
+ * of time (e.g. on a side stream while the previous layer runs): the top-k
+ * blocks, scored as in sd_decode_select, over every cached block except the
+ * current one (the block the next token lands in, whose sum that step
+ * changes).  sd_decode_layer merges them with the current block's fresh score,
+ * which gives the same top-k as scoring every block in the step.
+ * forecast: [B, Hkv*D] rows (stride f_sb); proto_sum as in sd_kv_append;
+ * cur_len: device int32, tokens cached before the step.  cand_idx int32 /
+ * cand_val fp32: [B,Hkv,top_k], -1 / -inf where no candidate exists. */
+SD_API int sd_decode_candidates(const void *forecast, int f_dtype, int64_t f_sb, const float *proto_sum,
+                                int64_t B, int64_t Hkv, int64_t D, int64_t NBcap, const int32_t *cur_len,
+                                int block_size, int top_k, int rule, float scale, int32_t *cand_idx,
+                                float *cand_val, void *stream);
 
 /* ---- prefill block-list modes (sd_prefill_lists) ----
  * One list per (sequence, kv head, 64-token query block qb), ascending:

@@ -1,9 +1,12 @@
 // K7 block-sparse GQA decode attention and the fused decode layer
 // (RoPE + KV append + compressor update + selection + attention).
 //
-// Staging: the selected KV blocks are cut into tiles of at most 64 cached rows
-// of ONE block, staged into shared memory through a ring of NS stages
-// completed on mbarriers.
+// Work split: one CTA (4 warps) per (sequence, kv head).  The selected KV
+// blocks are cut into tiles of at most 64 cached rows of ONE block, staged into
+// shared memory through a 6-stage ring completed on mbarriers, so up to 6
+// tiles (K and V) are in flight per CTA while earlier ones are consumed.
+//
+// Two staging/compute paths:
 //   * 16-bit caches whose rows are contiguous (the block-major cache of this
 //     library): each tile is one TMA tensor copy (cp.async.bulk.tensor, 128-byte
 //     swizzle) per K and V; warp w takes keys 16w..16w+15 of a tile and runs
@@ -12,32 +15,23 @@
 //   * fp32 caches (exact fp32 parity) and strided 16-bit caches: bulk copies of
 //     rows and the same split of keys over warps on CUDA cores.
 // Each warp keeps an online-softmax state (fp32, base-2 exponent) for all G
-// heads; warp states are merged through shared memory.
-//
-// The standalone attention kernel uses one CTA per (sequence, kv head).  The
-// fused decode layer uses a thread-block cluster of kCluster CTAs per
-// (sequence, kv head): every CTA scores a contiguous slice of the prototypes
-// and keeps its slice's top-k; the candidates are exchanged through
-// distributed shared memory and merged identically in every CTA; the tiles of
-// the selected blocks are dealt round-robin over the CTAs; the CTAs' softmax
-// states are merged by rank 0 over distributed shared memory.  No global
-// scratch memory is used.
-#include <cooperative_groups.h>
-
+// heads; the four warp states are merged at the end.
+// The fused kernel issues every tile it can name before any selection work -
+// the sink and current blocks always, the whole list on static-window and
+// dense steps - at kernel start, so the copies overlap the append and the
+// scoring; the new token's K/V rows are patched into the staged tile in shared
+// memory.  Selection either runs in the kernel or is merged from candidates a
+// separate kernel computed earlier (sd_decode_candidates).
 #include <type_traits>
 
 #include "sd_select_core.cuh"
 #include "sd_tma.cuh"
 
-namespace cg = cooperative_groups;
-
 namespace sd {
 
 constexpr int kD = 64;          // head_dim the attention kernels implement
 constexpr int kRows = 64;       // rows per tile
-constexpr int kStages = 6;      // ring depth of the standalone attention kernel
-constexpr int kClStages = 3;    // ring depth of each CTA of the fused (cluster) kernel
-constexpr int kCluster = 4;     // CTAs per (sequence, kv head) in the fused kernel
+constexpr int kStages = 6;
 constexpr int kThreads = 128;
 constexpr int kWarps = kThreads / 32;
 constexpr int kMaxTiles = 256;
@@ -79,36 +73,48 @@ template <> __device__ __forceinline__ float2 load2<float>(const float *row, int
 
 // ---------------------------------------------------------------- shared memory
 // Carve-up common to both kernels.  The stage buffers come first so that they
-// sit on the 1024-byte boundary the 128-byte TMA swizzle needs.
-// Every region is rounded up to 128 bytes, so each one (and the tail, which
-// holds rows read with 16-byte vector loads) starts 128-byte aligned.
+// sit on the 1024-byte boundary the 128-byte TMA swizzle needs; every region
+// is rounded up to 128 bytes, so each one (and the tail, which holds rows read
+// with 16-byte vector loads) starts 128-byte aligned.
 __host__ __device__ constexpr size_t round128(size_t n) { return (n + 127) & ~static_cast<size_t>(127); }
 
-template <typename T, int G, int NS> struct AttnSmem {
-  T *k;            // [NS][kRows][kD]
-  T *v;            // [NS][kRows][kD]
-  uint64_t *full;  // [NS]
+template <typename T, int G> struct AttnSmem {
+  T *k;            // [kStages][kRows][kD]
+  T *v;            // [kStages][kRows][kD]
+  uint64_t *full;  // [kStages]
   float *q;        // [G][kD]
   int *tile_tok;   // [kMaxTiles]
   int *tile_n;     // [kMaxTiles]
   float *red;      // [kWarps][G][kD + 2]
+  T *newkv;        // [2][kD] the new token's K and V rows (fused kernel)
   char *tail;      // kernel-specific
-  static constexpr size_t kKV = round128(sizeof(T) * NS * kRows * kD);
-  static constexpr size_t kFull = round128(sizeof(uint64_t) * NS);
+  static constexpr size_t kKV = round128(sizeof(T) * kStages * kRows * kD);
+  static constexpr size_t kFull = round128(sizeof(uint64_t) * kStages);
   static constexpr size_t kQ = round128(sizeof(float) * G * kD);
   static constexpr size_t kTiles = round128(sizeof(int) * kMaxTiles);
   static constexpr size_t kRed = round128(sizeof(float) * kWarps * G * (kD + 2));
-  static constexpr size_t bytes() { return 2 * kKV + kFull + kQ + 2 * kTiles + kRed; }
+  static constexpr size_t kNew = round128(sizeof(T) * 2 * kD);
+  static constexpr size_t bytes() { return 2 * kKV + kFull + kQ + 2 * kTiles + kRed + kNew; }
   __device__ explicit AttnSmem(char *raw) {
     char *base = raw + ((1024u - (smem_u32(raw) & 1023u)) & 1023u);
-    k = reinterpret_cast<T *>(base);
-    v = reinterpret_cast<T *>(base + kKV);
-    full = reinterpret_cast<uint64_t *>(base + 2 * kKV);
-    q = reinterpret_cast<float *>(base + 2 * kKV + kFull);
-    tile_tok = reinterpret_cast<int *>(base + 2 * kKV + kFull + kQ);
-    tile_n = reinterpret_cast<int *>(base + 2 * kKV + kFull + kQ + kTiles);
-    red = reinterpret_cast<float *>(base + 2 * kKV + kFull + kQ + 2 * kTiles);
-    tail = base + bytes();
+    size_t o = 0;
+    k = reinterpret_cast<T *>(base + o);
+    o += kKV;
+    v = reinterpret_cast<T *>(base + o);
+    o += kKV;
+    full = reinterpret_cast<uint64_t *>(base + o);
+    o += kFull;
+    q = reinterpret_cast<float *>(base + o);
+    o += kQ;
+    tile_tok = reinterpret_cast<int *>(base + o);
+    o += kTiles;
+    tile_n = reinterpret_cast<int *>(base + o);
+    o += kTiles;
+    red = reinterpret_cast<float *>(base + o);
+    o += kRed;
+    newkv = reinterpret_cast<T *>(base + o);
+    o += kNew;
+    tail = base + o;
   }
 };
 constexpr size_t kAlignSlack = 1024;
@@ -170,54 +176,15 @@ struct TmaLoader {
   }
 };
 
-template <typename T, int G, int NS, typename Ld>
-__device__ __forceinline__ void issue_tile(AttnSmem<T, G, NS> &S, int t, const Ld &ld) {
-  const int s = t % NS;
+template <typename T, int G, typename Ld>
+__device__ __forceinline__ void issue_tile(AttnSmem<T, G> &S, int t, const Ld &ld) {
+  const int s = t % kStages;
   ld(S.k + s * kRows * kD, S.v + s * kRows * kD, S.tile_tok[t], S.tile_n[t], &S.full[s]);
 }
 
-// Waits for tile t; the verdict is made uniform per warp.
-template <int NS> __device__ __forceinline__ bool wait_tile(uint64_t *full, int t) {
-  bool got = mbar_wait_bounded(&full[t % NS], (t / NS) & 1);
-  return __all_sync(0xffffffffu, got);
-}
-
-// After a bounded wait expired: let the copies still in flight land before
-// the CTA's shared memory is released.
-template <typename T, int G, int NS>
-__device__ __forceinline__ void drain(AttnSmem<T, G, NS> &S, int t, int ntiles) {
-  for (int u = t; u < ntiles && u < t + NS; ++u) mbar_wait_bounded(&S.full[u % NS], (u / NS) & 1);
-  __syncthreads();
-}
-
-// Merges the per-warp states of S.red into one state per head:
-// st[g] = {max, sum, acc[kD]} with acc and sum relative to that max.
-template <typename T, int G, int NS>
-__device__ __forceinline__ void merge_warps(AttnSmem<T, G, NS> &S, float *st) {
-  for (int e = threadIdx.x; e < G * (kD + 2); e += blockDim.x) {
-    const int g = e / (kD + 2), c = e - g * (kD + 2);
-    float M = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, S.red[(w * G + g) * (kD + 2)]);
-    if (c == 0) {
-      st[e] = M;
-      continue;
-    }
-    float acc = 0.f;
-    if (M != -INFINITY) {
-#pragma unroll
-      for (int w = 0; w < kWarps; ++w) {
-        const float *r = S.red + (w * G + g) * (kD + 2);
-        acc = fmaf(r[c], exp2f(r[0] - M), acc);
-      }
-    }
-    st[e] = acc;
-  }
-}
-
-// Merges the per-warp states and stores out[g*o_hs + d].
-template <typename T, int G, int NS>
-__device__ __forceinline__ void combine_store(AttnSmem<T, G, NS> &S, T *out, int64_t o_hs) {
+// Merges the per-warp states written to S.red and stores out[g*o_hs + d].
+template <typename T, int G>
+__device__ __forceinline__ void combine_store(AttnSmem<T, G> &S, T *out, int64_t o_hs) {
   for (int e = threadIdx.x; e < G * kD; e += blockDim.x) {
     const int g = e / kD, d = e - g * kD;
     float M = -INFINITY;
@@ -237,15 +204,48 @@ __device__ __forceinline__ void combine_store(AttnSmem<T, G, NS> &S, T *out, int
   }
 }
 
+// Waits for tile t; returns the uniform "all threads got it" verdict through
+// the CTA barrier at the end of the tile (see the loops below).
+__device__ __forceinline__ bool wait_tile(uint64_t *full, int t) {
+  bool got = mbar_wait_bounded(&full[t % kStages], (t / kStages) & 1);
+  return __all_sync(0xffffffffu, got);
+}
+
+// After a bounded wait expired: let the copies still in flight land before
+// the CTA's shared memory is released.
+template <typename T, int G>
+__device__ __forceinline__ void drain(AttnSmem<T, G> &S, int t, int ntiles) {
+  for (int u = t; u < ntiles && u < t + kStages; ++u) mbar_wait_bounded(&S.full[u % kStages], (u / kStages) & 1);
+  __syncthreads();
+}
+
+// Writes the new token's K/V rows (S.newkv) into row `row` of staged tile t,
+// over whatever the copy brought for that row.  TMA tiles are 128-byte
+// swizzled, bulk tiles are linear.  All threads call it (t is CTA-uniform).
+template <typename T, int G>
+__device__ __forceinline__ void patch_tile_rows(AttnSmem<T, G> &S, int t, int row, bool swizzled) {
+  const int s = t % kStages;
+  if (threadIdx.x < kD) {
+    const int d = threadIdx.x;
+    char *kb = reinterpret_cast<char *>(S.k + s * kRows * kD);
+    char *vb = reinterpret_cast<char *>(S.v + s * kRows * kD);
+    uint32_t off = swizzled ? sw128(row, d >> 3) + (d & 7) * sizeof(T) : (row * kD + d) * sizeof(T);
+    *reinterpret_cast<T *>(kb + off) = S.newkv[d];
+    *reinterpret_cast<T *>(vb + off) = S.newkv[kD + d];
+    // the stage is refilled by the async proxy later: order these writes first
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  __syncthreads();
+}
+
 // ---------------------------------------------------------------- CUDA-core path
-// Leaves each warp's {m, l, acc} in S.red; returns false (uniformly) when a
-// bounded wait expired.  Tiles 0..pre_issued-1 were already issued by thread 0.
-template <typename T, int G, int NS, typename Ld>
-__device__ bool attend_simt(AttnSmem<T, G, NS> &S, int ntiles, int pre_issued, const Ld &ld, float scale_log2) {
+template <typename T, int G, typename Ld>
+__device__ bool attend_simt(AttnSmem<T, G> &S, int ntiles, int pre_issued, const Ld &ld, float scale_log2, T *out,
+                            int64_t o_hs, int patch_t = -1, int patch_row = 0) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int kg = lane >> 3, dc = lane & 7;
   if (tid == 0) {
-    for (int t = pre_issued; t < ntiles && t < NS; ++t) issue_tile(S, t, ld);
+    for (int t = pre_issued; t < ntiles && t < kStages; ++t) issue_tile(S, t, ld);
   }
   float qr[G][8];
 #pragma unroll
@@ -259,9 +259,11 @@ __device__ bool attend_simt(AttnSmem<T, G, NS> &S, int ntiles, int pre_issued, c
     l[g] = 0.f;
     acc[g][0] = acc[g][1] = 0.f;
   }
-  for (int t = 0; t < ntiles; ++t) {
-    const int s = t % NS;
-    const bool got = wait_tile<NS>(S.full, t);
+  int t = 0;
+  for (; t < ntiles; ++t) {
+    const int s = t % kStages;
+    const bool got = wait_tile(S.full, t);
+    if (t == patch_t) patch_tile_rows(S, t, patch_row, false);
     if (got) {
       const T *ks = S.k + s * kRows * kD;
       const T *vs = S.v + s * kRows * kD;
@@ -324,7 +326,7 @@ __device__ bool attend_simt(AttnSmem<T, G, NS> &S, int ntiles, int pre_issued, c
       drain(S, t, ntiles);
       return false;
     }
-    if (tid == 0 && t + NS < ntiles) issue_tile(S, t + NS, ld);
+    if (tid == 0 && t + kStages < ntiles) issue_tile(S, t + kStages, ld);
   }
   float *rw = S.red + warp * G * (kD + 2);
 #pragma unroll
@@ -337,6 +339,7 @@ __device__ bool attend_simt(AttnSmem<T, G, NS> &S, int ntiles, int pre_issued, c
     rw[g * (kD + 2) + 3 + 2 * lane] = acc[g][1];
   }
   __syncthreads();
+  combine_store(S, out, o_hs);
   return true;
 }
 
@@ -346,16 +349,15 @@ __device__ bool attend_simt(AttnSmem<T, G, NS> &S, int ntiles, int pre_issued, c
 // accumulators (a quad of lanes holds one head's 16 scores), then
 // O[heads x 64] += P V as 8 n-tiles x 1 k-step, P reused from the accumulator
 // registers as the A operand.  K fragments come from ldmatrix, V fragments
-// from ldmatrix.trans, both on the 128-byte-swizzled TMA tiles.  Leaves each
-// warp's {m, l, acc} in S.red.
-template <typename T, int G, int NS>
-__device__ bool attend_mma(AttnSmem<T, G, NS> &S, int ntiles, int pre_issued, const TmaLoader &ld,
-                           float scale_log2) {
+// from ldmatrix.trans, both on the 128-byte-swizzled TMA tiles.
+template <typename T, int G>
+__device__ bool attend_mma(AttnSmem<T, G> &S, int ntiles, int pre_issued, const TmaLoader &ld, float scale_log2,
+                           T *out, int64_t o_hs, int patch_t = -1, int patch_row = 0) {
   static_assert(G <= 8, "query heads per kv head must fit the 16 rows of the A operand");
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int grp = lane >> 2, tig = lane & 3;
   if (tid == 0) {
-    for (int t = pre_issued; t < ntiles && t < NS; ++t) issue_tile(S, t, ld);
+    for (int t = pre_issued; t < ntiles && t < kStages; ++t) issue_tile(S, t, ld);
   }
   uint32_t qa[4][2];
 #pragma unroll
@@ -369,9 +371,11 @@ __device__ bool attend_mma(AttnSmem<T, G, NS> &S, int ntiles, int pre_issued, co
 #pragma unroll
   for (int n = 0; n < 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
   float m = -INFINITY, l = 0.f;
-  for (int t = 0; t < ntiles; ++t) {
-    const int s = t % NS;
-    const bool got = wait_tile<NS>(S.full, t);
+  int t = 0;
+  for (; t < ntiles; ++t) {
+    const int s = t % kStages;
+    const bool got = wait_tile(S.full, t);
+    if (t == patch_t) patch_tile_rows(S, t, patch_row, true);
     int nv = S.tile_n[t] - 16 * warp;
     nv = nv < 0 ? 0 : (nv > 16 ? 16 : nv);
     if (got && nv > 0) {
@@ -430,10 +434,9 @@ __device__ bool attend_mma(AttnSmem<T, G, NS> &S, int ntiles, int pre_issued, co
       drain(S, t, ntiles);
       return false;
     }
-    if (tid == 0 && t + NS < ntiles) issue_tile(S, t + NS, ld);
+    if (tid == 0 && t + kStages < ntiles) issue_tile(S, t + kStages, ld);
   }
   float *rw = S.red + warp * G * (kD + 2);
-  // rows of heads the warp never saw keep m = -inf and contribute nothing
   if (grp < G) {
     float *r = rw + grp * (kD + 2);
     if (tig == 0) {
@@ -447,6 +450,7 @@ __device__ bool attend_mma(AttnSmem<T, G, NS> &S, int ntiles, int pre_issued, co
     }
   }
   __syncthreads();
+  combine_store(S, out, o_hs);
   return true;
 }
 
@@ -454,10 +458,10 @@ __device__ __forceinline__ void report(int32_t *err, int code) {
   if (err && threadIdx.x == 0) atomicExch(err, code);
 }
 
-template <typename T, int G, int NS>
-__device__ __forceinline__ void init_barriers(AttnSmem<T, G, NS> &S) {
+template <typename T, int G>
+__device__ __forceinline__ void init_barriers(AttnSmem<T, G> &S) {
   if (threadIdx.x == 0) {
-    for (int s = 0; s < NS; ++s) mbar_init(&S.full[s], 1);
+    for (int s = 0; s < kStages; ++s) mbar_init(&S.full[s], 1);
     mbar_init_fence();
   }
 }
@@ -472,7 +476,7 @@ __global__ void __launch_bounds__(kThreads)
                             int64_t L, int bs, float scale_log2, T *__restrict__ out, int64_t o_sb,
                             int64_t o_sh, int32_t *err) {
   extern __shared__ __align__(1024) char smem_raw[];
-  AttnSmem<T, G, kStages> S(smem_raw);
+  AttnSmem<T, G> S(smem_raw);
   int *list = reinterpret_cast<int *>(S.tail);
   __shared__ int ntiles;
   const int b = blockIdx.x / Hkv, h = blockIdx.x - (blockIdx.x / Hkv) * Hkv;
@@ -488,20 +492,17 @@ __global__ void __launch_bounds__(kThreads)
   __syncthreads();
   if (threadIdx.x == 0) ntiles = build_tiles(list, c, L, bs, S.tile_tok, S.tile_n);
   __syncthreads();
+  T *o = out + b * o_sb + static_cast<int64_t>(h * G) * o_sh;
   bool ok;
   if constexpr (kTma) {
     const TmaLoader ld{&tmk, &tmv, h, b};
-    ok = attend_mma<T, G, kStages>(S, ntiles, 0, ld, scale_log2);
+    ok = attend_mma<T, G>(S, ntiles, 0, ld, scale_log2, o, o_sh);
   } else {
     const int64_t cb = b * c_sb + h * c_sh;
     const BulkLoader<T> ld{k_cache + cb, v_cache + cb, c_st};
-    ok = attend_simt<T, G, kStages>(S, ntiles, 0, ld, scale_log2);
+    ok = attend_simt<T, G>(S, ntiles, 0, ld, scale_log2, o, o_sh);
   }
-  if (!ok) {
-    report(err, SD_KERR_TIMEOUT);
-    return;
-  }
-  combine_store(S, out + b * o_sb + static_cast<int64_t>(h * G) * o_sh, o_sh);
+  if (!ok) report(err, SD_KERR_TIMEOUT);
 }
 
 // ------------------------------------------------------------ fused layer
@@ -517,38 +518,29 @@ __device__ __forceinline__ float rope_elem(float x, float partner, int d, float 
   return round_to<T>(__fadd_rn(a, bq));
 }
 
-// Tail of the fused kernel's shared memory (identical layout in every CTA of
-// a cluster, so distributed-shared-memory addresses line up).
+// Tail of the fused kernel's shared memory.
 struct LayerTail {
-  float *f;       // [kD] forecast row (fp32)
-  float *pnew;    // [kD] updated running sum of the current block (rank 0)
-  float *sc;      // [seg] scores of this CTA's prototype slice
-  int *list;      // [max(NBcap, top_k+2)] selected blocks, ascending
-  int *tk;        // [top_k] merged top-k
-  int *cand_i;    // [top_k + 1] this CTA's candidates (+ the current block on rank 0)
-  float *cand_v;  // [top_k + 1]
-  int *all_i;     // [kCluster * (top_k + 1)] gathered candidates
-  float *all_v;   // [kCluster * (top_k + 1)]
-  float *cst;     // [G * (kD + 2)] this CTA's merged softmax state
-  static size_t bytes(int64_t NBcap, int top_k, int G) {
-    const int64_t seg = (NBcap + kCluster - 1) / kCluster;
+  float *f;     // [kD] forecast row (fp32)
+  float *pnew;  // [kD] updated running sum of the current block
+  float *sc;    // [NBcap] prototype scores
+  int *list;    // [max(NBcap, top_k + 2)] selected blocks, ascending
+  int *tk;      // [top_k] merged top-k
+  int *ci;      // [top_k + 1] candidate indices (precomputed ones + the current block)
+  float *cv;    // [top_k + 1] candidate scores
+  static size_t bytes(int64_t NBcap, int top_k) {
     const int64_t lst = NBcap > top_k + 2 ? NBcap : top_k + 2;
-    return sizeof(float) * (2 * kD + seg) + sizeof(int) * (lst + top_k) +
-           (sizeof(int) + sizeof(float)) * (top_k + 1) * (1 + kCluster) + sizeof(float) * G * (kD + 2);
+    return sizeof(float) * (2 * kD + NBcap) + sizeof(int) * (lst + top_k) +
+           (sizeof(int) + sizeof(float)) * (top_k + 1);
   }
   __device__ LayerTail(char *p, int64_t NBcap, int top_k) {
-    const int64_t seg = (NBcap + kCluster - 1) / kCluster;
     const int64_t lst = NBcap > top_k + 2 ? NBcap : top_k + 2;
     f = reinterpret_cast<float *>(p);
     pnew = f + kD;
     sc = pnew + kD;
-    list = reinterpret_cast<int *>(sc + seg);
+    list = reinterpret_cast<int *>(sc + NBcap);
     tk = list + lst;
-    cand_i = tk + top_k;
-    cand_v = reinterpret_cast<float *>(cand_i + top_k + 1);
-    all_i = reinterpret_cast<int *>(cand_v + top_k + 1);
-    all_v = reinterpret_cast<float *>(all_i + kCluster * (top_k + 1));
-    cst = all_v + kCluster * (top_k + 1);
+    ci = tk + top_k;
+    cv = reinterpret_cast<float *>(ci + top_k + 1);
   }
 };
 
@@ -560,19 +552,17 @@ __global__ void __launch_bounds__(kThreads)
                         int64_t Tcap, int64_t NBcap, int bs, int top_k, int rule, float sel_scale,
                         float scale_log2, const __grid_constant__ CUtensorMap tmk,
                         const __grid_constant__ CUtensorMap tmv, T *__restrict__ out, int64_t o_sb,
+                        const int32_t *__restrict__ cand_idx, const float *__restrict__ cand_val,
                         int32_t *sel_out, int32_t *cnt_out, int sel_cap, int32_t *err) {
   extern __shared__ __align__(1024) char smem_raw[];
-  AttnSmem<T, G, kClStages> S(smem_raw);
+  AttnSmem<T, G> S(smem_raw);
   LayerTail X(S.tail, NBcap, top_k);
-  cg::cluster_group cl = cg::this_cluster();
-  const int rank = static_cast<int>(cl.block_rank());
-  __shared__ int count, ntiles, pre;
-  const int bhx = blockIdx.x / kCluster;
-  const int b = bhx / Hkv, h = bhx - (bhx / Hkv) * Hkv;
+  __shared__ int count, ntiles, pre, patch_t, patch_row;
+  const int b = blockIdx.x / Hkv, h = blockIdx.x - (blockIdx.x / Hkv) * Hkv;
   const int Hq = Hkv * G;
   const int64_t pos = *cur_len;
-  if (pos < 0 || pos >= Tcap) {  // cache full (or corrupt length): the whole cluster writes nothing
-    if (rank == 0) report(err, SD_KERR_BOUNDS);
+  if (pos < 0 || pos >= Tcap) {  // cache full (or corrupt length): write nothing
+    report(err, SD_KERR_BOUNDS);
     return;
   }
   const int64_t L = pos + 1;
@@ -580,6 +570,7 @@ __global__ void __launch_bounds__(kThreads)
   const int nb = curr + 1;
   const int ms = nb < top_k + 2 ? nb : top_k + 2;
   const int kk = top_k < nb ? top_k : nb;
+  const bool use_f = fc != nullptr && nb > ms;  // a forecast-driven selection is needed
   const int64_t bh = static_cast<int64_t>(b) * Hkv + h;
   const T *kb = k_cache + bh * Tcap * kD;
   const T *vb = v_cache + bh * Tcap * kD;
@@ -592,43 +583,50 @@ __global__ void __launch_bounds__(kThreads)
       issue_tile(S, t, bulk);
     }
   };
-  // Global tile order: the current block, the sink block, then the others
-  // ascending; CTA r owns global tiles r, r+kCluster, ...  With block_size <=
-  // 64 the current block is global tile 0 (rank 0, which also writes the new
-  // token) and the sink is tile 1 (rank 1): both are known before selection.
-  const bool early = bs <= kRows;
+
+  // -- 0. stage every tile that is known now: the whole list on dense and
+  //       static-window steps, the sink and current blocks otherwise
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kClStages; ++s) mbar_init(&S.full[s], 1);
+    for (int s = 0; s < kStages; ++s) mbar_init(&S.full[s], 1);
     mbar_init_fence();
-    pre = 0;
-    if (early && rank == 1 && curr != 0) {
-      add_block_tiles(0, L, bs, S.tile_tok, S.tile_n, 0);
-      issue(0);
-      pre = 1;
+    int nt = 0;
+    if (!use_f) {
+      if (nb <= ms) {
+        for (int j = 0; j < nb; ++j) X.list[j] = j;
+        count = nb;
+      } else {
+        count = assemble_decode_list(false, nullptr, 0, nb, curr, top_k, X.list);
+      }
+      nt = build_tiles(X.list, count, L, bs, S.tile_tok, S.tile_n);
+    } else {
+      nt = add_block_tiles(0, L, bs, S.tile_tok, S.tile_n, 0);
+      nt = add_block_tiles(curr, L, bs, S.tile_tok, S.tile_n, nt);
     }
+    pre = nt < kStages ? nt : kStages;
+    for (int t = 0; t < pre; ++t) issue(t);
+    ntiles = nt;
   }
 
-  // -- 1. RoPE of q (every CTA); rank 0 appends the new token and updates the
-  //       current block's running sum
+  // -- 1. RoPE, append, compressor running sum
   const T *row = qkv + b * qkv_sb;
   const float *cr = rcos + pos * (kD / 2);
   const float *sr = rsin + pos * (kD / 2);
   if (threadIdx.x < kD) {
     const int d = threadIdx.x;
-    if (rank == 0) {
-      const T *kr = row + static_cast<int64_t>(Hq + h) * kD;
-      const float x = to_f(kr[d]);
-      const float pr = to_f(kr[d < kD / 2 ? d + kD / 2 : d - kD / 2]);
-      const float y = rope_elem<T>(x, pr, d, cr[d & (kD / 2 - 1)], sr[d & (kD / 2 - 1)]);
-      const int64_t off = (bh * Tcap + pos) * kD + d;
-      k_cache[off] = from_f<T>(y);
-      v_cache[off] = row[static_cast<int64_t>(Hq + Hkv + h) * kD + d];
-      float *ps = proto_sum + (bh * NBcap + curr) * kD + d;
-      const float pn = (pos % bs == 0 ? 0.f : *ps) + y;
-      *ps = pn;
-      X.pnew[d] = pn;
-      fence_proxy_async_global();
-    }
+    const T *kr = row + static_cast<int64_t>(Hq + h) * kD;
+    const float x = to_f(kr[d]);
+    const float pr = to_f(kr[d < kD / 2 ? d + kD / 2 : d - kD / 2]);
+    const float y = rope_elem<T>(x, pr, d, cr[d & (kD / 2 - 1)], sr[d & (kD / 2 - 1)]);
+    const T vv = row[static_cast<int64_t>(Hq + Hkv + h) * kD + d];
+    const int64_t off = (bh * Tcap + pos) * kD + d;
+    k_cache[off] = from_f<T>(y);
+    v_cache[off] = vv;
+    S.newkv[d] = from_f<T>(y);
+    S.newkv[kD + d] = vv;
+    float *ps = proto_sum + (bh * NBcap + curr) * kD + d;
+    const float pn = (pos % bs == 0 ? 0.f : *ps) + y;
+    *ps = pn;
+    X.pnew[d] = pn;
     if (fc != nullptr) X.f[d] = to_f(fc[b * f_sb + h * kD + d]);
   } else {
     for (int e = threadIdx.x - kD; e < G * kD; e += blockDim.x - kD) {
@@ -640,143 +638,69 @@ __global__ void __launch_bounds__(kThreads)
     }
   }
   __syncthreads();
-  if (threadIdx.x == 0 && early && rank == 0) {
-    add_block_tiles(curr, L, bs, S.tile_tok, S.tile_n, 0);
-    issue(0);
-    pre = 1;
-  }
 
-  // -- 2. selection: slice scoring + local top-k, exchange, merge
-  const bool use_f = fc != nullptr && nb > ms;
+  // -- 2. selection over this layer's prototypes (sum / bs)
   if (use_f) {
     const int n_scored = rule == SD_RULE_REFERENCE ? 1 : nb;
-    const int seg = (nb + kCluster - 1) / kCluster;
-    const int lo = rank * seg;
-    const int len = lo < nb ? (nb - lo < seg ? nb - lo : seg) : 0;
-    int nsc = n_scored - lo;
-    nsc = nsc < 0 ? 0 : (nsc > len ? len : nsc);
-    // the current block's row changes in this kernel; it is scored by rank 0
-    // from its own updated sum below, not through global memory
-    score_blocks(proto_sum + (bh * NBcap + lo) * kD, kD, kD, X.f, nsc, sel_scale, X.sc);
-    __syncthreads();
-    if (threadIdx.x < 32) {
-      auto val = [&](int i) {
-        return lo + i == curr ? __int_as_float(0x7fc00000) : (i < nsc ? X.sc[i] : -INFINITY);
-      };
-      const int kl = kk < len ? kk : len;
-      if (kl > 0) warp_topk(val, len, kl, X.cand_i, nullptr);
-      __syncwarp();
-      for (int r = threadIdx.x; r < top_k + 1; r += 32) {
-        const int li = r < kl ? X.cand_i[r] : -1;
-        if (li >= 0 && r < kk) {
-          X.cand_i[r] = lo + li;
-          X.cand_v[r] = val(li);
-        } else {  // never wins against a real candidate
-          X.cand_i[r] = 0x70000000 + rank * 128 + r;
-          X.cand_v[r] = -INFINITY;
+    if (cand_idx != nullptr) {
+      // precomputed top-k over every block but the current one (whose sum
+      // changed above) merged with the current block's score: the same top-k
+      // as scoring every block here
+      if (threadIdx.x < 32) {
+        const int lane = threadIdx.x;
+        float p = fmaf(X.f[lane], X.pnew[lane], 0.f);
+        p = fmaf(X.f[lane + 32], X.pnew[lane + 32], p);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) p += __shfl_xor_sync(0xffffffffu, p, o);
+        for (int r = lane; r < top_k; r += 32) {
+          const int j = cand_idx[bh * top_k + r];
+          const bool ok = j >= 0 && j < nb && j != curr;
+          X.ci[r] = ok ? j : 0x70000000 + r;
+          X.cv[r] = ok ? cand_val[bh * top_k + r] : -INFINITY;
         }
+        if (lane == 0) {
+          X.ci[top_k] = curr;
+          X.cv[top_k] = curr < n_scored ? p * sel_scale : -INFINITY;
+        }
+        __syncwarp();
+        warp_topk_kv([&](int c) { return X.cv[c]; }, [&](int c) { return X.ci[c]; }, top_k + 1, kk, X.tk);
       }
-      __syncwarp();
-      if (rank == 0 && threadIdx.x == 0) {  // the current block as the extra candidate
-        float acc = 0.f;
-        if (curr < n_scored)
-          for (int d = 0; d < kD; ++d) acc = fmaf(X.f[d], X.pnew[d], acc);
-        X.cand_i[top_k] = curr;
-        X.cand_v[top_k] = curr < n_scored ? acc * sel_scale : -INFINITY;
-      }
-    }
-  }
-  cl.sync();
-  if (use_f) {
-    const int per = top_k + 1;
-    for (int c = threadIdx.x; c < kCluster * per; c += blockDim.x) {
-      const int r = c / per, i = c - r * per;
-      const int *ri = cl.map_shared_rank(X.cand_i, r);
-      const float *rv = cl.map_shared_rank(X.cand_v, r);
-      X.all_i[c] = ri[i];
-      X.all_v[c] = rv[i];
-    }
-    __syncthreads();
-    if (threadIdx.x < 32)
-      warp_topk_kv([&](int c) { return X.all_v[c]; }, [&](int c) { return X.all_i[c]; }, kCluster * per, kk, X.tk);
-    __syncthreads();
-  }
-  if (threadIdx.x == 0) {
-    if (nb <= ms) {  // dense fallback: every block
-      for (int j = 0; j < nb; ++j) X.list[j] = j;
-      count = nb;
+      __syncthreads();
     } else {
-      count = assemble_decode_list(use_f, X.tk, kk, nb, curr, top_k, X.list);
+      score_blocks(proto_sum + bh * NBcap * kD, kD, kD, X.f, n_scored, sel_scale, X.sc);
+      __syncthreads();
+      cta_topk([&](int j) { return j < n_scored ? X.sc[j] : -INFINITY; }, nb, kk, X.tk);
     }
+    if (threadIdx.x == 0) {
+      count = assemble_decode_list(true, X.tk, kk, nb, curr, top_k, X.list);
+      ntiles = build_tiles(X.list, count, L, bs, S.tile_tok, S.tile_n, ntiles, 0, curr);
+    }
+  }
+  if (threadIdx.x == 0) {  // the tile holding the new token gets its rows patched
+    patch_t = -1;
+    for (int t = 0; t < ntiles; ++t)
+      if (S.tile_tok[t] <= pos && pos < S.tile_tok[t] + S.tile_n[t]) {
+        patch_t = t;
+        patch_row = static_cast<int>(pos - S.tile_tok[t]);
+      }
   }
   __syncthreads();
-  if (sel_out && rank == 0) {
+  if (sel_out) {
     for (int i = threadIdx.x; i < sel_cap; i += blockDim.x) sel_out[bh * sel_cap + i] = i < count ? X.list[i] : -1;
     if (threadIdx.x == 0) cnt_out[bh] = count;
   }
-  // this CTA's tiles, in the global order above
-  if (threadIdx.x == 0) {
-    int g = 0, nt = 0;
-    auto take = [&](int j) {
-      int64_t n = L - static_cast<int64_t>(j) * bs;
-      if (j < 0 || n <= 0) return;
-      if (n > bs) n = bs;
-      for (int64_t r0 = 0; r0 < n; r0 += kRows) {
-        if (g % kCluster == rank && nt < kMaxTiles) {
-          S.tile_tok[nt] = static_cast<int>(static_cast<int64_t>(j) * bs + r0);
-          S.tile_n[nt] = static_cast<int>(n - r0 < kRows ? n - r0 : kRows);
-          ++nt;
-        }
-        ++g;
-      }
-    };
-    take(curr);
-    if (curr != 0) take(0);
-    for (int i = 0; i < count; ++i)
-      if (X.list[i] != 0 && X.list[i] != curr) take(X.list[i]);
-    ntiles = nt;
-  }
-  __syncthreads();
 
-  // -- 3. attention over this CTA's tiles, then the cluster-wide merge
+  // -- 3. attention over the selected blocks
+  T *o = out + b * o_sb + static_cast<int64_t>(h * G) * kD;
   bool ok;
   if constexpr (is16<T>()) {
-    ok = attend_mma<T, G, kClStages>(S, ntiles, pre, tma, scale_log2);
+    ok = attend_mma<T, G>(S, ntiles, pre, tma, scale_log2, o, kD, patch_t, patch_row);
   } else {
-    ok = attend_simt<T, G, kClStages>(S, ntiles, pre, bulk, scale_log2);
+    ok = attend_simt<T, G>(S, ntiles, pre, bulk, scale_log2, o, kD, patch_t, patch_row);
   }
   if (!ok) report(err, SD_KERR_TIMEOUT);
-  merge_warps(S, X.cst);
-  cl.sync();
-  if (rank == 0) {
-    T *o = out + b * o_sb + static_cast<int64_t>(h * G) * kD;
-    for (int e = threadIdx.x; e < G * kD; e += blockDim.x) {
-      const int g = e / kD, d = e - g * kD;
-      float mr[kCluster];
-      float M = -INFINITY;
-#pragma unroll
-      for (int r = 0; r < kCluster; ++r) {
-        mr[r] = cl.map_shared_rank(X.cst, r)[g * (kD + 2)];
-        M = fmaxf(M, mr[r]);
-      }
-      float den = 0.f, num = 0.f;
-      if (M != -INFINITY) {
-#pragma unroll
-        for (int r = 0; r < kCluster; ++r) {
-          if (mr[r] == -INFINITY) continue;
-          const float *st = cl.map_shared_rank(X.cst, r) + g * (kD + 2);
-          const float f = exp2f(mr[r] - M);
-          den = fmaf(st[1], f, den);
-          num = fmaf(st[2 + d], f, num);
-        }
-      }
-      o[e] = from_f<T>(den > 0.f ? num / den : 0.f);
-    }
-  }
-  cl.sync();  // keep every CTA's shared memory alive until rank 0 has read it
 }
 
-// Tensor maps for a [B][H][T][64] 16-bit cache pair; zeroed maps for fp32.
 template <typename T>
 int make_maps(CUtensorMap *mk, CUtensorMap *mv, const void *kc, const void *vc, int64_t B, int64_t H, int64_t T_,
               int64_t st, int64_t sh, int64_t sb) {
@@ -797,7 +721,7 @@ int launch_decode_attention(const void *q, int64_t B, int64_t Hkv, int64_t q_sb,
                             const void *vc, int64_t c_sb, int64_t c_sh, int64_t c_st, int64_t Tcap,
                             const int32_t *sel, const int32_t *cnt, int ms_cap, int64_t L, int bs, float scale,
                             void *out, int64_t o_sb, int64_t o_sh, int32_t *err, cudaStream_t s) {
-  const size_t smem = AttnSmem<T, G, kStages>::bytes() + sizeof(int) * ms_cap + kAlignSlack;
+  const size_t smem = AttnSmem<T, G>::bytes() + sizeof(int) * ms_cap + kAlignSlack;
   // the tensor-core path needs contiguous rows laid out [B][H][T] in memory order
   const bool tma = is16<T>() && c_st == kD && c_sh >= Tcap * kD && c_sb >= Hkv * c_sh;
   CUtensorMap mk, mv;
@@ -816,11 +740,13 @@ int launch_decode_attention(const void *q, int64_t B, int64_t Hkv, int64_t q_sb,
       return check_launch();
     }
   }
-  auto kern = decode_attention_kernel<T, G, false>;
-  if (set_max_smem(kern, smem) != SD_OK) return SD_ERR_CUDA;
-  kern<<<grid, kThreads, smem, s>>>(static_cast<const T *>(q), (int)Hkv, q_sb, q_sh, static_cast<const T *>(kc),
-                                    static_cast<const T *>(vc), c_sb, c_sh, c_st, mk, mv, sel, cnt, ms_cap, L, bs,
-                                    scale * kLog2e, static_cast<T *>(out), o_sb, o_sh, err);
+  {
+    auto kern = decode_attention_kernel<T, G, false>;
+    if (set_max_smem(kern, smem) != SD_OK) return SD_ERR_CUDA;
+    kern<<<grid, kThreads, smem, s>>>(static_cast<const T *>(q), (int)Hkv, q_sb, q_sh, static_cast<const T *>(kc),
+                                      static_cast<const T *>(vc), c_sb, c_sh, c_st, mk, mv, sel, cnt, ms_cap, L, bs,
+                                      scale * kLog2e, static_cast<T *>(out), o_sb, o_sh, err);
+  }
   return check_launch();
 }
 
@@ -828,36 +754,19 @@ template <typename T, typename F, int G>
 int launch_decode_layer(const void *qkv, int64_t qkv_sb, const void *fc, int64_t f_sb, const float *rc,
                         const float *rs, const int32_t *cur_len, void *kc, void *vc, float *ps, int64_t B,
                         int64_t Hkv, int64_t Tcap, int64_t NBcap, int bs, int top_k, int rule, float scale,
-                        void *out, int64_t o_sb, int32_t *sel_out, int32_t *cnt_out, int sel_cap, int32_t *err,
-                        cudaStream_t s) {
-  const size_t smem = AttnSmem<T, G, kClStages>::bytes() + LayerTail::bytes(NBcap, top_k, G) + kAlignSlack;
+                        void *out, int64_t o_sb, const int32_t *cand_idx, const float *cand_val,
+                        int32_t *sel_out, int32_t *cnt_out, int sel_cap, int32_t *err, cudaStream_t s) {
+  const size_t smem = AttnSmem<T, G>::bytes() + LayerTail::bytes(NBcap, top_k) + kAlignSlack;
   CUtensorMap mk, mv;
   const int r = make_maps<T>(&mk, &mv, kc, vc, B, Hkv, Tcap, kD, Tcap * kD, Hkv * Tcap * kD);
   if (r != SD_OK) return r;
   auto kern = decode_layer_kernel<T, F, G>;
   if (set_max_smem(kern, smem) != SD_OK) return SD_ERR_CUDA;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(B * Hkv * kCluster));
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = kCluster;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(
-      &cfg, kern, static_cast<const T *>(qkv), qkv_sb, static_cast<const F *>(fc), f_sb, rc, rs, cur_len,
+  kern<<<static_cast<unsigned>(B * Hkv), kThreads, smem, s>>>(
+      static_cast<const T *>(qkv), qkv_sb, static_cast<const F *>(fc), f_sb, rc, rs, cur_len,
       static_cast<T *>(kc), static_cast<T *>(vc), ps, (int)Hkv, Tcap, NBcap, bs, top_k, rule,
-      scale / static_cast<float>(bs), scale * kLog2e, mk, mv, static_cast<T *>(out), o_sb, sel_out, cnt_out,
-      sel_cap, err);
-  if (e != cudaSuccess) {
-    set_cuda_error(e);
-    cudaGetLastError();
-    return SD_ERR_CUDA;
-  }
+      scale / static_cast<float>(bs), scale * kLog2e, mk, mv, static_cast<T *>(out), o_sb, cand_idx, cand_val,
+      sel_out, cnt_out, sel_cap, err);
   return check_launch();
 }
 
@@ -904,8 +813,9 @@ extern "C" int sd_decode_layer(const void *qkv, int dtype, int64_t qkv_sb, const
                                int64_t f_sb, const float *rope_cos, const float *rope_sin, int64_t max_pos,
                                const int32_t *cur_len, void *k_cache, void *v_cache, float *proto_sum, int64_t B,
                                int64_t Hq, int64_t Hkv, int64_t D, int64_t Tcap, int64_t NBcap, int block_size,
-                               int top_k, int rule, float scale, void *out, int64_t o_sb, int32_t *sel_out,
-                               int32_t *cnt_out, int sel_cap, int32_t *err, void *stream) {
+                               int top_k, int rule, float scale, void *out, int64_t o_sb, const int32_t *cand_idx,
+                               const float *cand_val, int32_t *sel_out, int32_t *cnt_out, int sel_cap,
+                               int32_t *err, void *stream) {
   if (!qkv || !rope_cos || !rope_sin || !cur_len || !k_cache || !v_cache || !proto_sum || !out)
     return SD_ERR_INVALID;
   if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || block_size <= 0 || top_k <= 0 || Tcap <= 0 || NBcap <= 0 ||
@@ -914,7 +824,8 @@ extern "C" int sd_decode_layer(const void *qkv, int dtype, int64_t qkv_sb, const
   if (rule != SD_RULE_REFERENCE && rule != SD_RULE_ABSOLUTE) return SD_ERR_INVALID;
   if (NBcap * block_size < Tcap) return SD_ERR_INVALID;
   if ((sel_out == nullptr) != (cnt_out == nullptr) || (sel_out && sel_cap < top_k + 2)) return SD_ERR_INVALID;
-  if (D != sd::kD || top_k > 64 || NBcap > 16384 || B * Hkv > 0x7fffffff / sd::kCluster) return SD_ERR_UNSUPPORTED;
+  if ((cand_idx == nullptr) != (cand_val == nullptr)) return SD_ERR_INVALID;
+  if (D != sd::kD || top_k > 64 || NBcap > 16384 || B * Hkv > 0x7fffffff) return SD_ERR_UNSUPPORTED;
   if (static_cast<int64_t>(top_k + 2) * ((block_size + sd::kRows - 1) / sd::kRows) > sd::kMaxTiles)
     return SD_ERR_UNSUPPORTED;
   if (!sd::aligned16(k_cache) || !sd::aligned16(v_cache) || !sd::aligned16(proto_sum)) return SD_ERR_ALIGN;
@@ -926,12 +837,13 @@ extern "C" int sd_decode_layer(const void *qkv, int dtype, int64_t qkv_sb, const
       SD_DISPATCH_G(G, return sd::launch_decode_layer<E, E, GG>(qkv, qkv_sb, forecast, f_sb, rope_cos, rope_sin,
                                                                 cur_len, k_cache, v_cache, proto_sum, B, Hkv,
                                                                 Tcap, NBcap, block_size, top_k, rule, scale, out,
-                                                                o_sb, sel_out, cnt_out, sel_cap, err, s));
+                                                                o_sb, cand_idx, cand_val, sel_out, cnt_out,
+                                                                sel_cap, err, s));
     } else if (fdt == SD_DTYPE_F32) {
       SD_DISPATCH_G(G, return sd::launch_decode_layer<E, float, GG>(
                            qkv, qkv_sb, forecast, f_sb, rope_cos, rope_sin, cur_len, k_cache, v_cache, proto_sum,
-                           B, Hkv, Tcap, NBcap, block_size, top_k, rule, scale, out, o_sb, sel_out, cnt_out,
-                           sel_cap, err, s));
+                           B, Hkv, Tcap, NBcap, block_size, top_k, rule, scale, out, o_sb, cand_idx, cand_val,
+                           sel_out, cnt_out, sel_cap, err, s));
     } else {
       return SD_ERR_UNSUPPORTED;
     }

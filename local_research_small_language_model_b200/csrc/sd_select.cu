@@ -208,3 +208,72 @@ extern "C" int sd_decode_select(const void *forecast, int f_dtype, int64_t f_sb,
   });
   return sd::check_launch();
 }
+
+namespace sd {
+
+// One CTA per (b, h): top-k of every cached block except the one the next
+// token lands in, from the running sums (sum / bs), for the next decode step.
+template <typename F>
+__global__ void decode_candidates_kernel(const F *__restrict__ fc, int64_t f_sb, const float *proto_sum, int H,
+                                         int64_t NBcap, const int32_t *__restrict__ cur_len, int bs, int k,
+                                         int rule, float sel_scale, int32_t *__restrict__ cand_idx,
+                                         float *__restrict__ cand_val) {
+  extern __shared__ float smem[];
+  constexpr int D = 64;
+  const int bh = blockIdx.x;
+  const int b = bh / H, h = bh - (bh / H) * H;
+  const int64_t pos = *cur_len;
+  float *f_s = smem;      // [D]
+  float *sc = f_s + D;    // [NBcap]
+  __shared__ int tk[64];
+  int32_t *oi = cand_idx + static_cast<int64_t>(bh) * k;
+  float *ov = cand_val + static_cast<int64_t>(bh) * k;
+  const int64_t nb64 = pos / bs + 1;
+  const int ms = nb64 < k + 2 ? static_cast<int>(nb64) : k + 2;
+  if (pos < 0 || nb64 > NBcap || nb64 <= ms) {  // dense step (or nothing cached): no candidates needed
+    for (int r = threadIdx.x; r < k; r += blockDim.x) {
+      oi[r] = -1;
+      ov[r] = -INFINITY;
+    }
+    return;
+  }
+  const int nb = static_cast<int>(nb64), curr = nb - 1;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) f_s[d] = to_f(fc[b * f_sb + h * D + d]);
+  __syncthreads();
+  const int n_scored = rule == SD_RULE_REFERENCE ? 1 : curr;  // the current block is left out
+  const int nsc = n_scored < curr ? n_scored : curr;
+  score_blocks(proto_sum + static_cast<int64_t>(bh) * NBcap * D, D, D, f_s, nsc, sel_scale, sc);
+  __syncthreads();
+  auto val = [&](int j) { return j == curr ? __int_as_float(0x7fc00000) : (j < nsc ? sc[j] : -INFINITY); };
+  cta_topk(val, nb, k, tk);
+  for (int r = threadIdx.x; r < k; r += blockDim.x) {
+    const int j = tk[r];
+    oi[r] = j;
+    ov[r] = j >= 0 ? val(j) : -INFINITY;
+  }
+}
+
+}  // namespace sd
+
+extern "C" int sd_decode_candidates(const void *forecast, int f_dtype, int64_t f_sb, const float *proto_sum,
+                                    int64_t B, int64_t Hkv, int64_t D, int64_t NBcap, const int32_t *cur_len,
+                                    int block_size, int top_k, int rule, float scale, int32_t *cand_idx,
+                                    float *cand_val, void *stream) {
+  if (!forecast || !proto_sum || !cur_len || !cand_idx || !cand_val || B <= 0 || Hkv <= 0 || NBcap <= 0 ||
+      block_size <= 0 || top_k <= 0)
+    return SD_ERR_INVALID;
+  if (rule != SD_RULE_REFERENCE && rule != SD_RULE_ABSOLUTE) return SD_ERR_INVALID;
+  if (D != 64 || top_k > 64 || NBcap > 32768 || B * Hkv > 0x7fffffff) return SD_ERR_UNSUPPORTED;
+  if (!sd::aligned16(proto_sum)) return SD_ERR_ALIGN;
+  const size_t smem = sizeof(float) * (D + NBcap);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const float sel_scale = scale / static_cast<float>(block_size);
+  SD_DISPATCH_DTYPE(f_dtype, E, {
+    auto kern = sd::decode_candidates_kernel<E>;
+    if (sd::set_max_smem(kern, smem) != SD_OK) return SD_ERR_CUDA;
+    kern<<<static_cast<unsigned>(B * Hkv), 128, smem, s>>>(static_cast<const E *>(forecast), f_sb, proto_sum,
+                                                           (int)Hkv, NBcap, cur_len, block_size, top_k, rule,
+                                                           sel_scale, cand_idx, cand_val);
+  });
+  return sd::check_launch();
+}

@@ -96,6 +96,43 @@ __device__ __forceinline__ int assemble_decode_list(bool use_forecast, const int
   return n;
 }
 
+// Top-kk of n entries by the shared total order (value desc, index asc),
+// written to out_idx; val(j) may return NaN for entries that must not be
+// chosen.  Every warp takes the top-kk of a contiguous slice, then warp 0
+// merges the slices' candidates.  All threads call this; it ends with a
+// barrier.
+template <typename Val>
+__device__ __forceinline__ void cta_topk(Val val, int n, int kk, int *out_idx) {
+  __shared__ int cand_i[256];
+  __shared__ float cand_v[256];
+  const int nw = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (nw * kk <= 256 && n >= 4 * 32) {
+    const int seg = (n + nw - 1) / nw;
+    const int lo = warp * seg, len = lo < n ? (n - lo < seg ? n - lo : seg) : 0;
+    int *ci = cand_i + warp * kk;
+    if (len >= kk) {
+      warp_topk([&](int j) { return val(lo + j); }, len, kk, ci, nullptr);
+      __syncwarp();
+    }
+    for (int r = lane; r < kk; r += 32) {
+      const int li = len >= kk ? ci[r] : (r < len ? r : -1);
+      if (li >= 0) {
+        ci[r] = lo + li;
+        cand_v[warp * kk + r] = val(lo + li);
+      } else {  // exhausted slice: an entry that never wins
+        ci[r] = 0x70000000 + warp * 64 + r;
+        cand_v[warp * kk + r] = -INFINITY;
+      }
+    }
+    __syncthreads();
+    if (warp == 0)
+      warp_topk_kv([&](int c) { return cand_v[c]; }, [&](int c) { return cand_i[c]; }, nw * kk, kk, out_idx);
+  } else if (threadIdx.x < 32) {
+    warp_topk(val, n, kk, out_idx, nullptr);
+  }
+  __syncthreads();
+}
+
 // Builds the ascending selected-block list into list[0..*count).  `scores`
 // holds the scores of blocks 0..n_scored-1; blocks n_scored..nb-1 count as -inf.
 // topk_tmp needs room for top_k ints.  Must be called by all threads.
@@ -109,38 +146,7 @@ __device__ __forceinline__ void build_decode_list(bool use_forecast, const float
     return;
   }
   const int kk = top_k < nb ? top_k : nb;
-  if (use_forecast) {
-    // every warp takes the top-kk of a contiguous slice of blocks, then warp 0
-    // merges the slices' candidates under the same total order
-    __shared__ int cand_i[256];
-    __shared__ float cand_v[256];
-    const int nw = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    auto score = [&](int j) { return j < n_scored ? scores[j] : -INFINITY; };
-    if (nw * kk <= 256 && nb >= 4 * 32) {
-      const int seg = (nb + nw - 1) / nw;
-      const int lo = warp * seg, len = lo < nb ? (nb - lo < seg ? nb - lo : seg) : 0;
-      int *ci = cand_i + warp * kk;
-      if (len >= kk) {
-        warp_topk([&](int j) { return score(lo + j); }, len, kk, ci, nullptr);
-        __syncwarp();
-        for (int r = lane; r < kk; r += 32) {
-          ci[r] += lo;
-          cand_v[warp * kk + r] = score(ci[r]);
-        }
-      } else {  // short slice: take it whole, pad with entries that never win
-        for (int r = lane; r < kk; r += 32) {
-          ci[r] = r < len ? lo + r : 0x70000000 + warp * 64 + r;
-          cand_v[warp * kk + r] = r < len ? score(lo + r) : -INFINITY;
-        }
-      }
-      __syncthreads();
-      if (warp == 0)
-        warp_topk_kv([&](int c) { return cand_v[c]; }, [&](int c) { return cand_i[c]; }, nw * kk, kk, topk_tmp);
-    } else if (threadIdx.x < 32) {
-      warp_topk(score, nb, kk, topk_tmp, nullptr);
-    }
-  }
-  __syncthreads();
+  if (use_forecast) cta_topk([&](int j) { return j < n_scored ? scores[j] : -INFINITY; }, nb, kk, topk_tmp);
   if (threadIdx.x == 0) *count = assemble_decode_list(use_forecast, topk_tmp, kk, nb, curr, top_k, list);
   __syncthreads();
 }

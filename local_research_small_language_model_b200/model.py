@@ -130,13 +130,41 @@ class TransformerBlock(nn.Module):
                 rotary_emb._extend_cache(kv_cache.tcap, x.device)
             f = prev_layer_forecast if (a.mode == "forecast" and prev_layer_forecast is not None) else None
             probe = self.probe
+            # the next layer's forecast candidates only need this layer's forecast
+            # and the next layer's (unchanged until its own step) running sums:
+            # compute them on the side stream while this layer's attention and
+            # FFN run on the main stream
+            side = getattr(self, "side_stream", None)
+            if side is not None and next_layer_block is not None and isinstance(next_kv_cache, B200KVCache) \
+                    and next_layer_block.attention.mode == "forecast":
+                na = next_layer_block.attention
+                nc = next_kv_cache
+                if getattr(nc, "cand", None) is None:
+                    nc.cand = (torch.empty(b, na.n_kv_head, na.top_k_blocks, dtype=torch.int32, device=x.device),
+                               torch.empty(b, na.n_kv_head, na.top_k_blocks, dtype=torch.float32, device=x.device))
+                    nc.cand_event = torch.cuda.Event()
+                side.wait_stream(torch.cuda.current_stream())
+                with torch.cuda.stream(side):
+                    if probe is not None and "cstart" in probe:
+                        probe["cstart"].record(side)
+                    ops.decode_candidates(current_forecast, nc.proto_sum, nc.len_dev, na.n_kv_head, na.block_size,
+                                          na.top_k_blocks, na.rule, out=nc.cand)
+                    if probe is not None and "cend" in probe:
+                        probe["cend"].record(side)
+                    nc.cand_event.record(side)
+                nc.cand_ready = True
+            cand = None
+            if getattr(kv_cache, "cand_ready", False):
+                torch.cuda.current_stream().wait_event(kv_cache.cand_event)  # join the side stream
+                cand = kv_cache.cand if f is not None else None
+            kv_cache.cand_ready = False
             if probe is not None:
                 probe["start"].record()
             out = ops.decode_layer(proj[:, :nq], f, rotary_emb.cos, rotary_emb.sin, kv_cache.len_dev,
                                    kv_cache.k_store, kv_cache.v_store, kv_cache.proto_sum, a.n_head, a.n_kv_head,
                                    a.block_size, a.top_k_blocks, a.rule,
                                    sel_out=probe["sel"] if probe is not None else None,
-                                   cnt_out=probe["cnt"] if probe is not None else None)
+                                   cnt_out=probe["cnt"] if probe is not None else None, cand=cand)
             if probe is not None:
                 probe["end"].record()
             kv_cache.advance(1, device=not getattr(kv_cache, "shared_len", False))
@@ -176,9 +204,11 @@ class SparDAB200Model(nn.Module):
             nn.init.normal_(module.weight, mean=0.0, std=self.config.initializer_range)
 
     def allocate_caches(self, batch: int, max_seq_len: int, dtype: Optional[torch.dtype] = None,
-                        device=None) -> List[B200KVCache]:
+                        device=None, overlap_selection: bool = True) -> List[B200KVCache]:
         """One B200KVCache per layer, sharing one device length array so a
-        decode step bumps all lengths with a single launch."""
+        decode step bumps all lengths with a single launch.  With
+        ``overlap_selection`` each decode step scores layer L+1's prototypes on
+        a side stream while layer L's attention and FFN run."""
         cfg = self.config
         device = device or self.embeddings.weight.device
         dtype = dtype or self.embeddings.weight.dtype
@@ -190,6 +220,10 @@ class SparDAB200Model(nn.Module):
             c.shared_len = True
             caches.append(c)
         self.rotary_emb._extend_cache(caches[0].tcap, device)
+        if overlap_selection and torch.device(device).type == "cuda":
+            side = torch.cuda.Stream(device=device)
+            for layer in self.layers:
+                layer.side_stream = side
         return caches
 
     def forward(self, input_ids: torch.Tensor, targets: Optional[torch.Tensor] = None,

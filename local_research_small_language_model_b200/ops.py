@@ -205,12 +205,15 @@ def decode_layer(qkv: torch.Tensor, forecast: Optional[torch.Tensor], rope_cos: 
                  proto_sum: torch.Tensor, n_head: int, n_kv_head: int, block_size: int, top_k: int,
                  rule: str = "reference", scale: Optional[float] = None,
                  out: Optional[torch.Tensor] = None, sel_out: Optional[torch.Tensor] = None,
-                 cnt_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+                 cnt_out: Optional[torch.Tensor] = None,
+                 cand: Optional[Tuple[torch.Tensor, torch.Tensor]] = None) -> torch.Tensor:
     """Fused decode layer: RoPE + append + compressor update + selection +
     attention (model/attention/sparse.py:366-410 + :99-183 for T == 1).
     qkv [B,(Hq+2Hkv)*D] (pre-RoPE projections), forecast [B,Hkv,D] or None.
     sel_out [B,Hkv,cap] / cnt_out [B,Hkv] int32 (optional) receive each
-    (sequence, kv head)'s selected block list.  Returns [B,Hq*D]."""
+    (sequence, kv head)'s selected block list.  cand (optional) is the
+    (cand_idx, cand_val) pair decode_candidates produced for this step.
+    Returns [B,Hq*D]."""
     _cuda(qkv, forecast, rope_cos, rope_sin, cur_len, k_store, v_store, proto_sum)
     b = qkv.shape[0]
     d = k_store.shape[-1]
@@ -228,10 +231,34 @@ def decode_layer(qkv: torch.Tensor, forecast: Optional[torch.Tensor], rope_cos: 
            rope_sin.data_ptr(), rope_cos.shape[0], cur_len.data_ptr(), k_store.data_ptr(), v_store.data_ptr(),
            proto_sum.data_ptr(), b, n_head, n_kv_head, d, k_store.shape[2], proto_sum.shape[2], block_size, top_k,
            RULES[rule], sc, out.data_ptr(), out.stride(0),
+           cand[0].data_ptr() if cand is not None else None,
+           cand[1].data_ptr() if cand is not None else None,
            sel_out.data_ptr() if sel_out is not None else None,
            cnt_out.data_ptr() if cnt_out is not None else None,
            sel_out.shape[-1] if sel_out is not None else 0,
            error_buffer(qkv.device).data_ptr(), _stream(qkv))
+    return out
+
+
+def decode_candidates(forecast: torch.Tensor, proto_sum: torch.Tensor, cur_len: torch.Tensor, n_kv_head: int,
+                      block_size: int, top_k: int, rule: str = "reference",
+                      out: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
+                      scale: Optional[float] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Top-k candidate blocks for a layer's next decode step, over every cached
+    block but the current one (sd_decode_candidates).  forecast [B,Hkv,D] (or
+    [B,1,Hkv,D]) rows; proto_sum [B,Hkv,NBcap,D]; cur_len device int32.
+    Returns (cand_idx int32, cand_val fp32) [B,Hkv,top_k]."""
+    _cuda(forecast, proto_sum, cur_len)
+    b = forecast.shape[0]
+    d = proto_sum.shape[-1]
+    f = _inner1(forecast.reshape(b, n_kv_head * d))
+    if out is None:
+        out = (torch.empty(b, n_kv_head, top_k, dtype=torch.int32, device=forecast.device),
+               torch.empty(b, n_kv_head, top_k, dtype=torch.float32, device=forecast.device))
+    sc = 1.0 / math.sqrt(d) if scale is None else scale
+    L.call("sd_decode_candidates", f.data_ptr(), dtype_code(f), f.stride(0), proto_sum.data_ptr(), b, n_kv_head, d,
+           proto_sum.shape[2], cur_len.data_ptr(), block_size, top_k, RULES[rule], sc, out[0].data_ptr(),
+           out[1].data_ptr(), _stream(forecast))
     return out
 
 

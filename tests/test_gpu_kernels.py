@@ -331,3 +331,43 @@ def test_silu_mul_matches_reference_formula(dev, dt):
     ref = torch.nn.functional.silu(gu[:, :2048]) * gu[:, 2048:]
     torch.testing.assert_close(ops.silu_mul(gu).float(), ref.float(), rtol=1e-5 if dt == torch.float32 else 8e-3,
                                atol=1e-6 if dt == torch.float32 else 8e-3)
+
+
+# ------------------------------------------------------------------ fused-kernel selection
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("rule", ["reference", "absolute"])
+@pytest.mark.parametrize("start", [700, 1023, 1087, 1600])
+def test_decode_layer_selection_and_candidates(dev, dt, rule, start):
+    """The fused kernel's own selected lists equal the oracle's, and merging
+    precomputed candidates (sd_decode_candidates) gives the same lists and the
+    same output bits as scoring inside the kernel."""
+    b, hq, hkv = 3, 12, 4
+    caches = [sd.B200KVCache(b, 2048, hkv, 64, dev, dt) for _ in range(2)]
+    k0, v0 = t(normal((b, start, hkv, 64), seed=171), dev, dt), t(normal((b, start, hkv, 64), seed=172), dev, dt)
+    for c in caches:
+        c.update(k0, v0)
+    cos, sin = precompute_rope_freqs(64, 2048)
+    cos_d, sin_d = cos.to(dev), sin.to(dev)
+    for step in range(3):
+        pos = caches[0].current_len
+        qkv = t(normal((b, (hq + 2 * hkv) * 64), seed=180 + step), dev, dt)
+        f = t(normal((b, hkv, 64), seed=190 + step), dev, dt)
+        sels, outs = [], []
+        for i, c in enumerate(caches):
+            sel = torch.full((b, hkv, 10), -1, dtype=torch.int32, device=dev)
+            cnt = torch.zeros(b, hkv, dtype=torch.int32, device=dev)
+            cand = ops.decode_candidates(f, c.proto_sum, c.len_dev, hkv, 64, 8, rule) if i == 1 else None
+            outs.append(ops.decode_layer(qkv, f, cos_d, sin_d, c.len_dev, c.k_store, c.v_store, c.proto_sum, hq, hkv,
+                                         64, 8, rule, sel_out=sel, cnt_out=cnt, cand=cand))
+            c.advance(1)
+            sels.append((n(sel).astype(np.int64), n(cnt).astype(np.int64)))
+        _no_device_errors(dev)
+        assert np.array_equal(sels[0][0], sels[1][0]) and np.array_equal(sels[0][1], sels[1][1])
+        assert torch.equal(outs[0], outs[1])
+        kd = n(caches[0].k_store)
+        L = pos + 1
+        reps = O.compress_blocks(kd[:, :, :L].transpose(0, 2, 1, 3), 64)
+        rs, rc = O.decode_select(n(f)[:, None], reps, L, 64, 8, b, hkv, "forecast", rule)
+        assert np.array_equal(sels[0][1], rc)
+        for ix in np.ndindex(b, hkv):
+            assert list(sels[0][0][ix][:rc[ix]]) == list(rs[ix][:rc[ix]]), (step, ix)

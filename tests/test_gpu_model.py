@@ -105,3 +105,28 @@ def test_decode_engine_graph_matches_eager(dev):
         cur = nxt
     assert all(c.current_len == pre + 6 for c in c2)
     assert torch.equal(m1._lens, m2._lens)
+
+
+@pytest.mark.parametrize("rule", ["reference", "absolute"])
+@torch.no_grad()
+def test_overlapped_selection_matches_in_kernel_selection(dev, rule):
+    """Decode with layer L+1's candidates computed on the side stream during
+    layer L gives bit-identical logits to decode with selection in the kernel."""
+    m1, sc = _model(dev, torch.bfloat16, rule=rule)
+    m2, _ = _model(dev, torch.bfloat16, rule=rule)
+    b, pre = 3, 1500
+    c1 = m1.allocate_caches(b, 2048, overlap_selection=False)
+    c2 = m2.allocate_caches(b, 2048, overlap_selection=True)
+    gen = torch.Generator(device="cpu").manual_seed(2)
+    for ca, cb in zip(c1, c2):
+        k = torch.randn(b, pre, 4, 64, generator=gen).to(dev, torch.bfloat16)
+        v = torch.randn(b, pre, 4, 64, generator=gen).to(dev, torch.bfloat16)
+        ca.update(k, v)
+        cb.update(k, v)
+    ids = torch.randint(0, sc.vocab_size, (b, 1), generator=gen).to(dev)
+    for step in range(5):
+        l1 = m1(ids, kv_caches=c1)["logits"]
+        l2 = m2(ids, kv_caches=c2)["logits"]
+        assert torch.equal(l1, l2), f"step {step}"
+        ids = l1[:, -1:].argmax(-1)
+    sd.ops.check_device_errors(dev)
