@@ -129,7 +129,8 @@ __device__ __forceinline__ void warp_topk(Get get, int n, int k, int *out_idx, f
     int bi = 0x7fffffff;
     for (int j = lane; j < n; j += 32) {
       const float v = get(j);
-      const bool elig = first || (v < pv) || (v == pv && j > pi);
+      // NaN marks an entry that must never be chosen, in any round
+      const bool elig = (v == v) && (first || (v < pv) || (v == pv && j > pi));
       if (elig && (bi == 0x7fffffff || better(v, j, bv, bi))) {
         bv = v;
         bi = j;
@@ -169,7 +170,8 @@ __device__ __forceinline__ void warp_topk_kv(Val val, Idx idx, int n, int k, int
     for (int c = lane; c < n; c += 32) {
       const float v = val(c);
       const int j = idx(c);
-      const bool elig = first || (v < pv) || (v == pv && j > pi);
+      // NaN marks an entry that must never be chosen, in any round
+      const bool elig = (v == v) && (first || (v < pv) || (v == pv && j > pi));
       if (elig && (bi == 0x7fffffff || better(v, j, bv, bi))) {
         bv = v;
         bi = j;
