@@ -586,25 +586,60 @@ __global__ void __launch_bounds__(kThreads)
 
   // -- 0. stage every tile that is known now: the whole list on dense and
   //       static-window steps, the sink and current blocks otherwise
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) mbar_init(&S.full[s], 1);
+  //       (warp 0 does it in parallel: lane s initialises stage barrier s and
+  //       issues tile s; with block_size <= 64 every block is one tile and
+  //       tile t's block is arithmetic, so no list is built here)
+  const bool one_tile = bs <= kRows;
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    if (lane < kStages) mbar_init(&S.full[lane], 1);
     mbar_init_fence();
     int nt = 0;
-    if (!use_f) {
-      if (nb <= ms) {
-        for (int j = 0; j < nb; ++j) X.list[j] = j;
-        count = nb;
+    if (one_tile) {
+      int lo = 0;  // static window: {0} U {lo..curr}
+      if (use_f) {
+        nt = curr != 0 ? 2 : 1;
+      } else if (nb <= ms) {
+        nt = nb;
       } else {
-        count = assemble_decode_list(false, nullptr, 0, nb, curr, top_k, X.list);
+        lo = curr - top_k + 1 > 0 ? curr - top_k + 1 : 0;
+        nt = (lo > 0 ? 1 : 0) + (curr - lo + 1);
       }
-      nt = build_tiles(X.list, count, L, bs, S.tile_tok, S.tile_n);
-    } else {
-      nt = add_block_tiles(0, L, bs, S.tile_tok, S.tile_n, 0);
-      nt = add_block_tiles(curr, L, bs, S.tile_tok, S.tile_n, nt);
+      for (int t = lane; t < nt; t += 32) {
+        int j;
+        if (use_f) {
+          j = t == 0 ? 0 : curr;
+        } else if (nb <= ms) {
+          j = t;
+        } else {
+          j = lo > 0 ? (t == 0 ? 0 : lo + t - 1) : lo + t;
+        }
+        const int64_t n = L - static_cast<int64_t>(j) * bs;
+        S.tile_tok[t] = j * bs;
+        S.tile_n[t] = static_cast<int>(n < bs ? n : bs);
+      }
+    } else if (lane == 0) {
+      if (!use_f) {
+        if (nb <= ms) {
+          for (int j = 0; j < nb; ++j) X.list[j] = j;
+          count = nb;
+        } else {
+          count = assemble_decode_list(false, nullptr, 0, nb, curr, top_k, X.list);
+        }
+        nt = build_tiles(X.list, count, L, bs, S.tile_tok, S.tile_n);
+      } else {
+        nt = add_block_tiles(0, L, bs, S.tile_tok, S.tile_n, 0);
+        nt = add_block_tiles(curr, L, bs, S.tile_tok, S.tile_n, nt);
+      }
     }
-    pre = nt < kStages ? nt : kStages;
-    for (int t = 0; t < pre; ++t) issue(t);
-    ntiles = nt;
+    nt = __shfl_sync(0xffffffffu, nt, 0);
+    __syncwarp();
+    const int p = nt < kStages ? nt : kStages;
+    if (lane < p) issue(lane);
+    if (lane == 0) {
+      pre = p;
+      ntiles = nt;
+    }
   }
 
   // -- 1. RoPE, append, compressor running sum
@@ -643,27 +678,27 @@ __global__ void __launch_bounds__(kThreads)
   if (use_f) {
     const int n_scored = rule == SD_RULE_REFERENCE ? 1 : nb;
     if (cand_idx != nullptr) {
-      // precomputed top-k over every block but the current one (whose sum
-      // changed above) merged with the current block's score: the same top-k
-      // as scoring every block here
+      // precomputed top-k (rank order) over every block but the current one,
+      // whose sum changed above.  The current block is attended anyway, so
+      // scoring it can only push the k-th candidate out of the top-k: one
+      // comparison gives the same set as scoring every block here.
       if (threadIdx.x < 32) {
         const int lane = threadIdx.x;
         float p = fmaf(X.f[lane], X.pnew[lane], 0.f);
         p = fmaf(X.f[lane + 32], X.pnew[lane + 32], p);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) p += __shfl_xor_sync(0xffffffffu, p, o);
-        for (int r = lane; r < top_k; r += 32) {
-          const int j = cand_idx[bh * top_k + r];
-          const bool ok = j >= 0 && j < nb && j != curr;
-          X.ci[r] = ok ? j : 0x70000000 + r;
-          X.cv[r] = ok ? cand_val[bh * top_k + r] : -INFINITY;
+        const float vcur = curr < n_scored ? p * sel_scale : -INFINITY;
+        for (int r = lane; r < kk; r += 32) {
+          int j = cand_idx[bh * top_k + r];
+          float v = cand_val[bh * top_k + r];
+          if (j < 0 || j >= nb || j == curr) {
+            j = -1;
+            v = -INFINITY;
+          }
+          if (r == kk - 1 && (j < 0 || better(vcur, curr, v, j))) j = -1;  // displaced by the current block
+          X.tk[r] = j;
         }
-        if (lane == 0) {
-          X.ci[top_k] = curr;
-          X.cv[top_k] = curr < n_scored ? p * sel_scale : -INFINITY;
-        }
-        __syncwarp();
-        warp_topk_kv([&](int c) { return X.cv[c]; }, [&](int c) { return X.ci[c]; }, top_k + 1, kk, X.tk);
       }
       __syncthreads();
     } else {
@@ -671,24 +706,48 @@ __global__ void __launch_bounds__(kThreads)
       __syncthreads();
       cta_topk([&](int j) { return j < n_scored ? X.sc[j] : -INFINITY; }, nb, kk, X.tk);
     }
-    if (threadIdx.x == 0) {
+    // tiles of the chosen blocks other than the sink and the current block
+    // (already staged), deduplicated and placed in ascending block order by
+    // one warp: a kept block's slot is the number of kept blocks below it
+    if (one_tile && kk <= 32) {
+      if (threadIdx.x < 32) {
+        const int lane = threadIdx.x;
+        const int j = lane < kk ? X.tk[lane] : -1;
+        const bool valid = j > 0 && j < nb && j != curr;
+        const unsigned same = __match_any_sync(0xffffffffu, valid ? j : -1 - lane);
+        const bool keep = valid && (__ffs(same) - 1) == lane;
+        const int key = keep ? j : 0x7fffffff;
+        int rank = 0;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) rank += __shfl_sync(0xffffffffu, key, i) < key;
+        const int base = ntiles;
+        if (keep) {
+          const int64_t n = L - static_cast<int64_t>(j) * bs;
+          S.tile_tok[base + rank] = j * bs;
+          S.tile_n[base + rank] = static_cast<int>(n < bs ? n : bs);
+        }
+        const unsigned bal = __ballot_sync(0xffffffffu, keep);
+        if (lane == 0) ntiles = base + __popc(bal);
+      }
+    } else if (threadIdx.x == 0) {
       count = assemble_decode_list(true, X.tk, kk, nb, curr, top_k, X.list);
       ntiles = build_tiles(X.list, count, L, bs, S.tile_tok, S.tile_n, ntiles, 0, curr);
     }
   }
   if (threadIdx.x == 0) {  // the tile holding the new token gets its rows patched
     patch_t = -1;
-    for (int t = 0; t < ntiles; ++t)
-      if (S.tile_tok[t] <= pos && pos < S.tile_tok[t] + S.tile_n[t]) {
-        patch_t = t;
-        patch_row = static_cast<int>(pos - S.tile_tok[t]);
-      }
+    if (one_tile) {  // the current block's single tile
+      patch_t = use_f ? (curr != 0 ? 1 : 0) : (nb <= ms ? curr : ntiles - 1);
+      patch_row = static_cast<int>(pos - static_cast<int64_t>(curr) * bs);
+    } else {
+      for (int t = 0; t < ntiles; ++t)
+        if (S.tile_tok[t] <= pos && pos < S.tile_tok[t] + S.tile_n[t]) {
+          patch_t = t;
+          patch_row = static_cast<int>(pos - S.tile_tok[t]);
+        }
+    }
   }
   __syncthreads();
-  if (sel_out) {
-    for (int i = threadIdx.x; i < sel_cap; i += blockDim.x) sel_out[bh * sel_cap + i] = i < count ? X.list[i] : -1;
-    if (threadIdx.x == 0) cnt_out[bh] = count;
-  }
 
   // -- 3. attention over the selected blocks
   T *o = out + b * o_sb + static_cast<int64_t>(h * G) * kD;
@@ -699,6 +758,23 @@ __global__ void __launch_bounds__(kThreads)
     ok = attend_simt<T, G>(S, ntiles, pre, bulk, scale_log2, o, kD, patch_t, patch_row);
   }
   if (!ok) report(err, SD_KERR_TIMEOUT);
+
+  // -- 4. optional: the selected block list, ascending (inspection only)
+  if (sel_out) {
+    if (threadIdx.x == 0) {
+      if (use_f) {
+        count = assemble_decode_list(true, X.tk, kk, nb, curr, top_k, X.list);
+      } else if (nb <= ms) {
+        for (int j = 0; j < nb; ++j) X.list[j] = j;
+        count = nb;
+      } else {
+        count = assemble_decode_list(false, nullptr, 0, nb, curr, top_k, X.list);
+      }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < sel_cap; i += blockDim.x) sel_out[bh * sel_cap + i] = i < count ? X.list[i] : -1;
+    if (threadIdx.x == 0) cnt_out[bh] = count;
+  }
 }
 
 template <typename T>

@@ -271,7 +271,7 @@ extern "C" int sd_decode_candidates(const void *forecast, int f_dtype, int64_t f
   SD_DISPATCH_DTYPE(f_dtype, E, {
     auto kern = sd::decode_candidates_kernel<E>;
     if (sd::set_max_smem(kern, smem) != SD_OK) return SD_ERR_CUDA;
-    kern<<<static_cast<unsigned>(B * Hkv), 128, smem, s>>>(static_cast<const E *>(forecast), f_sb, proto_sum,
+    kern<<<static_cast<unsigned>(B * Hkv), 256, smem, s>>>(static_cast<const E *>(forecast), f_sb, proto_sum,
                                                            (int)Hkv, NBcap, cur_len, block_size, top_k, rule,
                                                            sel_scale, cand_idx, cand_val);
   });
