@@ -48,6 +48,9 @@ def parse():
     ap.add_argument("--ctx", type=int, default=16384)
     ap.add_argument("--rule", choices=["reference", "absolute"], default="absolute")
     ap.add_argument("--window", type=int, default=64)
+    ap.add_argument("--selection", choices=["kernel", "side-stream"], default="side-stream",
+                    help="forecast selection inside the fused decode kernel, or layer L+1's candidates computed on a "
+                         "side stream during layer L")
     ap.add_argument("--e2e-steps", type=int, default=1024)
     ap.add_argument("--probe-steps", type=int, default=64)
     ap.add_argument("--cpu-seqs", type=int, default=2)
@@ -198,7 +201,7 @@ def run_b200(args, rank, world, local):
     cfg = ModelConfig(block_size=64, top_k_blocks=8, context_length=4096, selector_rule=args.rule,
                       n_layer=args.layers)
     model = SparDAB200Model(cfg).to(dev, torch.bfloat16).eval()
-    caches = model.allocate_caches(B, ctx + W + 64)
+    caches = model.allocate_caches(B, ctx + W + 64, overlap_selection=args.selection == "side-stream")
     gen = torch.Generator(device=dev)
     gen.manual_seed(99 + rank)
     with torch.no_grad():
@@ -297,6 +300,7 @@ def run_b200(args, rank, world, local):
         rewind(caches[0].current_len - ctx)
 
         # ---- roofline of the fused decode kernel (instrumented graph)
+        side = args.selection == "side-stream"
         k_ms, k_bytes, k_launch = 0.0, 0.0, 0
         c_ms, c_bytes, c_launch = 0.0, 0.0, 0
         np_ = __import__("numpy")
@@ -314,16 +318,16 @@ def run_b200(args, rank, world, local):
                 for (b_, h_), c_ in np_.ndenumerate(cnt):
                     for j in sel[b_, h_, :c_]:
                         rows += min(64, L - int(j) * 64)
+                n_sc = (nb - 1) if args.rule == "absolute" else 1  # cached sums scored (current one in smem)
                 k_bytes += (rows * 64 * 2 * 2            # selected K and V rows (bf16)
-                            + B * 4 * 64 * 4             # the current block's running sum, scored in-kernel
                             + B * (1280 + 256 + 768) * 2  # q|k|v in, forecast in, attention out
                             + B * 4 * 64 * 2 * 2         # new K and V rows written
-                            + B * 4 * 64 * 4 * 2         # running block sum read + write
-                            + B * 4 * 8 * 8)             # candidates read
-                if li + 1 < len(probes):  # this block launched layer li+1's candidates
+                            + B * 4 * 64 * 4 * 2)        # current block's running sum read + write
+                if li > 0:  # forecast-driven layers
+                    k_bytes += B * 4 * 8 * 8 if side else B * 4 * n_sc * 64 * 4  # candidates, or every fp32 sum
+                if side and li + 1 < len(probes):  # this block launched layer li+1's candidates
                     c_ms += p["cstart"].elapsed_time(p["cend"])
                     c_launch += 1
-                    n_sc = (nb - 1) if args.rule == "absolute" else 1
                     c_bytes += B * 4 * (n_sc * 64 * 4 + 64 * 2 + 8 * 8)  # fp32 sums scored, forecast, output
             if (i + 1) % W == 0:
                 rewind(W)
@@ -347,14 +351,17 @@ def run_b200(args, rank, world, local):
                    "model": "SparDA-102.45M (12L, 768, 12q/4kv x 64, SwiGLU 2048, vocab 32000)",
                    "global_batch": B * world, "per_gpu_batch": B, "seq_len": ctx,
                    "ctx_window": [ctx + 1, ctx + W], "block_size": 64, "top_k": 8,
-                   "selector_rule": args.rule, "parallelism": f"batch-shard x{world}, no collective",
+                   "selector_rule": args.rule, "selection": args.selection,
+                   "parallelism": f"batch-shard x{world}, no collective",
                    "l2": "no flush: per-step working set (~0.9 GB of weights, prototypes and selected KV) "
                          "exceeds the 126 MB L2"},
         "e2e": {"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": B * 8, "d2h_bytes_per_step": B * 8,
                 "steps": ke, "note": "pinned host token ids in, argmax ids out and read on the host every step"},
-        # per step: fused decode (12) + side-stream candidates (11) + RMSNorm (25)
-        # + SwiGLU gate (12) + length bump (1) kernels of libspardab200.so
-        "gpu_launches": args.steps * (cfg.n_layer + (cfg.n_layer - 1) + (2 * cfg.n_layer + 1) + cfg.n_layer + 1),
+        # per step: fused decode (12) + side-stream candidates (11, side-stream
+        # selection only) + RMSNorm (25) + SwiGLU gate (12) + length bump (1)
+        # kernels of libspardab200.so
+        "gpu_launches": args.steps * (cfg.n_layer + (cfg.n_layer - 1 if side else 0) + (2 * cfg.n_layer + 1)
+                                      + cfg.n_layer + 1),
         "roofline": {"bound": "hbm", "kernel": "sd::decode_layer_kernel<bf16,bf16,3>",
                      "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                      "frac": round(achieved / hbm, 4), "peak_source": src,
@@ -365,7 +372,8 @@ def run_b200(args, rank, world, local):
                                          "achieved": round(c_gbs, 1) if c_gbs else None, "unit": "GB/s",
                                          "frac": round(c_gbs / hbm, 4) if c_gbs else None,
                                          "bytes_per_launch": round(c_bytes / max(c_launch, 1)),
-                                         "avg_launch_us": round(c_avg_s * 1e6, 3), "launches_sampled": c_launch},
+                                         "avg_launch_us": round(c_avg_s * 1e6, 3), "launches_sampled": c_launch}
+                     if side else None,
                      "path": {"achieved": round((k_bytes + c_bytes) / ((k_ms + c_ms) / 1000.0) / 1e9, 1),
                               "note": "decode + candidate kernels' algorithmic bytes over their summed time"}},
         "clocks": clock_info,

@@ -119,6 +119,18 @@ template <typename T, int G> struct AttnSmem {
 };
 constexpr size_t kAlignSlack = 1024;
 
+// Stage buffers 2..kStages-1 seen as fp32 prototype rows (kD floats each):
+// first the K half of that region, then the V half.
+template <typename T> struct ProtoStage {
+  static constexpr int kRowsPerHalf = static_cast<int>((kStages - 2) * kRows * kD * sizeof(T) / (kD * sizeof(float)));
+  template <int G> static __device__ float *k_half(AttnSmem<T, G> &S) {
+    return reinterpret_cast<float *>(S.k + 2 * kRows * kD);
+  }
+  template <int G> static __device__ float *v_half(AttnSmem<T, G> &S) {
+    return reinterpret_cast<float *>(S.v + 2 * kRows * kD);
+  }
+};
+
 // Appends the tiles (<= kRows cached rows each) of block j to the tile table.
 __device__ __forceinline__ int add_block_tiles(int64_t j, int64_t L, int bs, int *tile_tok, int *tile_n, int nt) {
   if (j < 0 || j * bs >= L) return nt;  // invalid or empty block: nothing to stage
@@ -558,6 +570,7 @@ __global__ void __launch_bounds__(kThreads)
   AttnSmem<T, G> S(smem_raw);
   LayerTail X(S.tail, NBcap, top_k);
   __shared__ int count, ntiles, pre, patch_t, patch_row;
+  __shared__ __align__(8) uint64_t proto_bar;  // completion of the staged prototype rows
   const int b = blockIdx.x / Hkv, h = blockIdx.x - (blockIdx.x / Hkv) * Hkv;
   const int Hq = Hkv * G;
   const int64_t pos = *cur_len;
@@ -590,10 +603,29 @@ __global__ void __launch_bounds__(kThreads)
   //       issues tile s; with block_size <= 64 every block is one tile and
   //       tile t's block is arithmetic, so no list is built here)
   const bool one_tile = bs <= kRows;
+  // In-kernel forecast selection stages the running sums of blocks
+  // 0..nstage-1 (every cached block but the current one, whose sum changes
+  // below) into the stage buffers 2..kStages-1, which hold no tile until the
+  // selection is known: one bulk copy per K/V half of that region, issued
+  // before anything else so the scoring reads shared memory.
+  const int stage_cap = ProtoStage<T>::kRowsPerHalf * 2;
+  const bool stage_protos = use_f && one_tile && cand_idx == nullptr && kk <= 32 && rule != SD_RULE_REFERENCE;
+  const int nstage = stage_protos ? (curr < stage_cap ? curr : stage_cap) : 0;
   if (threadIdx.x < 32) {
     const int lane = threadIdx.x;
     if (lane < kStages) mbar_init(&S.full[lane], 1);
+    if (lane == kStages) mbar_init(&proto_bar, 1);
     mbar_init_fence();
+    __syncwarp();
+    if (lane == 31 && nstage > 0) {
+      const float *src = proto_sum + bh * NBcap * kD;
+      const int n0 = nstage < ProtoStage<T>::kRowsPerHalf ? nstage : ProtoStage<T>::kRowsPerHalf;
+      mbar_arrive_expect_tx(&proto_bar, static_cast<uint32_t>(nstage) * kD * sizeof(float));
+      bulk_g2s(ProtoStage<T>::k_half(S), src, n0 * kD * sizeof(float), &proto_bar);
+      if (nstage > n0)
+        bulk_g2s(ProtoStage<T>::v_half(S), src + static_cast<int64_t>(n0) * kD, (nstage - n0) * kD * sizeof(float),
+                 &proto_bar);
+    }
     int nt = 0;
     if (one_tile) {
       int lo = 0;  // static window: {0} U {lo..curr}
@@ -683,11 +715,18 @@ __global__ void __launch_bounds__(kThreads)
       // scoring it can only push the k-th candidate out of the top-k: one
       // comparison gives the same set as scoring every block here.
       if (threadIdx.x < 32) {
+        // the current block's score, summed in the same order as the
+        // in-kernel scoring (cta_score_topk) so both paths agree bit for bit
         const int lane = threadIdx.x;
-        float p = fmaf(X.f[lane], X.pnew[lane], 0.f);
-        p = fmaf(X.f[lane + 32], X.pnew[lane + 32], p);
+        const float4 fq = reinterpret_cast<const float4 *>(X.f)[lane & 15];
+        const float4 pr = reinterpret_cast<const float4 *>(X.pnew)[lane & 15];
+        float p = 0.f;
+        p = fmaf(fq.x, pr.x, p);
+        p = fmaf(fq.y, pr.y, p);
+        p = fmaf(fq.z, pr.z, p);
+        p = fmaf(fq.w, pr.w, p);
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) p += __shfl_xor_sync(0xffffffffu, p, o);
+        for (int o = 8; o > 0; o >>= 1) p += __shfl_xor_sync(0xffffffffu, p, o);
         const float vcur = curr < n_scored ? p * sel_scale : -INFINITY;
         for (int r = lane; r < kk; r += 32) {
           int j = cand_idx[bh * top_k + r];
@@ -701,6 +740,26 @@ __global__ void __launch_bounds__(kThreads)
         }
       }
       __syncthreads();
+    } else if (kk <= 32) {
+      const float4 fq = reinterpret_cast<const float4 *>(X.f)[threadIdx.x & 15];
+      const float *gsum = proto_sum + bh * NBcap * kD;
+      if (nstage > 0) {
+        if (!mbar_wait_bounded(&proto_bar, 0)) {
+          report(err, SD_KERR_TIMEOUT);
+          mbar_wait_bounded(&proto_bar, 0);  // let the copy land before the region is reused
+        }
+        const float *kh = ProtoStage<T>::k_half(S), *vh = ProtoStage<T>::v_half(S);
+        auto row = [&](int j) -> const float * {
+          if (j < nstage)
+            return j < ProtoStage<T>::kRowsPerHalf ? kh + j * kD : vh + (j - ProtoStage<T>::kRowsPerHalf) * kD;
+          return j == curr ? X.pnew : gsum + static_cast<int64_t>(j) * kD;
+        };
+        cta_score_topk_rows(row, fq, nb, n_scored, -1, sel_scale, kk, X.tk, nullptr);
+        // the region is refilled with tiles by the async proxy next
+        if (threadIdx.x == 0) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      } else {
+        cta_score_topk(gsum, kD, fq, nb, n_scored, -1, sel_scale, kk, X.tk, nullptr);
+      }
     } else {
       score_blocks(proto_sum + bh * NBcap * kD, kD, kD, X.f, n_scored, sel_scale, X.sc);
       __syncthreads();

@@ -238,10 +238,18 @@ __global__ void decode_candidates_kernel(const F *__restrict__ fc, int64_t f_sb,
     return;
   }
   const int nb = static_cast<int>(nb64), curr = nb - 1;
-  for (int d = threadIdx.x; d < D; d += blockDim.x) f_s[d] = to_f(fc[b * f_sb + h * D + d]);
-  __syncthreads();
   const int n_scored = rule == SD_RULE_REFERENCE ? 1 : curr;  // the current block is left out
   const int nsc = n_scored < curr ? n_scored : curr;
+  const F *fr = fc + b * f_sb + h * D;
+  if (k <= 32) {  // scoring and top-k in registers
+    const int l16 = threadIdx.x & 15;
+    const float4 fv = make_float4(to_f(fr[4 * l16]), to_f(fr[4 * l16 + 1]), to_f(fr[4 * l16 + 2]),
+                                  to_f(fr[4 * l16 + 3]));
+    cta_score_topk(proto_sum + static_cast<int64_t>(bh) * NBcap * D, D, fv, curr, nsc, -1, sel_scale, k, oi, ov);
+    return;
+  }
+  for (int d = threadIdx.x; d < D; d += blockDim.x) f_s[d] = to_f(fr[d]);
+  __syncthreads();
   score_blocks(proto_sum + static_cast<int64_t>(bh) * NBcap * D, D, D, f_s, nsc, sel_scale, sc);
   __syncthreads();
   auto val = [&](int j) { return j == curr ? __int_as_float(0x7fc00000) : (j < nsc ? sc[j] : -INFINITY); };
@@ -265,7 +273,7 @@ extern "C" int sd_decode_candidates(const void *forecast, int f_dtype, int64_t f
   if (rule != SD_RULE_REFERENCE && rule != SD_RULE_ABSOLUTE) return SD_ERR_INVALID;
   if (D != 64 || top_k > 64 || NBcap > 32768 || B * Hkv > 0x7fffffff) return SD_ERR_UNSUPPORTED;
   if (!sd::aligned16(proto_sum)) return SD_ERR_ALIGN;
-  const size_t smem = sizeof(float) * (D + NBcap);
+  const size_t smem = top_k <= 32 ? 0 : sizeof(float) * (D + NBcap);  // register path needs none
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const float sel_scale = scale / static_cast<float>(block_size);
   SD_DISPATCH_DTYPE(f_dtype, E, {

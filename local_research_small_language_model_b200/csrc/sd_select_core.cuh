@@ -96,6 +96,201 @@ __device__ __forceinline__ int assemble_decode_list(bool use_forecast, const int
   return n;
 }
 
+// ------------------------------------------------------------ register top-k
+// Entry that is never chosen: loses every comparison, including -inf ties
+// (ties are ordered by ascending index).
+constexpr int kNoBlock = 0x7fffffff;
+
+// Compare-exchange of a bitonic network step with partner lane^j: in a run
+// sorted best-first (`best_first`), the lower lane keeps the better entry.
+// Keys are distinct except for identical kNoBlock entries, so "self is
+// better" is "other is not better"; written without branches so the warp
+// never diverges inside the network.
+__device__ __forceinline__ void bitonic_step(float &v, int &i, int j, bool best_first) {
+  const float ov = __shfl_xor_sync(0xffffffffu, v, j);
+  const int oi = __shfl_xor_sync(0xffffffffu, i, j);
+  const bool lower = (threadIdx.x & j) == 0;
+  const bool other_better = (ov > v) | ((ov == v) & (oi < i));
+  const bool take = other_better ^ (lower != best_first);
+  v = take ? ov : v;
+  i = take ? oi : i;
+}
+
+// Sorts every group of K2 lanes best-first (bitonic sort network).
+template <int K2> __device__ __forceinline__ void sort_groups(float &v, int &i) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k = 2; k <= K2; k <<= 1)
+#pragma unroll
+    for (int j = k >> 1; j > 0; j >>= 1) bitonic_step(v, i, j, k == K2 || (lane & k) == 0);
+}
+
+// Sorts a bitonic sequence held by each group of K2 lanes best-first.
+template <int K2> __device__ __forceinline__ void half_clean(float &v, int &i) {
+#pragma unroll
+  for (int j = K2 >> 1; j > 0; j >>= 1) bitonic_step(v, i, j, true);
+}
+
+// Each group of K2 lanes holds a best-first list in (av, ai) and another in
+// (bv, bi); leaves the best K2 of both, best-first, in (av, ai).  best(A[l],
+// B[K2-1-l]) is a bitonic sequence holding exactly that set.
+template <int K2> __device__ __forceinline__ void merge_regs(float &av, int &ai, float bv, int bi) {
+  const float pv = __shfl_xor_sync(0xffffffffu, bv, K2 - 1);
+  const int pi = __shfl_xor_sync(0xffffffffu, bi, K2 - 1);
+  const bool take = (pv > av) | ((pv == av) & (pi < ai));
+  av = take ? pv : av;
+  ai = take ? pi : ai;
+  half_clean<K2>(av, ai);
+}
+
+// Every group of K2 lanes holds a best-first list; leaves the best K2 of all
+// 32/K2 lists, best-first, in lanes 0..K2-1.  At block size s the list of
+// lanes [0, K2) of an s-block meets the mirrored copy of its neighbour's list
+// (lane l ^ (2s - 1)).
+template <int K2> __device__ __forceinline__ void merge_lanes(float &v, int &i) {
+#pragma unroll
+  for (int s = K2; s < 32; s <<= 1) {
+    const float pv = __shfl_xor_sync(0xffffffffu, v, 2 * s - 1);
+    const int pi = __shfl_xor_sync(0xffffffffu, i, 2 * s - 1);
+    const bool take = (pv > v) | ((pv == v) & (pi < i));
+    v = take ? pv : v;
+    i = take ? pi : i;
+    half_clean<K2>(v, i);
+  }
+}
+
+// Fused scoring + top-kk of one (sequence, kv head), all in registers:
+// block j's score is dot(f, row(j)[0 .. 64)) * mul for j < n_scored (row(j):
+// a 16-byte aligned fp32 row in global or shared memory), -inf for
+// n_scored <= j < n, and block `excl` is never chosen.  Every warp takes 32
+// blocks per chunk: lane (half, l16) loads float4 l16 of blocks 32c+2i+half
+// for i = 0..15 (coalesced, 16 loads in flight), then a 4-step reduce-scatter
+// leaves block 32c+2*l16+half's score in that lane; the dot products sum in
+// the same order as score_blocks (per-lane fma chain over 4 dims, then lane
+// pairs 8, 4, 2, 1 apart), so scores are bit-identical.  Up to kChunks chunks
+// are scored at once, their K2-lane groups sorted, and the lists merged in a
+// tournament (registers, then lane groups), which keeps the dependent
+// shuffle chain short; warp 0 merges the warps' lists the same way.  Writes
+// kk <= K2 (index, value) pairs best-first to out_idx (-1 when fewer than kk
+// entries exist) and out_val (nullable); NaN scores are never chosen.  All
+// threads of a CTA of at most 8 warps call it; it ends with a barrier.  fv:
+// the lane's float4 l16 of the fp32 forecast.  Rows are read with plain
+// (coherent) loads: the fused decode kernel writes one of them earlier in the
+// same launch.
+template <int K2, typename Row>
+__device__ __forceinline__ void cta_score_topk_k2(Row row, float4 fv, int n, int n_scored, int excl, float mul,
+                                                  int kk, int *out_idx, float *out_val, float *sv, int *si) {
+  constexpr int kChunks = 4;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int half = lane >> 4, l16 = lane & 15;
+  if (n_scored > n) n_scored = n;
+  float rv = -INFINITY;  // running best-first list of this warp (K2-lane groups)
+  int ri = kNoBlock;
+  for (int base = 32 * warp; base < n; base += 32 * nw * kChunks) {
+    float cv[kChunks];
+    int ci[kChunks];
+#pragma unroll
+    for (int c = 0; c < kChunks; ++c) {
+      const int c0 = base + 32 * nw * c;
+      cv[c] = -INFINITY;
+      ci[c] = kNoBlock;
+      if (c0 >= n) continue;  // warp-uniform: nothing left for this chunk
+      float p[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int j = c0 + 2 * i + half;
+        float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (j < n_scored) r = reinterpret_cast<const float4 *>(row(j))[l16];
+        float a = 0.f;
+        a = fmaf(fv.x, r.x, a);
+        a = fmaf(fv.y, r.y, a);
+        a = fmaf(fv.z, r.z, a);
+        a = fmaf(fv.w, r.w, a);
+        p[i] = a;
+      }
+#pragma unroll
+      for (int d = 8; d > 0; d >>= 1) {
+        const bool hi = (lane & d) != 0;
+#pragma unroll
+        for (int j = 0; j < d; ++j) {
+          const float send = hi ? p[j] : p[j + d];
+          const float keep = hi ? p[j + d] : p[j];
+          p[j] = keep + __shfl_xor_sync(0xffffffffu, send, d);
+        }
+      }
+      int b = c0 + 2 * l16 + half;
+      float v = b < n_scored ? p[0] * mul : -INFINITY;
+      const bool ok = b < n && b != excl && v == v;
+      cv[c] = ok ? v : -INFINITY;
+      ci[c] = ok ? b : kNoBlock;
+    }
+    // (chunks past n hold only never-chosen entries: their sorts and merges
+    // are skipped, warp-uniformly)
+#pragma unroll
+    for (int c = 0; c < kChunks; ++c)
+      if (base + 32 * nw * c < n) sort_groups<K2>(cv[c], ci[c]);
+#pragma unroll
+    for (int w = 1; w < kChunks; w <<= 1)
+#pragma unroll
+      for (int c = 0; c + w < kChunks; c += 2 * w)
+        if (base + 32 * nw * (c + w) < n) merge_regs<K2>(cv[c], ci[c], cv[c + w], ci[c + w]);
+    merge_lanes<K2>(cv[0], ci[0]);
+    if (base == 32 * warp) {  // first round: nothing to merge with yet
+      rv = cv[0];
+      ri = ci[0];
+    } else {
+      merge_regs<K2>(rv, ri, cv[0], ci[0]);  // both lists sit in lanes 0..K2-1
+    }
+  }
+  if (lane < K2) {
+    sv[warp * K2 + lane] = rv;
+    si[warp * K2 + lane] = ri;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const int total = nw * K2;
+    float v = lane < total ? sv[lane] : -INFINITY;
+    int i = lane < total ? si[lane] : kNoBlock;
+    for (int r = 32; r < total; r += 32) {
+      const bool in = r + lane < total;
+      merge_regs<K2>(v, i, in ? sv[r + lane] : -INFINITY, in ? si[r + lane] : kNoBlock);
+    }
+    merge_lanes<K2>(v, i);
+    if (lane < kk) {
+      out_idx[lane] = i == kNoBlock ? -1 : i;
+      if (out_val) out_val[lane] = v;
+    }
+  }
+  __syncthreads();
+}
+
+template <typename Row>
+__device__ __forceinline__ void cta_score_topk_rows(Row row, float4 fv, int n, int n_scored, int excl, float mul,
+                                                    int kk, int *out_idx, float *out_val) {
+  __shared__ float sv[8 * 32];  // the warps' lists, one buffer for every K2
+  __shared__ int si[8 * 32];
+  if (kk <= 1) {
+    cta_score_topk_k2<1>(row, fv, n, n_scored, excl, mul, kk, out_idx, out_val, sv, si);
+  } else if (kk <= 2) {
+    cta_score_topk_k2<2>(row, fv, n, n_scored, excl, mul, kk, out_idx, out_val, sv, si);
+  } else if (kk <= 4) {
+    cta_score_topk_k2<4>(row, fv, n, n_scored, excl, mul, kk, out_idx, out_val, sv, si);
+  } else if (kk <= 8) {
+    cta_score_topk_k2<8>(row, fv, n, n_scored, excl, mul, kk, out_idx, out_val, sv, si);
+  } else if (kk <= 16) {
+    cta_score_topk_k2<16>(row, fv, n, n_scored, excl, mul, kk, out_idx, out_val, sv, si);
+  } else {
+    cta_score_topk_k2<32>(row, fv, n, n_scored, excl, mul, kk, out_idx, out_val, sv, si);
+  }
+}
+
+// cta_score_topk_rows over rows reps + j*r_sn (global memory).
+__device__ __forceinline__ void cta_score_topk(const float *reps, int64_t r_sn, float4 fv, int n, int n_scored,
+                                               int excl, float mul, int kk, int *out_idx, float *out_val) {
+  cta_score_topk_rows([&](int j) { return reps + static_cast<int64_t>(j) * r_sn; }, fv, n, n_scored, excl, mul, kk,
+                      out_idx, out_val);
+}
+
 // Top-kk of n entries by the shared total order (value desc, index asc),
 // written to out_idx; val(j) may return NaN for entries that must not be
 // chosen.  Every warp takes the top-kk of a contiguous slice, then warp 0
