@@ -240,6 +240,45 @@ SD_API int sd_silu_mul(const void *gu, int dtype, int64_t rows, int64_t F, int64
 /* lens[i] += delta for i < n (device int32 array). */
 SD_API int sd_advance_len(int32_t *lens, int n, int delta, void *stream);
 
+/* ---- offloaded KV caches (model/attention/offload.py, async_offload.py) ----
+ * The authoritative K/V rows live in pinned host memory host_k/host_v
+ * [B, Hkv, host_tcap, 64] (block-major, read and written by the GPU through
+ * unified addressing).  Per (sequence, kv head) the device keeps a slot buffer
+ * slot_k/slot_v [B, Hkv, (2 + kslots) * 64, 64]: slot 0 the sink block, slot 1
+ * the block being appended to, slots 2.. the blocks staged for this step.
+ * kslots == top_k <= 31, block_size = 64, head_dim = 64. */
+
+/* Forecast-guided prefetch.  Replaces AsyncOffloadedKVCache.async_transfer_
+ * selected_blocks (model/attention/async_offload.py:55-112) and the transfer
+ * half of AsyncForecastOffloadAttention.prefetch (async_offload.py:170-294).
+ * For the step whose new token takes position *cur_len: wanted blocks are
+ * cand_idx [B, Hkv, top_k] (the side-stream top-k, forecast mode) or, with
+ * cand_idx NULL or on dense steps, the static window / every block.  Blocks
+ * already resident keep their slot; missing ones are copied from the host
+ * store.  slot_block int32 [B, Hkv, kslots + 1] is the residency state (init
+ * -1; the last entry tracks the sink); cand_slot int32 [B, Hkv, top_k]
+ * receives each candidate's slot (-1 = not staged).  stats (nullable) u64[3]
+ * accumulates wanted blocks, hits and bytes copied. */
+SD_API int sd_offload_prefetch(const void *host_k, const void *host_v, int dtype, int64_t B, int64_t Hkv,
+                               int64_t D, int64_t host_tcap, void *slot_k, void *slot_v, int kslots,
+                               const int32_t *cur_len, int block_size, int top_k, const int32_t *cand_idx,
+                               int32_t *slot_block, int32_t *cand_slot, unsigned long long *stats, void *stream);
+
+/* sd_decode_layer on an offloaded cache.  Replaces AsyncForecastOffloadAttention.
+ * _forward_async_decode (async_offload.py:296-519): the new token's K/V go to
+ * slot 1 and, written through, to the host store; attention reads the sink,
+ * current and staged slots.  Forecast steps need the candidates and their
+ * slots from sd_decode_candidates + sd_offload_prefetch (no in-kernel
+ * selection).  Other arguments as sd_decode_layer. */
+SD_API int sd_decode_layer_offload(const void *qkv, int dtype, int64_t qkv_sb, const void *forecast, int f_dtype,
+                                   int64_t f_sb, const float *rope_cos, const float *rope_sin, int64_t max_pos,
+                                   const int32_t *cur_len, void *host_k, void *host_v, int64_t host_tcap,
+                                   void *slot_k, void *slot_v, int kslots, float *proto_sum, int64_t B, int64_t Hq,
+                                   int64_t Hkv, int64_t D, int64_t NBcap, int block_size, int top_k, int rule,
+                                   float scale, void *out, int64_t o_sb, const int32_t *cand_idx,
+                                   const float *cand_val, const int32_t *cand_slot, int32_t *sel_out,
+                                   int32_t *cnt_out, int sel_cap, int32_t *err, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -556,6 +556,19 @@ struct LayerTail {
   }
 };
 
+// Offloaded caches: the authoritative K/V rows live in pinned host memory
+// (host_k/host_v, [B, Hkv, host_tcap, 64], read and written by the GPU over the
+// host link), and the device holds per (sequence, kv head) a slot buffer of
+// 2 + kslots blocks: slot 0 the sink block, slot 1 the block being written,
+// slots 2.. the blocks a prefetch staged for this step.  host_k == nullptr
+// means a plain device cache.
+template <typename T> struct SlotMap {
+  T *host_k = nullptr, *host_v = nullptr;
+  int64_t host_tcap = 0;
+  const int32_t *cand_slot = nullptr;  // [B, Hkv, top_k]: slot (0..kslots-1) of candidate rank r
+  int kslots = 0;
+};
+
 template <typename T, typename F, int G>
 __global__ void __launch_bounds__(kThreads)
     decode_layer_kernel(const T *__restrict__ qkv, int64_t qkv_sb, const F *__restrict__ fc, int64_t f_sb,
@@ -565,16 +578,17 @@ __global__ void __launch_bounds__(kThreads)
                         float scale_log2, const __grid_constant__ CUtensorMap tmk,
                         const __grid_constant__ CUtensorMap tmv, T *__restrict__ out, int64_t o_sb,
                         const int32_t *__restrict__ cand_idx, const float *__restrict__ cand_val,
-                        int32_t *sel_out, int32_t *cnt_out, int sel_cap, int32_t *err) {
+                        int32_t *sel_out, int32_t *cnt_out, int sel_cap, int32_t *err, const SlotMap<T> sm) {
   extern __shared__ __align__(1024) char smem_raw[];
   AttnSmem<T, G> S(smem_raw);
   LayerTail X(S.tail, NBcap, top_k);
+  const bool slots = sm.host_k != nullptr;
   __shared__ int count, ntiles, pre, patch_t, patch_row;
   __shared__ __align__(8) uint64_t proto_bar;  // completion of the staged prototype rows
   const int b = blockIdx.x / Hkv, h = blockIdx.x - (blockIdx.x / Hkv) * Hkv;
   const int Hq = Hkv * G;
   const int64_t pos = *cur_len;
-  if (pos < 0 || pos >= Tcap) {  // cache full (or corrupt length): write nothing
+  if (pos < 0 || pos >= (slots ? sm.host_tcap : Tcap)) {  // cache full (or corrupt length): write nothing
     report(err, SD_KERR_BOUNDS);
     return;
   }
@@ -647,7 +661,10 @@ __global__ void __launch_bounds__(kThreads)
           j = lo > 0 ? (t == 0 ? 0 : lo + t - 1) : lo + t;
         }
         const int64_t n = L - static_cast<int64_t>(j) * bs;
-        S.tile_tok[t] = j * bs;
+        // offloaded cache: the sink, current and window/dense blocks sit in
+        // fixed slots (a window block j in slot 2 + j % kslots)
+        const int src = !slots ? j : (j == curr ? 1 : (j == 0 ? 0 : 2 + j % sm.kslots));
+        S.tile_tok[t] = src * bs;
         S.tile_n[t] = static_cast<int>(n < bs ? n : bs);
       }
     } else if (lane == 0) {
@@ -685,7 +702,12 @@ __global__ void __launch_bounds__(kThreads)
     const float pr = to_f(kr[d < kD / 2 ? d + kD / 2 : d - kD / 2]);
     const float y = rope_elem<T>(x, pr, d, cr[d & (kD / 2 - 1)], sr[d & (kD / 2 - 1)]);
     const T vv = row[static_cast<int64_t>(Hq + Hkv + h) * kD + d];
-    const int64_t off = (bh * Tcap + pos) * kD + d;
+    const int64_t off = (bh * Tcap + (slots ? bs + pos % bs : pos)) * kD + d;
+    if (slots) {  // write-through to the host copy
+      const int64_t hoff = (bh * sm.host_tcap + pos) * kD + d;
+      sm.host_k[hoff] = from_f<T>(y);
+      sm.host_v[hoff] = row[static_cast<int64_t>(Hq + Hkv + h) * kD + d];
+    }
     k_cache[off] = from_f<T>(y);
     v_cache[off] = vv;
     S.newkv[d] = from_f<T>(y);
@@ -772,7 +794,8 @@ __global__ void __launch_bounds__(kThreads)
       if (threadIdx.x < 32) {
         const int lane = threadIdx.x;
         const int j = lane < kk ? X.tk[lane] : -1;
-        const bool valid = j > 0 && j < nb && j != curr;
+        const int cs = slots && lane < kk ? sm.cand_slot[bh * top_k + lane] : 0;
+        const bool valid = j > 0 && j < nb && j != curr && cs >= 0 && (!slots || cs < sm.kslots);
         const unsigned same = __match_any_sync(0xffffffffu, valid ? j : -1 - lane);
         const bool keep = valid && (__ffs(same) - 1) == lane;
         const int key = keep ? j : 0x7fffffff;
@@ -782,7 +805,7 @@ __global__ void __launch_bounds__(kThreads)
         const int base = ntiles;
         if (keep) {
           const int64_t n = L - static_cast<int64_t>(j) * bs;
-          S.tile_tok[base + rank] = j * bs;
+          S.tile_tok[base + rank] = (slots ? 2 + cs : j) * bs;
           S.tile_n[base + rank] = static_cast<int>(n < bs ? n : bs);
         }
         const unsigned bal = __ballot_sync(0xffffffffu, keep);
@@ -890,7 +913,8 @@ int launch_decode_layer(const void *qkv, int64_t qkv_sb, const void *fc, int64_t
                         const float *rs, const int32_t *cur_len, void *kc, void *vc, float *ps, int64_t B,
                         int64_t Hkv, int64_t Tcap, int64_t NBcap, int bs, int top_k, int rule, float scale,
                         void *out, int64_t o_sb, const int32_t *cand_idx, const float *cand_val,
-                        int32_t *sel_out, int32_t *cnt_out, int sel_cap, int32_t *err, cudaStream_t s) {
+                        int32_t *sel_out, int32_t *cnt_out, int sel_cap, int32_t *err, cudaStream_t s,
+                        const SlotMap<T> &sm = SlotMap<T>()) {
   const size_t smem = AttnSmem<T, G>::bytes() + LayerTail::bytes(NBcap, top_k) + kAlignSlack;
   CUtensorMap mk, mv;
   const int r = make_maps<T>(&mk, &mv, kc, vc, B, Hkv, Tcap, kD, Tcap * kD, Hkv * Tcap * kD);
@@ -901,7 +925,7 @@ int launch_decode_layer(const void *qkv, int64_t qkv_sb, const void *fc, int64_t
       static_cast<const T *>(qkv), qkv_sb, static_cast<const F *>(fc), f_sb, rc, rs, cur_len,
       static_cast<T *>(kc), static_cast<T *>(vc), ps, (int)Hkv, Tcap, NBcap, bs, top_k, rule,
       scale / static_cast<float>(bs), scale * kLog2e, mk, mv, static_cast<T *>(out), o_sb, cand_idx, cand_val,
-      sel_out, cnt_out, sel_cap, err);
+      sel_out, cnt_out, sel_cap, err, sm);
   return check_launch();
 }
 
@@ -979,6 +1003,61 @@ extern "C" int sd_decode_layer(const void *qkv, int dtype, int64_t qkv_sb, const
                            qkv, qkv_sb, forecast, f_sb, rope_cos, rope_sin, cur_len, k_cache, v_cache, proto_sum,
                            B, Hkv, Tcap, NBcap, block_size, top_k, rule, scale, out, o_sb, cand_idx, cand_val,
                            sel_out, cnt_out, sel_cap, err, s));
+    } else {
+      return SD_ERR_UNSUPPORTED;
+    }
+  });
+  return SD_OK;
+}
+
+extern "C" int sd_decode_layer_offload(const void *qkv, int dtype, int64_t qkv_sb, const void *forecast,
+                                       int f_dtype, int64_t f_sb, const float *rope_cos, const float *rope_sin,
+                                       int64_t max_pos, const int32_t *cur_len, void *host_k, void *host_v,
+                                       int64_t host_tcap, void *slot_k, void *slot_v, int kslots, float *proto_sum,
+                                       int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t NBcap, int block_size,
+                                       int top_k, int rule, float scale, void *out, int64_t o_sb,
+                                       const int32_t *cand_idx, const float *cand_val, const int32_t *cand_slot,
+                                       int32_t *sel_out, int32_t *cnt_out, int sel_cap, int32_t *err,
+                                       void *stream) {
+  if (!qkv || !rope_cos || !rope_sin || !cur_len || !host_k || !host_v || !slot_k || !slot_v || !proto_sum || !out)
+    return SD_ERR_INVALID;
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || top_k <= 0 || host_tcap <= 0 || NBcap <= 0 ||
+      max_pos < host_tcap)
+    return SD_ERR_INVALID;
+  if (rule != SD_RULE_REFERENCE && rule != SD_RULE_ABSOLUTE) return SD_ERR_INVALID;
+  if (NBcap * block_size < host_tcap) return SD_ERR_INVALID;
+  if ((sel_out == nullptr) != (cnt_out == nullptr) || (sel_out && sel_cap < top_k + 2)) return SD_ERR_INVALID;
+  // the slots only hold what a prefetch staged: forecast steps need the
+  // prefetched candidates (and their slots), never in-kernel selection
+  if ((cand_idx == nullptr) != (cand_val == nullptr) || (cand_idx == nullptr) != (cand_slot == nullptr))
+    return SD_ERR_INVALID;
+  if (forecast != nullptr && cand_idx == nullptr) return SD_ERR_INVALID;
+  if (D != sd::kD || block_size != sd::kRows || kslots != top_k || top_k > 31 || NBcap > 16384 ||
+      B * Hkv > 0x7fffffff)
+    return SD_ERR_UNSUPPORTED;
+  if (!sd::aligned16(slot_k) || !sd::aligned16(slot_v) || !sd::aligned16(proto_sum)) return SD_ERR_ALIGN;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int G = static_cast<int>(Hq / Hkv);
+  const int fdt = forecast ? f_dtype : dtype;
+  const int64_t tslot = static_cast<int64_t>(kslots + 2) * block_size;
+  SD_DISPATCH_DTYPE(dtype, E, {
+    sd::SlotMap<E> sm;
+    sm.host_k = static_cast<E *>(host_k);
+    sm.host_v = static_cast<E *>(host_v);
+    sm.host_tcap = host_tcap;
+    sm.cand_slot = cand_slot;
+    sm.kslots = kslots;
+    if (fdt == dtype) {
+      SD_DISPATCH_G(G, return sd::launch_decode_layer<E, E, GG>(qkv, qkv_sb, forecast, f_sb, rope_cos, rope_sin,
+                                                                cur_len, slot_k, slot_v, proto_sum, B, Hkv, tslot,
+                                                                NBcap, block_size, top_k, rule, scale, out, o_sb,
+                                                                cand_idx, cand_val, sel_out, cnt_out, sel_cap, err,
+                                                                s, sm));
+    } else if (fdt == SD_DTYPE_F32) {
+      SD_DISPATCH_G(G, return sd::launch_decode_layer<E, float, GG>(
+                           qkv, qkv_sb, forecast, f_sb, rope_cos, rope_sin, cur_len, slot_k, slot_v, proto_sum, B,
+                           Hkv, tslot, NBcap, block_size, top_k, rule, scale, out, o_sb, cand_idx, cand_val,
+                           sel_out, cnt_out, sel_cap, err, s, sm));
     } else {
       return SD_ERR_UNSUPPORTED;
     }

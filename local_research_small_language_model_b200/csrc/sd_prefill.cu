@@ -88,6 +88,8 @@ __global__ void prefill_lists_kernel(int mode, int causal, int64_t T, int bs, in
 // 64*G threads: thread (g, r) owns query row r of head h*G+g, keeps q and the
 // fp32 accumulator in registers and streams the listed K/V blocks through
 // shared memory (every thread reads the same key row: broadcast loads).
+constexpr int kKeyChunk = 16;
+
 template <typename T, int G>
 __global__ void __launch_bounds__(64 * G)
     prefill_simt_kernel(const T *__restrict__ q, int64_t q_sb, int64_t q_st, int64_t q_sh, const T *__restrict__ k,
@@ -149,33 +151,34 @@ __global__ void __launch_bounds__(64 * G)
     }
     if (!blk_ok) continue;
     const int nk = static_cast<int>(T_ - k0 < bs ? T_ - k0 : bs);
-    float s[kQTile];
-    float mt = -INFINITY;
+    // online softmax over chunks of 16 keys (keeps the unrolled body small)
+    for (int c0 = 0; c0 < kQTile; c0 += kKeyChunk) {
+      float s[kKeyChunk];
+      float mt = -INFINITY;
 #pragma unroll
-    for (int c = 0; c < kQTile; ++c) {
-      float a = 0.f;
+      for (int c = 0; c < kKeyChunk; ++c) {
+        float a = 0.f;
 #pragma unroll
-      for (int d = 0; d < kHeadDim; ++d) a = fmaf(qr[d], ks[c][d], a);
-      const bool ok = c < nk && (!causal || k0 + c <= t);
-      s[c] = ok ? a : -INFINITY;
-      mt = fmaxf(mt, s[c]);
-    }
-    const float mn = fmaxf(m, mt);
-    if (mn == -INFINITY) continue;
-    const float alpha = exp2f(m - mn);
-    l *= alpha;
-#pragma unroll
-    for (int d = 0; d < kHeadDim; ++d) acc[d] *= alpha;
-#pragma unroll
-    for (int c = 0; c < kQTile; ++c) {
-      const float p = s[c] == -INFINITY ? 0.f : exp2f(s[c] - mn);
-      l += p;
-      if (p != 0.f) {
-#pragma unroll
-        for (int d = 0; d < kHeadDim; ++d) acc[d] = fmaf(p, vs[c][d], acc[d]);
+        for (int d = 0; d < kHeadDim; ++d) a = fmaf(qr[d], ks[c0 + c][d], a);
+        const bool ok = c0 + c < nk && (!causal || k0 + c0 + c <= t);
+        s[c] = ok ? a : -INFINITY;
+        mt = fmaxf(mt, s[c]);
       }
+      const float mn = fmaxf(m, mt);
+      if (mn == -INFINITY) continue;
+      const float alpha = exp2f(m - mn);
+      l *= alpha;
+#pragma unroll
+      for (int d = 0; d < kHeadDim; ++d) acc[d] *= alpha;
+#pragma unroll
+      for (int c = 0; c < kKeyChunk; ++c) {
+        const float p = s[c] == -INFINITY ? 0.f : exp2f(s[c] - mn);
+        l += p;
+#pragma unroll
+        for (int d = 0; d < kHeadDim; ++d) acc[d] = fmaf(p, vs[c0 + c][d], acc[d]);
+      }
+      m = mn;
     }
-    m = mn;
   }
   if (!row_ok) return;
   T *op = out + b * o_sb + t * o_st + static_cast<int64_t>(hq) * o_sh;

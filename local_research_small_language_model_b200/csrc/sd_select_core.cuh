@@ -269,16 +269,10 @@ __device__ __forceinline__ void cta_score_topk_rows(Row row, float4 fv, int n, i
                                                     int kk, int *out_idx, float *out_val) {
   __shared__ float sv[8 * 32];  // the warps' lists, one buffer for every K2
   __shared__ int si[8 * 32];
-  if (kk <= 1) {
-    cta_score_topk_k2<1>(row, fv, n, n_scored, excl, mul, kk, out_idx, out_val, sv, si);
-  } else if (kk <= 2) {
-    cta_score_topk_k2<2>(row, fv, n, n_scored, excl, mul, kk, out_idx, out_val, sv, si);
-  } else if (kk <= 4) {
-    cta_score_topk_k2<4>(row, fv, n, n_scored, excl, mul, kk, out_idx, out_val, sv, si);
-  } else if (kk <= 8) {
+  // two list widths keep the number of instantiations (and build time) small:
+  // a top-kk list is the first kk entries of the top-8 or top-32 list
+  if (kk <= 8) {
     cta_score_topk_k2<8>(row, fv, n, n_scored, excl, mul, kk, out_idx, out_val, sv, si);
-  } else if (kk <= 16) {
-    cta_score_topk_k2<16>(row, fv, n, n_scored, excl, mul, kk, out_idx, out_val, sv, si);
   } else {
     cta_score_topk_k2<32>(row, fv, n, n_scored, excl, mul, kk, out_idx, out_val, sv, si);
   }
