@@ -6,6 +6,7 @@ Drop-in for the reference's attention-backend / forecast API
 * ``KVBlockCompressor``, ``ForecastBlockSelector``  (model/forecast.py)
 * ``B200SparseAttention``, ``gather_kv_blocks``      (model/attention/sparse.py)
 * ``B200KVCache``                                    (model/attention/base.py KVCache)
+* ``B200OffloadKVCache``                             (model/attention/offload.py, async_offload.py)
 * ``install(model)`` swaps the attention of every layer of a reference model.
 
 All compute runs in libspardab200.so (hand-written CUDA for sm_100a, C ABI in
@@ -14,6 +15,7 @@ include/spardab200.h).  There is no CPU path.
 
 from .config import ModelConfig
 from .cache import B200KVCache
+from .offload import B200OffloadKVCache
 from .forecast import ForecastBlockSelector, ForecastProjection, KVBlockCompressor
 from .attention import B200SparseAttention, BaseAttention
 from .ops import gather_kv_blocks
@@ -21,7 +23,7 @@ from .rope import RotaryEmbedding
 from . import ops
 from ._lib import SparDAError, load as load_library
 
-__all__ = ["ModelConfig", "B200KVCache", "ForecastBlockSelector", "ForecastProjection", "KVBlockCompressor",
+__all__ = ["ModelConfig", "B200KVCache", "B200OffloadKVCache", "ForecastBlockSelector", "ForecastProjection", "KVBlockCompressor",
            "B200SparseAttention", "BaseAttention", "gather_kv_blocks", "RotaryEmbedding", "ops", "SparDAError",
            "load_library", "install"]
 

@@ -11,6 +11,7 @@ import torch.nn.functional as F
 
 from . import ops
 from .cache import B200KVCache
+from .offload import B200OffloadKVCache
 from .forecast import ForecastBlockSelector, KVBlockCompressor
 from .rope import apply_rotary_emb
 
@@ -83,6 +84,8 @@ class B200SparseAttention(BaseAttention):
         if kv_cache is not None and t == 1:
             if isinstance(kv_cache, B200KVCache):
                 return self._decode_fused(x, rotary_emb, kv_cache, forecast_vector)
+            if isinstance(kv_cache, B200OffloadKVCache):
+                return self._decode_offload(x, rotary_emb, kv_cache, forecast_vector)
             return self._decode_generic(x, rotary_emb, kv_cache, forecast_vector)
         return self._prefill(x, rotary_emb, kv_cache, mask, is_causal, forecast_vector, **kwargs)
 
@@ -99,6 +102,45 @@ class B200SparseAttention(BaseAttention):
         out = ops.decode_layer(qkv, f, rotary_emb.cos, rotary_emb.sin, cache.len_dev, cache.k_store,
                                cache.v_store, cache.proto_sum, self.n_head, self.n_kv_head, self.block_size,
                                self.top_k_blocks, self.rule)
+        cache.advance(1, device=not getattr(cache, "shared_len", False))
+        return self.wo(out.to(x.dtype)).view(b, 1, self.n_embd)
+
+    # -- offloaded caches (model/attention/async_offload.py:170-519)
+    def prefetch(self, forecast_vector: Optional[torch.Tensor], offload_cache) -> bool:
+        """Called by layer L with its forecast to stage layer L+1's blocks
+        (this layer's) on the cache's transfer stream while layer L computes
+        (async_offload.py:170-294).  Returns False when there is nothing to do."""
+        if not isinstance(offload_cache, B200OffloadKVCache) or offload_cache.current_len == 0:
+            return False
+        f = forecast_vector if self.mode == "forecast" else None
+        offload_cache.issue_prefetch(f, self.rule, self.top_k_blocks)
+        return True
+
+    def offload_ready(self, cache: B200OffloadKVCache, f: Optional[torch.Tensor]) -> None:
+        """Orders the current stream after this step's prefetch, issuing it
+        here (synchronously in stream order) when none is in flight or the one
+        in flight was for the other selection mode (async_offload.py:392-460)."""
+        cur = torch.cuda.current_stream(cache.gpu_device)
+        if cache.prefetched:
+            cur.wait_event(cache.prefetch_event)
+            if cache.has_cand == (f is not None):
+                return
+        cache.issue_prefetch(f, self.rule, self.top_k_blocks, stream=cur)
+
+    def _decode_offload(self, x, rotary_emb, cache: B200OffloadKVCache, forecast_vector):
+        b = x.shape[0]
+        if cache.current_len >= cache.tcap:
+            raise ValueError(f"cache full: {cache.current_len} tokens of {cache.tcap}")
+        if rotary_emb.cos.shape[0] < cache.tcap:
+            rotary_emb._extend_cache(cache.tcap, x.device)
+        qkv = F.linear(x.view(b, self.n_embd), self.qkv_weight())
+        if qkv.dtype != cache.slot_k.dtype:
+            qkv = qkv.to(cache.slot_k.dtype)
+        f = forecast_vector if (self.mode == "forecast" and forecast_vector is not None) else None
+        self.offload_ready(cache, f)
+        out = ops.decode_layer_offload(qkv, f, rotary_emb.cos, rotary_emb.sin, cache, self.n_head, self.rule,
+                                       cand=cache.cand if f is not None else None)
+        cache.prefetched = False
         cache.advance(1, device=not getattr(cache, "shared_len", False))
         return self.wo(out.to(x.dtype)).view(b, 1, self.n_embd)
 
@@ -133,7 +175,10 @@ class B200SparseAttention(BaseAttention):
             # (sparse.py:413-430), so a prompt cannot extend a filled cache
             raise NotImplementedError("prefill into a non-empty cache")
         xq, xk = rotary_emb(xq, xk, offset=0)
-        if kv_cache is not None:
+        if isinstance(kv_cache, B200OffloadKVCache):
+            kv_cache.update(xk, xv)  # host store + block sums + slots; attend over the prompt itself
+            kh, vh = xk.transpose(1, 2), xv.transpose(1, 2)
+        elif kv_cache is not None:
             k_all, v_all = kv_cache.update(xk, xv)
             if isinstance(kv_cache, B200KVCache):
                 kh, vh = kv_cache.k_store[:, :, :t], kv_cache.v_store[:, :, :t]

@@ -19,6 +19,7 @@ import torch.nn.functional as F
 from . import ops
 from .attention import B200SparseAttention
 from .cache import B200KVCache
+from .offload import B200OffloadKVCache
 from .config import ModelConfig
 from .forecast import ForecastProjection
 from .rope import RotaryEmbedding
@@ -114,7 +115,7 @@ class TransformerBlock(nn.Module):
     def forward(self, x, rotary_emb, kv_cache=None, mask=None, is_causal=True, prev_layer_forecast=None,
                 next_layer_block=None, next_kv_cache=None):
         b, t, c = x.shape
-        if isinstance(kv_cache, B200KVCache) and t == 1:
+        if isinstance(kv_cache, (B200KVCache, B200OffloadKVCache)) and t == 1:
             # decode step: 8 launches per layer (norm, [wq;wk;wv;wf] GEMM, fused
             # attention kernel, wo GEMM with the residual add folded into addmm,
             # norm, [w_gate;w_up] GEMM, SwiGLU gate kernel, w_down addmm)
@@ -135,7 +136,16 @@ class TransformerBlock(nn.Module):
             # compute them on the side stream while this layer's attention and
             # FFN run on the main stream
             side = getattr(self, "side_stream", None)
-            if side is not None and next_layer_block is not None and isinstance(next_kv_cache, B200KVCache) \
+            if next_layer_block is not None and isinstance(next_kv_cache, B200OffloadKVCache):
+                # offloaded next layer: candidates + host -> device staging of
+                # its blocks on the transfer stream (transformer.py:110-115)
+                if probe is not None and "cstart" in probe:
+                    next_kv_cache.transfer_stream.wait_stream(torch.cuda.current_stream())
+                    probe["cstart"].record(next_kv_cache.transfer_stream)
+                next_layer_block.attention.prefetch(current_forecast, next_kv_cache)
+                if probe is not None and "cend" in probe:
+                    probe["cend"].record(next_kv_cache.transfer_stream)
+            elif side is not None and next_layer_block is not None and isinstance(next_kv_cache, B200KVCache) \
                     and next_layer_block.attention.mode == "forecast":
                 na = next_layer_block.attention
                 nc = next_kv_cache
@@ -153,6 +163,26 @@ class TransformerBlock(nn.Module):
                         probe["cend"].record(side)
                     nc.cand_event.record(side)
                 nc.cand_ready = True
+            if isinstance(kv_cache, B200OffloadKVCache):
+                if probe is not None and "wstart" in probe:
+                    probe["wstart"].record()
+                a.offload_ready(kv_cache, f)
+                if probe is not None and "wend" in probe:
+                    probe["wend"].record()
+                if probe is not None:
+                    probe["start"].record()
+                out = ops.decode_layer_offload(proj[:, :nq], f, rotary_emb.cos, rotary_emb.sin, kv_cache, a.n_head,
+                                               a.rule, sel_out=probe["sel"] if probe is not None else None,
+                                               cnt_out=probe["cnt"] if probe is not None else None,
+                                               cand=kv_cache.cand if f is not None else None)
+                if probe is not None:
+                    probe["end"].record()
+                kv_cache.prefetched = False
+                kv_cache.advance(1, device=not getattr(kv_cache, "shared_len", False))
+                x2 = torch.addmm(x2, out, a.wo.weight.t())
+                gu = F.linear(self.ffn_norm(x2), self.packed_ffn_weight())
+                x2 = torch.addmm(x2, ops.silu_mul(gu), self.ffn.w_down.weight.t())
+                return x2.view(b, 1, c), current_forecast
             cand = None
             if getattr(kv_cache, "cand_ready", False):
                 torch.cuda.current_stream().wait_event(kv_cache.cand_event)  # join the side stream
@@ -204,24 +234,31 @@ class SparDAB200Model(nn.Module):
             nn.init.normal_(module.weight, mean=0.0, std=self.config.initializer_range)
 
     def allocate_caches(self, batch: int, max_seq_len: int, dtype: Optional[torch.dtype] = None,
-                        device=None, overlap_selection: bool = True) -> List[B200KVCache]:
-        """One B200KVCache per layer, sharing one device length array so a
-        decode step bumps all lengths with a single launch.  With
+                        device=None, overlap_selection: bool = True, offload: bool = False) -> List:
+        """One cache per layer, sharing one device length array so a decode
+        step bumps all lengths with a single launch.  With
         ``overlap_selection`` each decode step scores layer L+1's prototypes on
-        a side stream while layer L's attention and FFN run."""
+        a side stream while layer L's attention and FFN run.  With ``offload``
+        the K/V rows live in pinned host memory (B200OffloadKVCache) and the
+        side stream also stages layer L+1's selected blocks into device slots."""
         cfg = self.config
         device = device or self.embeddings.weight.device
         dtype = dtype or self.embeddings.weight.dtype
         self._lens = torch.zeros(cfg.n_layer, dtype=torch.int32, device=device)
         caches = []
+        side = torch.cuda.Stream(device=device) if torch.device(device).type == "cuda" else None
         for i in range(cfg.n_layer):
-            c = B200KVCache(batch, max_seq_len, cfg.n_kv_head, cfg.head_dim, device, dtype, cfg.block_size,
-                            len_dev=self._lens[i:i + 1])
+            if offload:
+                c = B200OffloadKVCache(batch, max_seq_len, cfg.n_kv_head, cfg.head_dim, device, dtype,
+                                       transfer_stream=side, block_size=cfg.block_size, top_k=cfg.top_k_blocks,
+                                       len_dev=self._lens[i:i + 1])
+            else:
+                c = B200KVCache(batch, max_seq_len, cfg.n_kv_head, cfg.head_dim, device, dtype, cfg.block_size,
+                                len_dev=self._lens[i:i + 1])
             c.shared_len = True
             caches.append(c)
         self.rotary_emb._extend_cache(caches[0].tcap, device)
-        if overlap_selection and torch.device(device).type == "cuda":
-            side = torch.cuda.Stream(device=device)
+        if overlap_selection and side is not None:
             for layer in self.layers:
                 layer.side_stream = side
         return caches

@@ -114,22 +114,34 @@ def topk_rows(scores: torch.Tensor, k: int) -> Tuple[torch.Tensor, torch.Tensor]
 
 # ---------------------------------------------------------------- K4 gather
 def gather_kv_blocks(k: torch.Tensor, v: torch.Tensor, block_indices: torch.Tensor,
-                     block_size: int) -> Tuple[torch.Tensor, torch.Tensor]:
+                     block_size: int, device: Optional[torch.device] = None) -> Tuple[torch.Tensor, torch.Tensor]:
     """gather_kv_blocks (model/attention/sparse.py:19-62): k, v [B,H,T,D],
-    indices [B,H,S] -> [B,H,S*block_size,D]."""
-    _cuda(k, v, block_indices)
-    if k.stride() != v.stride() or k.dtype != v.dtype:
-        k, v = k.contiguous(), v.contiguous()
-    k, v = _inner1(k), _inner1(v)
-    if k.stride() != v.stride():
-        k, v = k.contiguous(), v.contiguous()
+    indices [B,H,S] -> [B,H,S*block_size,D].  k and v may also be pinned host
+    tensors (an offloaded cache): the kernel on ``device`` then reads the
+    selected rows straight from host memory."""
+    if not k.is_cuda or not v.is_cuda:
+        if not (k.is_pinned() and v.is_pinned()) or device is None:
+            raise ValueError("host K/V must be pinned, and the gather needs a target device")
+        if k.stride() != v.stride() or k.dtype != v.dtype or k.stride(-1) != 1:
+            raise ValueError("pinned host K/V must share dtype and strides, innermost stride 1")
+        _cuda(block_indices)
+        out_dev = torch.device(device)
+    else:
+        _cuda(block_indices)
+        if k.stride() != v.stride() or k.dtype != v.dtype:
+            k, v = k.contiguous(), v.contiguous()
+        k, v = _inner1(k), _inner1(v)
+        if k.stride() != v.stride():
+            k, v = k.contiguous(), v.contiguous()
+        out_dev = k.device
     b, h, t, d = k.shape
     idx = block_indices.to(torch.int64).contiguous()
     s = idx.shape[-1]
-    ko = torch.empty(b, h, s * block_size, d, dtype=k.dtype, device=k.device)
+    ko = torch.empty(b, h, s * block_size, d, dtype=k.dtype, device=out_dev)
     vo = torch.empty_like(ko)
     L.call("sd_gather_kv_blocks", k.data_ptr(), v.data_ptr(), dtype_code(k), b, h, t, d, k.stride(0), k.stride(1),
-           k.stride(2), idx.data_ptr(), s, block_size, ko.data_ptr(), vo.data_ptr(), _stream(k))
+           k.stride(2), idx.data_ptr(), s, block_size, ko.data_ptr(), vo.data_ptr(),
+           torch.cuda.current_stream(out_dev).cuda_stream)
     return ko, vo
 
 
@@ -261,6 +273,58 @@ def decode_candidates(forecast: torch.Tensor, proto_sum: torch.Tensor, cur_len: 
            out[1].data_ptr(), _stream(forecast))
     return out
 
+
+
+# ---------------------------------------------------------------- offloaded caches
+def offload_prefetch(cache, cand_idx: Optional[torch.Tensor] = None) -> None:
+    """Stages the blocks the next decode step of an offloaded layer attends to
+    (sd_offload_prefetch): the candidates cand_idx [B,Hkv,top_k] (forecast
+    steps) or the static window / every block, copied from the pinned host
+    store into the cache's device slots unless already resident."""
+    _cuda(cache.slot_k, cache.len_dev)
+    b, h, _, d = cache.slot_k.shape
+    L.call("sd_offload_prefetch", cache.host_k.data_ptr(), cache.host_v.data_ptr(), dtype_code(cache.slot_k), b, h,
+           d, cache.tcap, cache.slot_k.data_ptr(), cache.slot_v.data_ptr(), cache.kslots, cache.len_dev.data_ptr(),
+           cache.block_size, cache.kslots, cand_idx.data_ptr() if cand_idx is not None else None,
+           cache.slot_block.data_ptr(), cache.cand_slot.data_ptr(), cache.stats.data_ptr(),
+           torch.cuda.current_stream(cache.slot_k.device).cuda_stream)
+
+
+def decode_layer_offload(qkv: torch.Tensor, forecast: Optional[torch.Tensor], rope_cos: torch.Tensor,
+                         rope_sin: torch.Tensor, cache, n_head: int, rule: str = "reference",
+                         scale: Optional[float] = None, out: Optional[torch.Tensor] = None,
+                         sel_out: Optional[torch.Tensor] = None, cnt_out: Optional[torch.Tensor] = None,
+                         cand: Optional[Tuple[torch.Tensor, torch.Tensor]] = None) -> torch.Tensor:
+    """decode_layer on an offloaded cache (sd_decode_layer_offload): the new
+    token is written to the current-block slot and through to the host store;
+    attention reads the sink, current and prefetched slots.  Forecast steps
+    need ``cand`` (and the slots offload_prefetch assigned to it)."""
+    _cuda(qkv, forecast, rope_cos, rope_sin, cache.slot_k)
+    b = qkv.shape[0]
+    d = cache.slot_k.shape[-1]
+    hkv = cache.n_kv_head
+    qkv = _inner1(qkv)
+    if out is None:
+        out = torch.empty(b, n_head * d, dtype=cache.slot_k.dtype, device=qkv.device)
+    if forecast is not None:
+        f = _inner1(forecast.reshape(b, hkv * d))
+        fargs = (f.data_ptr(), dtype_code(f), f.stride(0))
+    else:
+        fargs = (None, dtype_code(cache.slot_k), 0)
+    sc = 1.0 / math.sqrt(d) if scale is None else scale
+    L.call("sd_decode_layer_offload", qkv.data_ptr(), dtype_code(qkv), qkv.stride(0), *fargs, rope_cos.data_ptr(),
+           rope_sin.data_ptr(), rope_cos.shape[0], cache.len_dev.data_ptr(), cache.host_k.data_ptr(),
+           cache.host_v.data_ptr(), cache.tcap, cache.slot_k.data_ptr(), cache.slot_v.data_ptr(), cache.kslots,
+           cache.proto_sum.data_ptr(), b, n_head, hkv, d, cache.nbcap, cache.block_size, cache.kslots, RULES[rule],
+           sc, out.data_ptr(), out.stride(0),
+           cand[0].data_ptr() if cand is not None else None,
+           cand[1].data_ptr() if cand is not None else None,
+           cache.cand_slot.data_ptr() if cand is not None else None,
+           sel_out.data_ptr() if sel_out is not None else None,
+           cnt_out.data_ptr() if cnt_out is not None else None,
+           sel_out.shape[-1] if sel_out is not None else 0,
+           error_buffer(qkv.device).data_ptr(), _stream(qkv))
+    return out
 
 # ---------------------------------------------------------------- prefill
 LIST_MODES = {"dense": 0, "masked_forecast": 1, "masked_static": 2, "chunked_forecast": 3, "chunked_static": 4}
