@@ -48,6 +48,9 @@ def parse():
     ap.add_argument("--ctx", type=int, default=16384)
     ap.add_argument("--rule", choices=["reference", "absolute"], default="absolute")
     ap.add_argument("--window", type=int, default=64)
+    ap.add_argument("--offload", action="store_true",
+                    help="BASELINE config 5 sample: K/V rows in pinned host memory, forecast-guided prefetch of the "
+                         "selected blocks into device slots (use with e.g. --ctx 32768)")
     ap.add_argument("--selection", choices=["kernel", "side-stream"], default="side-stream",
                     help="forecast selection inside the fused decode kernel, or layer L+1's candidates computed on a "
                          "side stream during layer L")
@@ -201,11 +204,18 @@ def run_b200(args, rank, world, local):
     cfg = ModelConfig(block_size=64, top_k_blocks=8, context_length=4096, selector_rule=args.rule,
                       n_layer=args.layers)
     model = SparDAB200Model(cfg).to(dev, torch.bfloat16).eval()
-    caches = model.allocate_caches(B, ctx + W + 64, overlap_selection=args.selection == "side-stream")
+    caches = model.allocate_caches(B, ctx + W + 64, overlap_selection=args.selection == "side-stream",
+                                   offload=args.offload)
     gen = torch.Generator(device=dev)
     gen.manual_seed(99 + rank)
     with torch.no_grad():
         for c in caches:
+            if args.offload:  # one prompt per layer: host store, block sums and slots
+                k = torch.randn(B, ctx, 4, 64, generator=gen, device=dev, dtype=torch.bfloat16)
+                v = torch.randn(B, ctx, 4, 64, generator=gen, device=dev, dtype=torch.bfloat16)
+                c.update(k, v)
+                del k, v
+                continue
             for s in range(0, ctx, 2048):
                 n = min(2048, ctx - s)
                 k = torch.randn(B, n, 4, 64, generator=gen, device=dev, dtype=torch.bfloat16)
@@ -232,6 +242,9 @@ def run_b200(args, rank, world, local):
              "cend": torch.cuda.Event(enable_timing=True, external=True),
              "sel": torch.full((B, 4, 16), -1, dtype=torch.int32, device=dev),
              "cnt": torch.zeros(B, 4, dtype=torch.int32, device=dev)}
+        if args.offload:  # the compute stream's wait for the layer's prefetch
+            p["wstart"] = torch.cuda.Event(enable_timing=True, external=True)
+            p["wend"] = torch.cuda.Event(enable_timing=True, external=True)
         layer.probe = p
         probes.append(p)
     inst = DecodeEngine(model, caches, B)
@@ -263,6 +276,7 @@ def run_b200(args, rank, world, local):
         clocks.start()
         barrier()
         torch.cuda.synchronize()
+        stats0 = sum(c.stats.clone() for c in caches) if args.offload else None
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         ev0.record()
         for i in range(args.steps):
@@ -274,6 +288,7 @@ def run_b200(args, rank, world, local):
         barrier()
         clock_info = clocks.stop()
         ms = max_over_ranks(ev0.elapsed_time(ev1))
+        stats1 = sum(c.stats.clone() for c in caches) if args.offload else None
         rewind(caches[0].current_len - ctx)
 
         # ---- e2e: the public API with host buffers, greedy loop that reads
@@ -302,6 +317,7 @@ def run_b200(args, rank, world, local):
         # ---- roofline of the fused decode kernel (instrumented graph)
         side = args.selection == "side-stream"
         k_ms, k_bytes, k_launch = 0.0, 0.0, 0
+        w_ms = 0.0
         c_ms, c_bytes, c_launch = 0.0, 0.0, 0
         np_ = __import__("numpy")
         for i in range(args.probe_steps):
@@ -311,6 +327,8 @@ def run_b200(args, rank, world, local):
             nb = (L + 63) // 64
             for li, p in enumerate(probes):
                 k_ms += p["start"].elapsed_time(p["end"])
+                if args.offload:
+                    w_ms += p["wstart"].elapsed_time(p["wend"])
                 k_launch += 1
                 sel = p["sel"].cpu().numpy()
                 cnt = p["cnt"].cpu().numpy()
@@ -325,7 +343,7 @@ def run_b200(args, rank, world, local):
                             + B * 4 * 64 * 4 * 2)        # current block's running sum read + write
                 if li > 0:  # forecast-driven layers
                     k_bytes += B * 4 * 8 * 8 if side else B * 4 * n_sc * 64 * 4  # candidates, or every fp32 sum
-                if side and li + 1 < len(probes):  # this block launched layer li+1's candidates
+                if (side or args.offload) and li + 1 < len(probes):  # layer li+1's candidates (+ prefetch)
                     c_ms += p["cstart"].elapsed_time(p["cend"])
                     c_launch += 1
                     c_bytes += B * 4 * (n_sc * 64 * 4 + 64 * 2 + 8 * 8)  # fp32 sums scored, forecast, output
@@ -378,6 +396,20 @@ def run_b200(args, rank, world, local):
                               "note": "decode + candidate kernels' algorithmic bytes over their summed time"}},
         "clocks": clock_info,
     }
+    if args.offload:
+        wanted, hits, h2d = (float(x) for x in (stats1 - stats0).tolist())
+        result["metric"] = "KV-offload decode tok/s (BASELINE config 5 sample)"
+        result["config"]["workload"] = (f"BASELINE config 5 sample: {B} sequences per GPU at {ctx} cached tokens, "
+                                        "K/V in pinned host memory, forecast-guided prefetch into device slots")
+        result["offload"] = {
+            "host_store_gb": round(sum(2 * c.host_k.numel() * c.host_k.element_size() for c in caches) / 1e9, 2),
+            "h2d_bytes_per_step": round(h2d / args.steps),
+            "h2d_gbs": round(h2d / (ms / 1000.0) / 1e9, 2),
+            "prefetch_hit_rate": round(hits / wanted, 4) if wanted else None,
+            "exposed_wait_us_per_step": round(w_ms * 1000.0 / max(args.probe_steps, 1), 2),
+            "prefetch_us_per_layer": round(c_ms * 1000.0 / max(c_launch, 1), 2),
+            "note": "exposed wait = compute-stream time blocked on the layers' prefetch events (instrumented "
+                    "graph); prefetch time includes the candidate kernel"}
     return result
 
 

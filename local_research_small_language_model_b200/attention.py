@@ -106,14 +106,14 @@ class B200SparseAttention(BaseAttention):
         return self.wo(out.to(x.dtype)).view(b, 1, self.n_embd)
 
     # -- offloaded caches (model/attention/async_offload.py:170-519)
-    def prefetch(self, forecast_vector: Optional[torch.Tensor], offload_cache) -> bool:
+    def prefetch(self, forecast_vector: Optional[torch.Tensor], offload_cache, timing_events=None) -> bool:
         """Called by layer L with its forecast to stage layer L+1's blocks
         (this layer's) on the cache's transfer stream while layer L computes
         (async_offload.py:170-294).  Returns False when there is nothing to do."""
         if not isinstance(offload_cache, B200OffloadKVCache) or offload_cache.current_len == 0:
             return False
         f = forecast_vector if self.mode == "forecast" else None
-        offload_cache.issue_prefetch(f, self.rule, self.top_k_blocks)
+        offload_cache.issue_prefetch(f, self.rule, self.top_k_blocks, timing_events=timing_events)
         return True
 
     def offload_ready(self, cache: B200OffloadKVCache, f: Optional[torch.Tensor]) -> None:

@@ -139,12 +139,8 @@ class TransformerBlock(nn.Module):
             if next_layer_block is not None and isinstance(next_kv_cache, B200OffloadKVCache):
                 # offloaded next layer: candidates + host -> device staging of
                 # its blocks on the transfer stream (transformer.py:110-115)
-                if probe is not None and "cstart" in probe:
-                    next_kv_cache.transfer_stream.wait_stream(torch.cuda.current_stream())
-                    probe["cstart"].record(next_kv_cache.transfer_stream)
-                next_layer_block.attention.prefetch(current_forecast, next_kv_cache)
-                if probe is not None and "cend" in probe:
-                    probe["cend"].record(next_kv_cache.transfer_stream)
+                ev = (probe["cstart"], probe["cend"]) if probe is not None and "cstart" in probe else None
+                next_layer_block.attention.prefetch(current_forecast, next_kv_cache, timing_events=ev)
             elif side is not None and next_layer_block is not None and isinstance(next_kv_cache, B200KVCache) \
                     and next_layer_block.attention.mode == "forecast":
                 na = next_layer_block.attention

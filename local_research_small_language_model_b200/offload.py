@@ -184,21 +184,26 @@ class B200OffloadKVCache:
 
     # -- forecast-guided prefetch
     def issue_prefetch(self, forecast: Optional[torch.Tensor], rule: str, top_k: int,
-                       stream: Optional[torch.cuda.Stream] = None) -> None:
+                       stream: Optional[torch.cuda.Stream] = None, timing_events=None) -> None:
         """For the next decode step: candidates from the forecast (if any) and
         the staging of the wanted blocks, on ``stream`` (default: the transfer
-        stream, ordered after the current stream's work)."""
+        stream, ordered after the current stream's work).  timing_events: an
+        optional (start, end) pair of CUDA events recorded around that work."""
         s = stream or self.transfer_stream
         cur = torch.cuda.current_stream(self.gpu_device)
         if s is not cur:
             s.wait_stream(cur)
         with torch.cuda.stream(s):
+            if timing_events is not None:
+                timing_events[0].record(s)
             if forecast is not None:
                 ops.decode_candidates(forecast, self.proto_sum, self.len_dev, self.n_kv_head, self.block_size, top_k,
                                       rule, out=self.cand)
                 ops.offload_prefetch(self, self.cand[0])
             else:
                 ops.offload_prefetch(self, None)
+            if timing_events is not None:
+                timing_events[1].record(s)
             self.prefetch_event.record(s)
         self.prefetched = True
         self.has_cand = forecast is not None
