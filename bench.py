@@ -48,6 +48,9 @@ def parse():
     ap.add_argument("--ctx", type=int, default=16384)
     ap.add_argument("--rule", choices=["reference", "absolute"], default="absolute")
     ap.add_argument("--window", type=int, default=64)
+    ap.add_argument("--prefill", action="store_true",
+                    help="BASELINE config 3: prefill of one --ctx-token sequence (e.g. --ctx 32768) through the "
+                         "12-layer model; roofline of the tensor-core block-sparse prefill attention")
     ap.add_argument("--offload", action="store_true",
                     help="BASELINE config 5 sample: K/V rows in pinned host memory, forecast-guided prefetch of the "
                          "selected blocks into device slots (use with e.g. --ctx 32768)")
@@ -413,6 +416,113 @@ def run_b200(args, rank, world, local):
     return result
 
 
+def prefill_flops(lists, counts, T, G, causal=True):
+    """Algorithmic attention FLOPs of one prefill: 4*D per valid (query head,
+    query, key) triple of the block lists (QK^T and PV, 2 flops per MAC)."""
+    import numpy as np
+    lists = lists.cpu().numpy()
+    counts = counts.cpu().numpy()
+    total = 0
+    b_, h_, nqt, _ = lists.shape
+    for ib in range(b_):
+        for ih in range(h_):
+            for qt in range(nqt):
+                q0, q1 = qt * 64, min(T, qt * 64 + 64)
+                tq = np.arange(q0, q1)
+                for j in lists[ib, ih, qt, :counts[ib, ih, qt]]:
+                    if j < 0:
+                        continue
+                    k0, k1 = j * 64, min(T, j * 64 + 64)
+                    if causal:
+                        total += int(np.clip(np.minimum(tq + 1, k1) - k0, 0, None).sum())
+                    else:
+                        total += (q1 - q0) * (k1 - k0)
+    return 4 * 64 * G * total
+
+
+def run_prefill(args, rank, world, local):
+    import torch
+    from local_research_small_language_model_b200 import ModelConfig, ops
+    from local_research_small_language_model_b200.model import SparDAB200Model
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    torch.manual_seed(1234 + rank)
+    T = args.ctx
+    cfg = ModelConfig(block_size=64, top_k_blocks=8, context_length=4096, n_layer=args.layers)
+    model = SparDAB200Model(cfg).to(dev, torch.bfloat16).eval()
+    caches = model.allocate_caches(1, T + 64)
+    gen = torch.Generator(device="cpu").manual_seed(0)
+    ids = torch.randint(0, cfg.vocab_size, (1, T), generator=gen).to(dev)
+    with torch.no_grad():
+        def step():
+            for c in caches:
+                c.reset()
+            return model(ids, kv_caches=caches)["logits"]
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        clocks = ClockSampler(gpu_id_for(local))
+        clocks.start()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+        clock_info = clocks.stop()
+        ms = max_over_ranks_simple(e0.elapsed_time(e1))
+        # the attention kernel alone on one layer's shapes (chunked forecast lists)
+        q = torch.randn(1, T, 12, 64, device=dev, dtype=torch.bfloat16)
+        k = torch.randn(1, 4, T, 64, device=dev, dtype=torch.bfloat16)
+        v = torch.randn(1, 4, T, 64, device=dev, dtype=torch.bfloat16)
+        f = torch.randn(1, T, 4, 64, device=dev, dtype=torch.bfloat16)
+        reps = ops.compress_blocks(k.transpose(1, 2), 64)
+        _, topk = ops.select_blocks(f, reps, 8, 64, False)
+        lists, counts = ops.prefill_lists("chunked_forecast", 1, 4, T, 64, 8, topk, True, device=dev)
+        for _ in range(3):
+            ops.prefill_attention(q, k, v, lists, counts, 64, None, True)
+        torch.cuda.synchronize()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps_n = 10
+        a0.record()
+        for _ in range(reps_n):
+            ops.prefill_attention(q, k, v, lists, counts, 64, None, True)
+        a1.record()
+        torch.cuda.synchronize()
+        att_s = a0.elapsed_time(a1) / 1000.0 / reps_n
+    flops = prefill_flops(lists, counts, T, 3)
+    peak = read_peak_tflops()
+    achieved = flops / att_s / 1e12
+    value = world * args.steps * T / (ms / 1000.0)
+    return {
+        "metric": "prefill tok/s (BASELINE config 3: one 32K-token sequence, 12 layers)", "value": round(value, 1),
+        "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms / args.steps, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"BASELINE config 3: prefill of one {T}-token sequence of uniform random ids, "
+                               "random-init 102.45M model, chunked block-sparse path, block 64, top-k 8",
+                   "seq_len": T, "layers": args.layers},
+        "roofline": {"bound": "tensor", "kernel": "sd::prefill_tc_kernel<bf16> (chunked forecast lists, one layer)",
+                     "achieved": round(achieved, 2), "peak": peak[0], "unit": "TFLOP/s",
+                     "frac": round(achieved / peak[0], 4), "peak_source": peak[1],
+                     "flops_per_launch": flops, "avg_launch_us": round(att_s * 1e6, 2), "traffic": None},
+        "clocks": clock_info,
+    }
+
+
+def max_over_ranks_simple(x):
+    from local_research_small_language_model_b200.sharding import max_over_ranks
+    return max_over_ranks(x)
+
+
+def read_peak_tflops():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as fh:
+            return float(json.load(fh)["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
+
+
 def main():
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -443,9 +553,9 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
     try:
-        res = run_b200(args, rank, world, local)
+        res = run_prefill(args, rank, world, local) if args.prefill else run_b200(args, rank, world, local)
         if rank == 0:
-            if world == 1 and not args.no_cpu_baseline:
+            if world == 1 and not args.no_cpu_baseline and not args.prefill:
                 r = cpu_reference(args.ctx, args.cpu_seqs, args.cpu_budget_s, args.rule)
                 res["cpu_baseline"] = {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")}
             print(json.dumps(res), flush=True)

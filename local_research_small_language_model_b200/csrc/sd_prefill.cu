@@ -257,6 +257,11 @@ extern "C" int sd_prefill_attention(const void *q, int dtype, int64_t B, int64_t
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const float sl2 = scale * sd::kLog2eF;
   const int G = static_cast<int>(Hq / Hkv);
+  // 16-bit inputs run on the tensor cores; fp32 (exact parity) and shapes the
+  // tensor-core kernel does not take run on CUDA cores
+  const int rt = sd::launch_prefill_tc(dtype, G, grid, s, q, q_sb, q_st, q_sh, k, v, c_sb, c_sh, c_st, T, (int)Hkv,
+                                       B, lists, counts, lcap, topk, kk, causal, sl2, out, o_sb, o_st, o_sh);
+  if (rt != SD_ERR_UNSUPPORTED) return rt;
   SD_DISPATCH_DTYPE(dtype, E,
                     return sd::launch_prefill_simt<E>(G, grid, s, q, q_sb, q_st, q_sh, k, v, c_sb, c_sh, c_st, T,
                                                       (int)Hkv, lists, counts, lcap, topk, kk, block_size, causal,

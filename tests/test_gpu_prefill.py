@@ -156,3 +156,32 @@ def test_attention_module_prefill_paths_vs_oracle(dev, dt):
             ref = ref.transpose(0, 2, 1, 3).reshape(b, tt, 768)
             tol = 1e-4 if dt == torch.float32 else 2e-2
             np.testing.assert_allclose(n(out), ref, rtol=0, atol=tol)
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("mode,tt,causal", [("masked_forecast", 700, True), ("masked_forecast", 640, False),
+                                            ("masked_static", 900, True), ("chunked_forecast", 1000, True),
+                                            ("dense", 128, True), ("dense", 100, False)])
+def test_tensor_core_prefill_matches_fp32_path(dev, dt, mode, tt, causal):
+    """The tcgen05 kernel (16-bit inputs) against the CUDA-core kernel run in
+    fp32 on the same rounded inputs and the same lists: max-abs 2e-2 (P is
+    rounded to 16 bits before the PV product)."""
+    b, hq, hkv = 2, 12, 4
+    q = normal((b, tt, hq, 64), seed=41)
+    k = normal((b, hkv, tt, 64), seed=42)
+    v = normal((b, hkv, tt, 64), seed=43)
+    f = normal((b, tt, hkv, 64), seed=44)
+    qd, kd, vd = t(q, dev, dt), t(k, dev, dt), t(v, dev, dt)
+    topk = None
+    if mode in ("masked_forecast", "chunked_forecast"):
+        reps = ops.compress_blocks(kd.float().transpose(1, 2), 64)
+        _, topk = ops.select_blocks(t(f, dev), reps, 8, 64, mode == "masked_forecast" and causal)
+    lists, counts = ops.prefill_lists(mode, b, hkv, tt, 64, 8, topk, causal, device=dev)
+    row_topk = topk if mode == "masked_forecast" else None
+    got = ops.prefill_attention(qd, kd, vd, lists, counts, 64, row_topk, causal)
+    ref = ops.prefill_attention(qd.float(), kd.float(), vd.float(), lists, counts, 64, row_topk, causal)
+    assert torch.isfinite(got.float()).all()
+    np.testing.assert_allclose(n(got), n(ref), rtol=0, atol=2e-2)
+    if mode == "masked_forecast" and causal:
+        oref = O.masked_prefill(n(qd).transpose(0, 2, 1, 3), n(kd), n(vd), f, 64, 8, layer_idx=1)
+        np.testing.assert_allclose(n(got), oref.transpose(0, 2, 1, 3), rtol=0, atol=2e-2)
