@@ -193,7 +193,7 @@ class B200SparseAttention(BaseAttention):
         if kwargs.get("use_chunked_gather", t > 8192):
             causal = True  # the chunked path always clears future blocks (sparse.py:330-346)
             if f is not None:
-                _, topk = self.selector(f, self.compressor(xk), kk, is_causal=False)
+                _, topk = ops.select_blocks(f, self.compressor(xk), kk, bs, False, return_scores=False)
                 mode = "chunked_forecast"
             else:
                 mode = "chunked_static"
@@ -203,7 +203,7 @@ class B200SparseAttention(BaseAttention):
             if nb <= 2 or (self.mode == "forecast" and (f is None or self.layer_idx == 0)):
                 mode = "dense"
             elif self.mode == "forecast":
-                _, topk = self.selector(f, self.compressor(xk), kk, is_causal=is_causal)
+                _, topk = ops.select_blocks(f, self.compressor(xk), kk, bs, is_causal, return_scores=False)
                 mode = "masked_forecast"
             else:
                 mode = "masked_static"

@@ -87,6 +87,136 @@ __global__ void __launch_bounds__(kSelThreads)
   }
 }
 
+// Many-row selector for D = 64 and top-k <= 8 (prefill): a CTA scores 64 rows
+// of one (b, h) against the prototypes in chunks of 128 blocks.  Thread
+// (ty, tx) accumulates a 4-row x 8-block register tile (rows 4ty.., blocks
+// tx + 16c) from float4 shared-memory loads, summing d = 0..63 in order (the
+// same order as select_blocks_kernel); each warp then folds its 8 rows'
+// chunk scores into per-row running top-8 lists with the register tournament
+// (sort_groups / merge_regs / merge_lanes).
+constexpr int kTileRows = 64;
+constexpr int kTileBlocks = 128;
+constexpr int kPitch = 68;  // floats per staged row (16-byte aligned, conflict-free float4 reads)
+
+template <typename T>
+__global__ void __launch_bounds__(256)
+    select_rows_tiled_kernel(const T *__restrict__ fc, int64_t Tq, int H, int64_t f_sb, int64_t f_st,
+                             int64_t f_sh, const float *__restrict__ reps, int64_t NB, int64_t r_sb, int64_t r_sn,
+                             int64_t r_sh, int k, int bs, int causal, int64_t q_offset, float scale,
+                             float *__restrict__ scores_out, int64_t *__restrict__ idx_out) {
+  extern __shared__ __align__(16) float tsm[];
+  float *f_s = tsm;                             // [64][kPitch]
+  float *r_s = f_s + kTileRows * kPitch;        // [128][kPitch]
+  float *s_s = r_s + kTileBlocks * kPitch;      // [64][128 + 1]
+  const int b = blockIdx.z, h = blockIdx.y;
+  const int64_t row0 = static_cast<int64_t>(blockIdx.x) * kTileRows;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int ty = tid >> 4, tx = tid & 15;
+  for (int e = tid; e < kTileRows * 64; e += 256) {
+    const int r = e >> 6, d = e & 63;
+    f_s[r * kPitch + d] = row0 + r < Tq ? to_f(fc[b * f_sb + (row0 + r) * f_st + h * f_sh + d]) : 0.f;
+  }
+  int64_t jmax = NB;  // blocks no row of the tile can see are not scored
+  if (causal) {
+    const int64_t last_row = (Tq - row0 < kTileRows ? Tq - 1 : row0 + kTileRows - 1);
+    const int64_t last = (last_row + q_offset) / bs + 1;
+    jmax = last < NB ? (last > 0 ? last : 0) : NB;
+  }
+  float rv[8];
+  int ri[8];
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    rv[q] = -INFINITY;
+    ri[q] = kNoBlock;
+  }
+  for (int64_t j0 = 0; j0 < NB; j0 += kTileBlocks) {
+    __syncthreads();
+    const bool scored = j0 < jmax;
+    if (scored) {
+      for (int e = tid; e < kTileBlocks * 16; e += 256) {
+        const int jj = e >> 4, c = e & 15;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (j0 + jj < NB) v = *reinterpret_cast<const float4 *>(reps + b * r_sb + (j0 + jj) * r_sn + h * r_sh + 4 * c);
+        *reinterpret_cast<float4 *>(r_s + jj * kPitch + 4 * c) = v;
+      }
+    }
+    __syncthreads();
+    float acc[4][8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int c = 0; c < 8; ++c) acc[i][c] = 0.f;
+    if (scored) {
+#pragma unroll 4
+      for (int d4 = 0; d4 < 16; ++d4) {
+        float4 fq[4], rr[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) fq[i] = *reinterpret_cast<const float4 *>(f_s + (4 * ty + i) * kPitch + 4 * d4);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) rr[c] = *reinterpret_cast<const float4 *>(r_s + (tx + 16 * c) * kPitch + 4 * d4);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            acc[i][c] = fmaf(fq[i].x, rr[c].x, acc[i][c]);
+            acc[i][c] = fmaf(fq[i].y, rr[c].y, acc[i][c]);
+            acc[i][c] = fmaf(fq[i].z, rr[c].z, acc[i][c]);
+            acc[i][c] = fmaf(fq[i].w, rr[c].w, acc[i][c]);
+          }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int r = 4 * ty + i;
+      const int64_t t = row0 + r + q_offset;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const int64_t j = j0 + tx + 16 * c;
+        float v = acc[i][c] * scale;
+        if (!scored || (causal && (t < 0 || j > t / bs))) v = -INFINITY;
+        s_s[r * (kTileBlocks + 1) + tx + 16 * c] = v;
+      }
+    }
+    __syncthreads();
+    if (scores_out) {
+      for (int e = tid; e < kTileRows * kTileBlocks; e += 256) {
+        const int r = e / kTileBlocks, jj = e - r * kTileBlocks;
+        if (row0 + r < Tq && j0 + jj < NB)
+          scores_out[((static_cast<int64_t>(b) * H + h) * Tq + row0 + r) * NB + j0 + jj] =
+              s_s[r * (kTileBlocks + 1) + jj];
+      }
+    }
+    // fold the chunk into the running top-8 of each of this warp's 8 rows
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int r = warp * 8 + q;
+      float cv[4];
+      int ci[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int jj = lane + 32 * u;
+        const int64_t j = j0 + jj;
+        const float v = s_s[r * (kTileBlocks + 1) + jj];
+        const bool ok = j < NB && v == v;
+        cv[u] = ok ? v : -INFINITY;
+        ci[u] = ok ? static_cast<int>(j) : kNoBlock;
+        sort_groups<8>(cv[u], ci[u]);
+      }
+      merge_regs<8>(cv[0], ci[0], cv[1], ci[1]);
+      merge_regs<8>(cv[2], ci[2], cv[3], ci[3]);
+      merge_regs<8>(cv[0], ci[0], cv[2], ci[2]);
+      merge_lanes<8>(cv[0], ci[0]);
+      merge_regs<8>(rv[q], ri[q], cv[0], ci[0]);
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const int64_t row = row0 + warp * 8 + q;
+    if (row < Tq && lane < k)
+      idx_out[((static_cast<int64_t>(b) * H + h) * Tq + row) * k + lane] = ri[q] == kNoBlock ? -1 : ri[q];
+  }
+}
+
 // One warp per row.
 __global__ void topk_rows_kernel(const float *__restrict__ s, int64_t rows, int64_t n, int64_t ld, int k,
                                  int64_t *__restrict__ idx, float *__restrict__ vals) {
@@ -149,6 +279,24 @@ extern "C" int sd_select_blocks(const void *forecast, int f_dtype, int64_t B, in
   if (D < 1 || D > 256) return SD_ERR_UNSUPPORTED;
   const int k = static_cast<int>(top_k < NB ? top_k : NB);
   if (k > 64 || NB > 24576 || B > 65535 || H > 65535) return SD_ERR_UNSUPPORTED;
+  if (D == 64 && k <= 8 && Tq >= sd::kTileRows && (r_sn % 4) == 0 && (r_sb % 4) == 0 && (r_sh % 4) == 0 &&
+      sd::aligned16(reps)) {
+    // many rows: register-tiled scoring and register top-k
+    const size_t tsmem = sizeof(float) * (sd::kTileRows * sd::kPitch + sd::kTileBlocks * sd::kPitch +
+                                          sd::kTileRows * (sd::kTileBlocks + 1));
+    const int64_t tiles = (Tq + sd::kTileRows - 1) / sd::kTileRows;
+    if (tiles > 0x7fffffff) return SD_ERR_UNSUPPORTED;
+    dim3 grid(static_cast<unsigned>(tiles), static_cast<unsigned>(H), static_cast<unsigned>(B));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const float scale = sd::inv_sqrt(D);
+    SD_DISPATCH_DTYPE(f_dtype, E, {
+      auto kern = sd::select_rows_tiled_kernel<E>;
+      if (sd::set_max_smem(kern, tsmem) != SD_OK) return SD_ERR_CUDA;
+      kern<<<grid, 256, tsmem, s>>>(static_cast<const E *>(forecast), Tq, (int)H, f_sb, f_st, f_sh, reps, NB, r_sb,
+                                    r_sn, r_sh, k, block_size, causal, q_offset, scale, scores, topk_idx);
+    });
+    return sd::check_launch();
+  }
   int RT = static_cast<int>(24576 / NB);
   RT = RT > 32 ? 32 : (RT < 1 ? 1 : RT);
   if (RT > Tq) RT = static_cast<int>(Tq);

@@ -137,6 +137,23 @@ def test_selector_large_prefill_rows(dev):
         assert same and frac > 0.9
 
 
+@pytest.mark.parametrize("nb,tq,causal,k", [(300, 1000, False, 8), (300, 1000, True, 8), (129, 200, False, 5)])
+def test_selector_many_blocks_tie_order(dev, nb, tq, causal, k):
+    """Many-row selector over several 128-block chunks (partial last chunk):
+    scores vs the oracle, and indices exactly the top-k of the kernel's own
+    scores under the value-desc / index-asc rule (-inf fills included)."""
+    f = normal((2, tq, 4, 64), seed=21)
+    r = normal((2, nb, 4, 64), seed=22)
+    scores, idx = ops.select_blocks(t(f, dev), t(r, dev), k, 64, causal)
+    ref_s, _ = O.select_blocks(f, r, k, 64, causal)
+    fin = np.isfinite(ref_s)
+    assert np.array_equal(np.isfinite(n(scores)), fin)
+    np.testing.assert_allclose(n(scores)[fin], ref_s[fin], rtol=1e-5, atol=1e-5)
+    np.testing.assert_array_equal(n(idx).astype(np.int64), O.topk_desc(n(scores), k))
+    _, idx2 = ops.select_blocks(t(f, dev), t(r, dev), k, 64, causal, return_scores=False)
+    assert torch.equal(idx, idx2)
+
+
 # ------------------------------------------------------------------ gather
 def test_gather_kv_blocks_vs_oracle(dev):
     k = normal((2, 4, 1000, 64), seed=21)
