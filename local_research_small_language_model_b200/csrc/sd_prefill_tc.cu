@@ -87,6 +87,18 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 2^x for finite x <= 0 on the FMA pipe: x = n + f with n = floor(x), 2^f
+// from a degree-4 least-squares polynomial on [0, 1) (max relative error
+// 2.7e-6, far below the 16-bit rounding of P), 2^n added to the exponent.
+__device__ __forceinline__ float exp2_fma(float x) {
+  x = fmaxf(x, -126.f);
+  const float n = floorf(x);
+  const float f = x - n;
+  const float p =
+      fmaf(fmaf(fmaf(fmaf(0.013520603f, f, 0.052037429f), f, 0.24142750f), f, 0.69300663f), f, 1.0000025f);
+  return __int_as_float(__float_as_int(p) + (static_cast<int>(n) << 23));
+}
+
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 }  // namespace tc
@@ -187,76 +199,97 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
   const uint32_t id_s = idesc_f16(fmt, false), id_pv = idesc_f16(fmt, true);
   bool ok = true;
 
+  // a warp whose 32 rows are all padding (missing heads, rows past T) skips
+  // the TMEM reads and the softmax; its P rows stay garbage and only feed
+  // output rows that are never read
+  const bool warp_active = __any_sync(0xffffffffu, row_ok);
+  auto issue_s = [&](int i) {  // thread 0: S = Q K^T for list entry i
+    const int s = i % kStages;
+    const bool got = mbar_wait_bounded(&full[s], (i / kStages) & 1);
+    fence_after_sync();
+    const uint32_t kaddr = smem_u32(sm + Smem::kK + s * kKvBytes);
+#pragma unroll
+    for (int xx = 0; xx < 2; ++xx) {
+      const uint32_t qaddr = smem_u32(sm + Smem::kQ + xx * kTileBytes);
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        mma_f16(tmem + 64 * xx, umma_desc_sw128(qaddr + 32 * k, 16, 1024), umma_desc_sw128(kaddr + 32 * k, 16, 1024),
+                id_s, k > 0);
+    }
+    mma_commit(s_bar);
+    return got;
+  };
+  if (tid == 0 && cnt > 0) ok = issue_s(0);
+
   for (int i = 0; i < cnt; ++i) {
     const int s = i % kStages;
     const int j = block_of(i);
-    // S = Q K^T
-    if (tid == 0) {
-      ok = mbar_wait_bounded(&full[s], (i / kStages) & 1);
-      fence_after_sync();
-      const uint32_t kaddr = smem_u32(sm + Smem::kK + s * kKvBytes);
-#pragma unroll
-      for (int xx = 0; xx < 2; ++xx) {
-        const uint32_t qaddr = smem_u32(sm + Smem::kQ + xx * kTileBytes);
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-          mma_f16(tmem + 64 * xx, umma_desc_sw128(qaddr + 32 * k, 16, 1024), umma_desc_sw128(kaddr + 32 * k, 16, 1024),
-                  id_s, k > 0);
-      }
-      mma_commit(s_bar);
-    }
     ok = mbar_wait_bounded(s_bar, i & 1) && ok;
     fence_after_sync();
-    // softmax of this row's 64 scores
-    float sc[64];
+    float alpha = 1.f;
+    if (warp_active) {
+      // softmax of this row's 64 scores
+      float sc[64];
 #pragma unroll
-    for (int c4 = 0; c4 < 4; ++c4) {
-      float v[16];
-      tmem_ld16(t_s + 16 * c4, v);
+      for (int c4 = 0; c4 < 4; ++c4) {
+        float v[16];
+        tmem_ld16(t_s + 16 * c4, v);
 #pragma unroll
-      for (int u = 0; u < 16; ++u) sc[16 * c4 + u] = v[u];
-    }
-    tmem_wait_ld();
-    bool blk_ok = row_ok && j >= 0;
-    if (blk_ok && use_rk) {  // masked forecast rows: per-row membership (sparse.py:243-247)
-      bool in = (j == 0) || (j == bq);
-#pragma unroll
-      for (int e = 0; e < kMaxKK; ++e) in = in || (rk[e] == j);
-      blk_ok = in;
-    }
-    const int64_t k0 = static_cast<int64_t>(j) * 64;
-    float mt = -INFINITY;
-#pragma unroll
-    for (int c = 0; c < 64; ++c) {
-      const bool v = blk_ok && k0 + c < T_ && (!causal || k0 + c <= t);
-      sc[c] = v ? sc[c] * scale_log2 : -INFINITY;
-      mt = fmaxf(mt, sc[c]);
-    }
-    const float mn = fmaxf(m, mt);
-    const float alpha = mn == -INFINITY ? 1.f : exp2f(m - mn);
-    float ps = 0.f;
-    char *prow = sm + Smem::kP + x * kTileBytes;
-#pragma unroll
-    for (int c8 = 0; c8 < 8; ++c8) {
-      float p[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        p[u] = sc[8 * c8 + u] == -INFINITY ? 0.f : exp2f(sc[8 * c8 + u] - mn);
-        ps += p[u];
+        for (int u = 0; u < 16; ++u) sc[16 * c4 + u] = v[u];
       }
-      uint4 w;
-      w.x = pack2<T>(p[0], p[1]);
-      w.y = pack2<T>(p[2], p[3]);
-      w.z = pack2<T>(p[4], p[5]);
-      w.w = pack2<T>(p[6], p[7]);
-      *reinterpret_cast<uint4 *>(prow + sw128(r, c8)) = w;
+      tmem_wait_ld();
+      bool blk_ok = row_ok && j >= 0;
+      if (blk_ok && use_rk) {  // masked forecast rows: per-row membership (sparse.py:243-247)
+        bool in = (j == 0) || (j == bq);
+#pragma unroll
+        for (int e = 0; e < kMaxKK; ++e) in = in || (rk[e] == j);
+        blk_ok = in;
+      }
+      // keys k0 .. k0 + nv - 1 of this block are visible to this row
+      int nv = 0;
+      if (blk_ok) {
+        const int k0 = j * 64;
+        int lim = static_cast<int>(T_) - k0;
+        if (causal) {
+          const int lc = static_cast<int>(t) - k0 + 1;
+          lim = lc < lim ? lc : lim;
+        }
+        nv = lim < 0 ? 0 : (lim > 64 ? 64 : lim);
+      }
+      float mt = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 64; ++c) mt = fmaxf(mt, c < nv ? sc[c] : -INFINITY);
+      const float mn = fmaxf(m, mt * scale_log2);  // scale_log2 > 0: max of the scaled scores
+      alpha = mn == -INFINITY ? 1.f : exp2f(m - mn);
+      float ps = 0.f;
+      char *prow = sm + Smem::kP + x * kTileBytes;
+#pragma unroll
+      for (int c8 = 0; c8 < 8; ++c8) {
+        float p[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int c = 8 * c8 + u;
+          const float z = fmaf(sc[c], scale_log2, -mn);
+          // half of the exponentials on the FMA pipe, half on the SFU
+          const float e = (u & 1) ? exp2_fma(z) : exp2f(z);
+          p[u] = c < nv ? e : 0.f;
+          ps += p[u];
+        }
+        uint4 w;
+        w.x = pack2<T>(p[0], p[1]);
+        w.y = pack2<T>(p[2], p[3]);
+        w.z = pack2<T>(p[4], p[5]);
+        w.w = pack2<T>(p[6], p[7]);
+        *reinterpret_cast<uint4 *>(prow + sw128(r, c8)) = w;
+      }
+      l = l * alpha + ps;
+      m = mn;
     }
-    l = l * alpha + ps;
-    m = mn;
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     fence_before_sync();
     __syncthreads();
-    // PV = P V  (V tile MN-major: 64 keys of 128-byte rows)
+    // PV = P V (V tile MN-major: 64 keys of 128-byte rows), then the next
+    // block's S = Q K^T right behind it (S was read out above)
     if (tid == 0) {
       fence_after_sync();
       const uint32_t vaddr = smem_u32(sm + Smem::kV + s * kKvBytes);
@@ -269,17 +302,20 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
                   umma_desc_sw128(vaddr + 2048 * k, kKvBytes, 1024), id_pv, k > 0);
       }
       mma_commit(o_bar);
+      if (i + 1 < cnt) ok = issue_s(i + 1) && ok;
     }
     ok = mbar_wait_bounded(o_bar, i & 1) && ok;
     fence_after_sync();
+    if (warp_active) {
 #pragma unroll
-    for (int c4 = 0; c4 < 4; ++c4) {
-      float v[16];
-      tmem_ld16(t_pv + 16 * c4, v);
+      for (int c4 = 0; c4 < 4; ++c4) {
+        float v[16];
+        tmem_ld16(t_pv + 16 * c4, v);
 #pragma unroll
-      for (int u = 0; u < 16; ++u) o[16 * c4 + u] = fmaf(o[16 * c4 + u], alpha, v[u]);
+        for (int u = 0; u < 16; ++u) o[16 * c4 + u] = fmaf(o[16 * c4 + u], alpha, v[u]);
+      }
+      tmem_wait_ld();
     }
-    tmem_wait_ld();
     fence_before_sync();
     // stage s is free again (both MMAs that read it completed): refill it
     if (__syncthreads_or(!ok)) break;
