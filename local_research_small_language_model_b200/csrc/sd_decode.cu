@@ -3,8 +3,10 @@
 //
 // Work split: one CTA (4 warps) per (sequence, kv head).  The selected KV
 // blocks are cut into tiles of at most 64 cached rows of ONE block, staged into
-// shared memory through a 6-stage ring completed on mbarriers, so up to 6
-// tiles (K and V) are in flight per CTA while earlier ones are consumed.
+// shared memory through a 4-stage ring completed on mbarriers, so up to 4
+// tiles (K and V) are in flight per CTA while earlier ones are consumed.  (Four
+// stages keep two CTAs per SM with room left for the side-stream candidate
+// kernel that runs concurrently inside a decode step.)
 //
 // Two staging/compute paths:
 //   * 16-bit caches whose rows are contiguous (the block-major cache of this
@@ -31,7 +33,7 @@ namespace sd {
 
 constexpr int kD = 64;          // head_dim the attention kernels implement
 constexpr int kRows = 64;       // rows per tile
-constexpr int kStages = 6;
+constexpr int kStages = 4;
 constexpr int kThreads = 128;
 constexpr int kWarps = kThreads / 32;
 constexpr int kMaxTiles = 256;
