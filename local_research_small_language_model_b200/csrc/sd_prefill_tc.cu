@@ -7,15 +7,16 @@
 // query heads of the kv head give 64*G query rows, laid out as two 128-row
 // MMA tiles (tile x holds heads 2x and 2x+1; missing heads are zero rows).
 // For every listed key block (64 keys, staged by TMA with 128-byte swizzle in
-// a 3-deep ring):
+// a 3-deep ring shared by the two tiles), each tile's warpgroup runs its own
+// pipeline (ping-pong: one tile's softmax overlaps the other's MMAs):
 //   S_x = Q_x K^T       tcgen05.mma M=128 N=64 K=64 (4 instructions), fp32 in TMEM
 //   softmax             one thread per query row: tcgen05.ld of its 64 scores,
 //                       masks (block membership, causality, length), online
 //                       max/sum in fp32, P row -> 16-bit -> swizzled smem
 //   PV_x = P_x V        tcgen05.mma M=128 N=64 K=64 with V MN-major, into TMEM
 //   O_x = O_x*alpha+PV  in registers after a tcgen05.ld of the row
-// Single thread 0 issues the MMAs and commits them to mbarriers; every wait is
-// bounded.  TMEM: 256 columns (S0, S1, PV0, PV1) per CTA, <= 2 CTAs per SM.
+// The first thread of each warpgroup issues its tile's MMAs and commits them
+// to that tile's mbarriers; every wait is bounded.  TMEM: 256 columns (S0, S1, PV0, PV1) per CTA, <= 2 CTAs per SM.
 #include <type_traits>
 
 #include "sd_prefill.cuh"
@@ -40,7 +41,7 @@ struct Smem {
   static constexpr int kK = kP + 2 * kTileBytes;        // kStages tiles
   static constexpr int kV = kK + kStages * kKvBytes;    // kStages tiles
   static constexpr int kBar = kV + kStages * kKvBytes;  // mbarriers
-  static constexpr int kBytes = kBar + 128;
+  static constexpr int kBytes = kBar + 256;
 };
 
 __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
@@ -87,16 +88,13 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// 2^x for finite x <= 0 on the FMA pipe: x = n + f with n = floor(x), 2^f
-// from a degree-4 least-squares polynomial on [0, 1) (max relative error
-// 2.7e-6, far below the 16-bit rounding of P), 2^n added to the exponent.
-__device__ __forceinline__ float exp2_fma(float x) {
-  x = fmaxf(x, -126.f);
-  const float n = floorf(x);
-  const float f = x - n;
-  const float p =
-      fmaf(fmaf(fmaf(fmaf(0.013520603f, f, 0.052037429f), f, 0.24142750f), f, 0.69300663f), f, 1.0000025f);
-  return __int_as_float(__float_as_int(p) + (static_cast<int>(n) << 23));
+// 2^x with the SFU's approximate base-2 exponential (one instruction;
+// 2^-inf = +0, so masked keys need no select).  The kernel is issue-bound,
+// so the cheapest form per element wins.
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
@@ -114,9 +112,10 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
   extern __shared__ __align__(1024) char smem_raw[];
   char *sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t *full = reinterpret_cast<uint64_t *>(sm + Smem::kBar);  // [kStages]
-  uint64_t *s_bar = full + kStages;
-  uint64_t *o_bar = s_bar + 1;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(o_bar + 1);
+  uint64_t *s_bar = full + kStages;  // [2]: S of tile x ready
+  uint64_t *o_bar = s_bar + 2;       // [2]: PV of tile x ready
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(o_bar + 2);
+  int *refill = reinterpret_cast<int *>(tmem_slot + 1);  // [kStages]: tiles done with the stage
   const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int nqt = gridDim.x;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -130,9 +129,14 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   if (tid == 32) {
-    for (int s = 0; s < kStages; ++s) mbar_init(&full[s], 1);
-    mbar_init(s_bar, 1);
-    mbar_init(o_bar, 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      refill[s] = 0;
+    }
+    for (int xx = 0; xx < 2; ++xx) {
+      mbar_init(&s_bar[xx], 1);
+      mbar_init(&o_bar[xx], 1);
+    }
     mbar_init_fence();
   }
   const int64_t lrow = (static_cast<int64_t>(b) * Hkv + h) * nqt + qt;
@@ -158,15 +162,27 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
     for (int i = 0; i < cnt && i < kStages; ++i) issue(i);
 
   // ---- Q tiles: rows r of tile x = head 2x + r/64, token qt*64 + r%64
-  for (int e = tid; e < 2 * kRowsTile * 8; e += kThreads) {
-    const int x = e / (kRowsTile * 8), rem = e - x * kRowsTile * 8;
-    const int r = rem >> 3, c = rem & 7;
-    const int g = 2 * x + (r >> 6);
-    const int64_t t = static_cast<int64_t>(qt) * 64 + (r & 63);
-    uint4 val = make_uint4(0u, 0u, 0u, 0u);
-    if (g < G && t < T_)
-      val = *reinterpret_cast<const uint4 *>(q + b * q_sb + t * q_st + static_cast<int64_t>(h * G + g) * q_sh + 8 * c);
-    *reinterpret_cast<uint4 *>(sm + Smem::kQ + x * kTileBytes + sw128(r, c)) = val;
+  {
+    constexpr int kPer = 2 * kRowsTile * 8 / kThreads;  // 16-byte chunks per thread
+    uint4 val[kPer];
+#pragma unroll
+    for (int u = 0; u < kPer; ++u) {  // all loads in flight before any store
+      const int e = tid + u * kThreads;
+      const int x = e / (kRowsTile * 8), rem = e - x * kRowsTile * 8;
+      const int r = rem >> 3, c = rem & 7;
+      const int g = 2 * x + (r >> 6);
+      const int64_t t = static_cast<int64_t>(qt) * 64 + (r & 63);
+      val[u] = make_uint4(0u, 0u, 0u, 0u);
+      if (g < G && t < T_)
+        val[u] = *reinterpret_cast<const uint4 *>(q + b * q_sb + t * q_st + static_cast<int64_t>(h * G + g) * q_sh +
+                                                  8 * c);
+    }
+#pragma unroll
+    for (int u = 0; u < kPer; ++u) {
+      const int e = tid + u * kThreads;
+      const int x = e / (kRowsTile * 8), rem = e - x * kRowsTile * 8;
+      *reinterpret_cast<uint4 *>(sm + Smem::kQ + x * kTileBytes + sw128(rem >> 3, rem & 7)) = val[u];
+    }
   }
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   __syncthreads();
@@ -203,28 +219,43 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
   // the TMEM reads and the softmax; its P rows stay garbage and only feed
   // output rows that are never read
   const bool warp_active = __any_sync(0xffffffffu, row_ok);
-  auto issue_s = [&](int i) {  // thread 0: S = Q K^T for list entry i
+  // Ping-pong: the warpgroup of tile x (warps 4x..4x+3) runs its own
+  // pipeline with its own barriers and MMA-issuing thread (its first thread),
+  // so one tile's softmax overlaps the other tile's tensor-core work.  The two
+  // tiles share the K/V ring; the second tile to finish with a stage refills it.
+  const bool leader = (tid & 127) == 0;
+  const uint32_t bar_id = 1 + x;  // named barrier of this warpgroup (0 is __syncthreads)
+  auto wg_sync = [&]() { asm volatile("bar.sync %0, 128;" ::"r"(bar_id) : "memory"); };
+  auto wg_any = [&](bool pred) {
+    uint32_t res;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 q, %1, 0;\n\tbar.red.or.pred p, %2, 128, q;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(res)
+        : "r"(pred ? 1u : 0u), "r"(bar_id)
+        : "memory");
+    return res != 0;
+  };
+  const uint32_t qaddr = smem_u32(sm + Smem::kQ + x * kTileBytes);
+  const uint32_t paddr = smem_u32(sm + Smem::kP + x * kTileBytes);
+  auto issue_s = [&](int i) {  // leader: S_x = Q_x K^T for list entry i
     const int s = i % kStages;
     const bool got = mbar_wait_bounded(&full[s], (i / kStages) & 1);
     fence_after_sync();
     const uint32_t kaddr = smem_u32(sm + Smem::kK + s * kKvBytes);
 #pragma unroll
-    for (int xx = 0; xx < 2; ++xx) {
-      const uint32_t qaddr = smem_u32(sm + Smem::kQ + xx * kTileBytes);
-#pragma unroll
-      for (int k = 0; k < 4; ++k)
-        mma_f16(tmem + 64 * xx, umma_desc_sw128(qaddr + 32 * k, 16, 1024), umma_desc_sw128(kaddr + 32 * k, 16, 1024),
-                id_s, k > 0);
-    }
-    mma_commit(s_bar);
+    for (int k = 0; k < 4; ++k)
+      mma_f16(tmem + 64 * x, umma_desc_sw128(qaddr + 32 * k, 16, 1024), umma_desc_sw128(kaddr + 32 * k, 16, 1024),
+              id_s, k > 0);
+    mma_commit(&s_bar[x]);
     return got;
   };
-  if (tid == 0 && cnt > 0) ok = issue_s(0);
+  if (leader && cnt > 0) ok = issue_s(0);
 
   for (int i = 0; i < cnt; ++i) {
     const int s = i % kStages;
     const int j = block_of(i);
-    ok = mbar_wait_bounded(s_bar, i & 1) && ok;
+    ok = mbar_wait_bounded(&s_bar[x], i & 1) && ok;
     fence_after_sync();
     float alpha = 1.f;
     if (warp_active) {
@@ -256,11 +287,16 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
         }
         nv = lim < 0 ? 0 : (lim > 64 ? 64 : lim);
       }
-      float mt = -INFINITY;
+      if (nv < 64) {  // partial or masked block (rare): hide the invisible keys
 #pragma unroll
-      for (int c = 0; c < 64; ++c) mt = fmaxf(mt, c < nv ? sc[c] : -INFINITY);
+        for (int c = 0; c < 64; ++c) sc[c] = c < nv ? sc[c] : -INFINITY;
+      }
+      float mt = sc[0];
+#pragma unroll
+      for (int c = 1; c < 64; ++c) mt = fmaxf(mt, sc[c]);
       const float mn = fmaxf(m, mt * scale_log2);  // scale_log2 > 0: max of the scaled scores
-      alpha = mn == -INFINITY ? 1.f : exp2f(m - mn);
+      alpha = mn == -INFINITY ? 1.f : ex2(m - mn);
+      const float nmn = mn == -INFINITY ? 0.f : -mn;  // rows with nothing visible yet keep p = 0
       float ps = 0.f;
       char *prow = sm + Smem::kP + x * kTileBytes;
 #pragma unroll
@@ -268,11 +304,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
         float p[8];
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
-          const int c = 8 * c8 + u;
-          const float z = fmaf(sc[c], scale_log2, -mn);
-          // half of the exponentials on the FMA pipe, half on the SFU
-          const float e = (u & 1) ? exp2_fma(z) : exp2f(z);
-          p[u] = c < nv ? e : 0.f;
+          p[u] = ex2(fmaf(sc[8 * c8 + u], scale_log2, nmn));
           ps += p[u];
         }
         uint4 w;
@@ -287,24 +319,20 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
     }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     fence_before_sync();
-    __syncthreads();
-    // PV = P V (V tile MN-major: 64 keys of 128-byte rows), then the next
-    // block's S = Q K^T right behind it (S was read out above)
-    if (tid == 0) {
+    wg_sync();
+    // PV_x = P_x V (V tile MN-major: 64 keys of 128-byte rows), then the next
+    // block's S_x right behind it (S_x was read out above)
+    if (leader) {
       fence_after_sync();
       const uint32_t vaddr = smem_u32(sm + Smem::kV + s * kKvBytes);
 #pragma unroll
-      for (int xx = 0; xx < 2; ++xx) {
-        const uint32_t paddr = smem_u32(sm + Smem::kP + xx * kTileBytes);
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-          mma_f16(tmem + 128 + 64 * xx, umma_desc_sw128(paddr + 32 * k, 16, 1024),
-                  umma_desc_sw128(vaddr + 2048 * k, kKvBytes, 1024), id_pv, k > 0);
-      }
-      mma_commit(o_bar);
+      for (int k = 0; k < 4; ++k)
+        mma_f16(tmem + 128 + 64 * x, umma_desc_sw128(paddr + 32 * k, 16, 1024),
+                umma_desc_sw128(vaddr + 2048 * k, kKvBytes, 1024), id_pv, k > 0);
+      mma_commit(&o_bar[x]);
       if (i + 1 < cnt) ok = issue_s(i + 1) && ok;
     }
-    ok = mbar_wait_bounded(o_bar, i & 1) && ok;
+    ok = mbar_wait_bounded(&o_bar[x], i & 1) && ok;
     fence_after_sync();
     if (warp_active) {
 #pragma unroll
@@ -317,11 +345,16 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
       tmem_wait_ld();
     }
     fence_before_sync();
-    // stage s is free again (both MMAs that read it completed): refill it
-    if (__syncthreads_or(!ok)) break;
-    if (tid == 0 && i + kStages < cnt) issue(i + kStages);
+    // both MMAs of this tile that read stage s are complete: the second tile
+    // to get here refills the stage
+    if (leader && atomicAdd(&refill[s], 1) == 1) {
+      refill[s] = 0;
+      if (i + kStages < cnt) issue(i + kStages);
+    }
+    if (wg_any(!ok)) break;
   }
-  if (!ok) {  // a bounded wait expired: let copies in flight land, poison the rows
+  const bool failed = __syncthreads_or(!ok);
+  if (failed) {  // a bounded wait expired: let copies in flight land, poison the rows
     if (tid == 0)
       for (int s = 0; s < kStages; ++s) mbar_wait_bounded(&full[s], 0, 1000000ull);
     l = __int_as_float(0x7fc00000);
