@@ -36,6 +36,45 @@ __global__ void rmsnorm_kernel(const T *__restrict__ x, int64_t x_rs, const T *_
   }
 }
 
+// Same arithmetic for many rows (prefill): one warp per row, 16-byte vector
+// loads and stores, no block-wide reductions.
+template <typename T>
+__global__ void __launch_bounds__(256) rmsnorm_rows_kernel(const T *__restrict__ x, int64_t x_rs,
+                                                           const T *__restrict__ w, int C, float eps,
+                                                           T *__restrict__ out, int64_t o_rs, int64_t rows) {
+  constexpr int kE = 16 / static_cast<int>(sizeof(T));  // elements per 16-byte chunk
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const uint4 *xr = reinterpret_cast<const uint4 *>(x + row * x_rs);
+  const uint4 *wr = reinterpret_cast<const uint4 *>(w);
+  uint4 *orow = reinterpret_cast<uint4 *>(out + row * o_rs);
+  const int nv = C / kE;
+  float ss = 0.f;
+  for (int c = lane; c < nv; c += 32) {
+    const uint4 u = xr[c];
+    const T *e = reinterpret_cast<const T *>(&u);
+#pragma unroll
+    for (int i = 0; i < kE; ++i) {
+      const float v = to_f(e[i]);
+      ss = fmaf(v, v, ss);
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  const float r = rsqrtf(ss / static_cast<float>(C) + eps);
+  for (int c = lane; c < nv; c += 32) {
+    const uint4 u = xr[c], g = wr[c];
+    const T *e = reinterpret_cast<const T *>(&u);
+    const T *ge = reinterpret_cast<const T *>(&g);
+    uint4 o;
+    T *oe = reinterpret_cast<T *>(&o);
+#pragma unroll
+    for (int i = 0; i < kE; ++i) oe[i] = from_f<T>(round_to<T>(to_f(e[i]) * r) * to_f(ge[i]));
+    orow[c] = o;
+  }
+}
+
 // gu rows hold [gate | up] (2F values); out = T(T(silu(gate)) * up).
 template <typename T>
 __global__ void silu_mul_kernel(const T *__restrict__ gu, int64_t g_rs, int F, T *__restrict__ out,
@@ -56,6 +95,16 @@ extern "C" int sd_rmsnorm(const void *x, int dtype, int64_t rows, int64_t C, int
   if (!x || !w || !out || rows <= 0 || C <= 0) return SD_ERR_INVALID;
   if (rows > 0x7fffffff) return SD_ERR_UNSUPPORTED;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int es = sd::dtype_size(dtype);
+  if (rows >= 512 && (C * es) % 16 == 0 && (x_rs * es) % 16 == 0 && (o_rs * es) % 16 == 0 && sd::aligned16(x) &&
+      sd::aligned16(w) && sd::aligned16(out)) {
+    const unsigned grid = static_cast<unsigned>((rows + 7) / 8);
+    SD_DISPATCH_DTYPE(dtype, E,
+                      sd::rmsnorm_rows_kernel<E><<<grid, 256, 0, s>>>(static_cast<const E *>(x), x_rs,
+                                                                      static_cast<const E *>(w), (int)C, eps,
+                                                                      static_cast<E *>(out), o_rs, rows));
+    return sd::check_launch();
+  }
   const int threads = C >= 1024 ? 1024 : static_cast<int>(((C + 31) / 32) * 32);
   SD_DISPATCH_DTYPE(dtype, E,
                     sd::rmsnorm_kernel<E><<<static_cast<unsigned>(rows), threads, 0, s>>>(

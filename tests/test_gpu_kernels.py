@@ -331,9 +331,11 @@ def test_decode_layer_rope_bitexact_bf16(dev):
 
 # ------------------------------------------------------------------ decode-step row kernels
 @pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
-def test_rmsnorm_matches_reference_formula(dev, dt):
-    """model/norm.py:15-21: fp32 normalisation, cast, gain multiply in dtype."""
-    x = t(normal((64, 768), seed=1), dev, dt)
+@pytest.mark.parametrize("rows", [64, 1000])
+def test_rmsnorm_matches_reference_formula(dev, dt, rows):
+    """model/norm.py:15-21: fp32 normalisation, cast, gain multiply in dtype
+    (64 rows: block-per-row kernel; 1000 rows: warp-per-row kernel)."""
+    x = t(normal((rows, 768), seed=1), dev, dt)
     w = t(1.0 + 0.1 * normal((768,), seed=2), dev, dt)
     ref = (x.float() * torch.rsqrt(x.float().pow(2).mean(-1, keepdim=True) + 1e-6)).type_as(x) * w
     got = ops.rmsnorm(x, w, 1e-6)
