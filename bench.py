@@ -54,9 +54,9 @@ def parse():
     ap.add_argument("--offload", action="store_true",
                     help="BASELINE config 5 sample: K/V rows in pinned host memory, forecast-guided prefetch of the "
                          "selected blocks into device slots (use with e.g. --ctx 32768)")
-    ap.add_argument("--selection", choices=["kernel", "side-stream"], default="side-stream",
-                    help="forecast selection inside the fused decode kernel, or layer L+1's candidates computed on a "
-                         "side stream during layer L")
+    ap.add_argument("--selection", choices=["kernel", "side-stream", "chain"], default="chain",
+                    help="forecast selection inside the fused decode kernel, layer L+1's candidates computed on a "
+                         "side stream during layer L, or at the end of layer L's fused kernel")
     ap.add_argument("--e2e-steps", type=int, default=1024)
     ap.add_argument("--probe-steps", type=int, default=64)
     ap.add_argument("--cpu-seqs", type=int, default=2)
@@ -207,8 +207,7 @@ def run_b200(args, rank, world, local):
     cfg = ModelConfig(block_size=64, top_k_blocks=8, context_length=4096, selector_rule=args.rule,
                       n_layer=args.layers)
     model = SparDAB200Model(cfg).to(dev, torch.bfloat16).eval()
-    caches = model.allocate_caches(B, ctx + W + 64, overlap_selection=args.selection == "side-stream",
-                                   offload=args.offload)
+    caches = model.allocate_caches(B, ctx + W + 64, selection=args.selection, offload=args.offload)
     gen = torch.Generator(device=dev)
     gen.manual_seed(99 + rank)
     with torch.no_grad():
@@ -319,6 +318,7 @@ def run_b200(args, rank, world, local):
 
         # ---- roofline of the fused decode kernel (instrumented graph)
         side = args.selection == "side-stream"
+        chain = args.selection == "chain"
         k_ms, k_bytes, k_launch = 0.0, 0.0, 0
         w_ms = 0.0
         c_ms, c_bytes, c_launch = 0.0, 0.0, 0
@@ -345,7 +345,9 @@ def run_b200(args, rank, world, local):
                             + B * 4 * 64 * 2 * 2         # new K and V rows written
                             + B * 4 * 64 * 4 * 2)        # current block's running sum read + write
                 if li > 0:  # forecast-driven layers
-                    k_bytes += B * 4 * 8 * 8 if side else B * 4 * n_sc * 64 * 4  # candidates, or every fp32 sum
+                    k_bytes += B * 4 * 8 * 8 if (side or chain) else B * 4 * n_sc * 64 * 4  # candidates, or sums
+                if chain and li + 1 < len(probes):  # the next layer's candidates, computed by this kernel
+                    k_bytes += B * 4 * (n_sc * 64 * 4 + 64 * 2 + 8 * 8)
                 if (side or args.offload) and li + 1 < len(probes):  # layer li+1's candidates (+ prefetch)
                     c_ms += p["cstart"].elapsed_time(p["cend"])
                     c_launch += 1

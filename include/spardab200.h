@@ -159,7 +159,12 @@ SD_API int sd_kv_append(const void *xk, const void *xv, int dtype, int64_t B, in
  * prototype itself (same result).
  * sel_out/cnt_out (nullable, together): the selected block list of every
  * (sequence, kv head), int32 [B,Hkv,sel_cap] ascending and -1 padded, and its
- * length int32 [B,Hkv]; sel_cap >= top_k + 2. */
+ * length int32 [B,Hkv]; sel_cap >= top_k + 2.
+ * next_* (nullable, together; top_k <= 32): the next layer's block sums, its
+ * forecast rows (this layer's forecast projection, activation dtype, row
+ * stride next_f_sb) and its candidate outputs [B,Hkv,top_k]: the kernel ends
+ * by computing what sd_decode_candidates would for the next layer's coming
+ * step, with no separate launch or stream. */
 SD_API int sd_decode_layer(const void *qkv, int dtype, int64_t qkv_sb, const void *forecast,
                     int f_dtype, int64_t f_sb, const float *rope_cos, const float *rope_sin,
                     int64_t max_pos, const int32_t *cur_len, void *k_cache, void *v_cache,
@@ -167,7 +172,8 @@ SD_API int sd_decode_layer(const void *qkv, int dtype, int64_t qkv_sb, const voi
                     int64_t Tcap, int64_t NBcap, int block_size, int top_k, int rule,
                     float scale, void *out, int64_t o_sb, const int32_t *cand_idx,
                     const float *cand_val, int32_t *sel_out, int32_t *cnt_out, int sel_cap,
-                    int32_t *err, void *stream);
+                    int32_t *err, const float *next_proto_sum, const void *next_forecast,
+                    int64_t next_f_sb, int32_t *next_cand_idx, float *next_cand_val, void *stream);
 
 /* Forecast candidates for the next decode step of one layer, computed ahead
  * of time (e.g. on a side stream while the previous layer runs): the top-k

@@ -44,7 +44,8 @@ _SIGS = {
                      _c_void_p, _i64, _i64, _i64, _i32, _c_void_p],
     "sd_decode_layer": [_c_void_p, _i32, _i64, _c_void_p, _i32, _i64, _c_void_p, _c_void_p, _i64, _c_void_p,
                         _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _i32, _i32, _f32,
-                        _c_void_p, _i64, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _c_void_p, _c_void_p],
+                        _c_void_p, _i64, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _c_void_p,
+                        _c_void_p, _c_void_p, _i64, _c_void_p, _c_void_p, _c_void_p],
     "sd_decode_candidates": [_c_void_p, _i32, _i64, _c_void_p, _i64, _i64, _i64, _i64, _c_void_p, _i32, _i32, _i32,
                              _f32, _c_void_p, _c_void_p, _c_void_p],
     "sd_prefill_lists": [_i32, _i32, _i64, _i64, _i64, _i32, _i32, _c_void_p, _i32, _c_void_p, _c_void_p, _i32,

@@ -564,6 +564,18 @@ struct LayerTail {
 // 2 + kslots blocks: slot 0 the sink block, slot 1 the block being written,
 // slots 2.. the blocks a prefetch staged for this step.  host_k == nullptr
 // means a plain device cache.
+// The next layer's candidates, computed at the end of this layer's kernel
+// (what sd_decode_candidates computes on a side stream): the next layer's
+// running block sums do not change until its own step, and its forecast is
+// this layer's projection.  proto == nullptr: not requested.
+struct NextCand {
+  const float *proto = nullptr;
+  const void *fc = nullptr;  // forecast rows, activation dtype, row stride f_sb
+  int64_t f_sb = 0;
+  int32_t *cand_idx = nullptr;
+  float *cand_val = nullptr;
+};
+
 template <typename T> struct SlotMap {
   T *host_k = nullptr, *host_v = nullptr;
   int64_t host_tcap = 0;
@@ -580,7 +592,8 @@ __global__ void __launch_bounds__(kThreads)
                         float scale_log2, const __grid_constant__ CUtensorMap tmk,
                         const __grid_constant__ CUtensorMap tmv, T *__restrict__ out, int64_t o_sb,
                         const int32_t *__restrict__ cand_idx, const float *__restrict__ cand_val,
-                        int32_t *sel_out, int32_t *cnt_out, int sel_cap, int32_t *err, const SlotMap<T> sm) {
+                        int32_t *sel_out, int32_t *cnt_out, int sel_cap, int32_t *err, const SlotMap<T> sm,
+                        const NextCand nx) {
   extern __shared__ __align__(1024) char smem_raw[];
   AttnSmem<T, G> S(smem_raw);
   LayerTail X(S.tail, NBcap, top_k);
@@ -859,6 +872,26 @@ __global__ void __launch_bounds__(kThreads)
     for (int i = threadIdx.x; i < sel_cap; i += blockDim.x) sel_out[bh * sel_cap + i] = i < count ? X.list[i] : -1;
     if (threadIdx.x == 0) cnt_out[bh] = count;
   }
+
+  // -- 5. optional: the next layer's candidates for its coming step (top-k
+  //       over its blocks 0..curr-1; it caches as many tokens as this layer)
+  if (nx.proto != nullptr) {
+    int32_t *oi = nx.cand_idx + bh * top_k;
+    float *ov = nx.cand_val + bh * top_k;
+    if (nb <= ms) {  // its step is dense: no candidates needed
+      for (int r = threadIdx.x; r < top_k; r += blockDim.x) {
+        oi[r] = -1;
+        ov[r] = -INFINITY;
+      }
+    } else {
+      const T *fr = static_cast<const T *>(nx.fc) + b * nx.f_sb + h * kD;
+      const int l16 = threadIdx.x & 15;
+      const float4 fv = make_float4(to_f(fr[4 * l16]), to_f(fr[4 * l16 + 1]), to_f(fr[4 * l16 + 2]),
+                                    to_f(fr[4 * l16 + 3]));
+      const int nsc = rule == SD_RULE_REFERENCE ? 1 : curr;
+      cta_score_topk(nx.proto + bh * NBcap * kD, kD, fv, curr, nsc, -1, sel_scale, top_k, oi, ov);
+    }
+  }
 }
 
 template <typename T>
@@ -916,7 +949,7 @@ int launch_decode_layer(const void *qkv, int64_t qkv_sb, const void *fc, int64_t
                         int64_t Hkv, int64_t Tcap, int64_t NBcap, int bs, int top_k, int rule, float scale,
                         void *out, int64_t o_sb, const int32_t *cand_idx, const float *cand_val,
                         int32_t *sel_out, int32_t *cnt_out, int sel_cap, int32_t *err, cudaStream_t s,
-                        const SlotMap<T> &sm = SlotMap<T>()) {
+                        const SlotMap<T> &sm = SlotMap<T>(), const NextCand &nx = NextCand()) {
   const size_t smem = AttnSmem<T, G>::bytes() + LayerTail::bytes(NBcap, top_k) + kAlignSlack;
   CUtensorMap mk, mv;
   const int r = make_maps<T>(&mk, &mv, kc, vc, B, Hkv, Tcap, kD, Tcap * kD, Hkv * Tcap * kD);
@@ -927,7 +960,7 @@ int launch_decode_layer(const void *qkv, int64_t qkv_sb, const void *fc, int64_t
       static_cast<const T *>(qkv), qkv_sb, static_cast<const F *>(fc), f_sb, rc, rs, cur_len,
       static_cast<T *>(kc), static_cast<T *>(vc), ps, (int)Hkv, Tcap, NBcap, bs, top_k, rule,
       scale / static_cast<float>(bs), scale * kLog2e, mk, mv, static_cast<T *>(out), o_sb, cand_idx, cand_val,
-      sel_out, cnt_out, sel_cap, err, sm);
+      sel_out, cnt_out, sel_cap, err, sm, nx);
   return check_launch();
 }
 
@@ -976,9 +1009,21 @@ extern "C" int sd_decode_layer(const void *qkv, int dtype, int64_t qkv_sb, const
                                int64_t Hq, int64_t Hkv, int64_t D, int64_t Tcap, int64_t NBcap, int block_size,
                                int top_k, int rule, float scale, void *out, int64_t o_sb, const int32_t *cand_idx,
                                const float *cand_val, int32_t *sel_out, int32_t *cnt_out, int sel_cap,
-                               int32_t *err, void *stream) {
+                               int32_t *err, const float *next_proto_sum, const void *next_forecast,
+                               int64_t next_f_sb, int32_t *next_cand_idx, float *next_cand_val, void *stream) {
   if (!qkv || !rope_cos || !rope_sin || !cur_len || !k_cache || !v_cache || !proto_sum || !out)
     return SD_ERR_INVALID;
+  sd::NextCand nx;
+  if (next_proto_sum != nullptr) {
+    if (!next_forecast || !next_cand_idx || !next_cand_val) return SD_ERR_INVALID;
+    if (top_k > 32) return SD_ERR_UNSUPPORTED;
+    if (!sd::aligned16(next_proto_sum)) return SD_ERR_ALIGN;
+    nx.proto = next_proto_sum;
+    nx.fc = next_forecast;
+    nx.f_sb = next_f_sb;
+    nx.cand_idx = next_cand_idx;
+    nx.cand_val = next_cand_val;
+  }
   if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || block_size <= 0 || top_k <= 0 || Tcap <= 0 || NBcap <= 0 ||
       max_pos < Tcap)
     return SD_ERR_INVALID;
@@ -999,12 +1044,12 @@ extern "C" int sd_decode_layer(const void *qkv, int dtype, int64_t qkv_sb, const
                                                                 cur_len, k_cache, v_cache, proto_sum, B, Hkv,
                                                                 Tcap, NBcap, block_size, top_k, rule, scale, out,
                                                                 o_sb, cand_idx, cand_val, sel_out, cnt_out,
-                                                                sel_cap, err, s));
+                                                                sel_cap, err, s, sd::SlotMap<E>(), nx));
     } else if (fdt == SD_DTYPE_F32) {
       SD_DISPATCH_G(G, return sd::launch_decode_layer<E, float, GG>(
                            qkv, qkv_sb, forecast, f_sb, rope_cos, rope_sin, cur_len, k_cache, v_cache, proto_sum,
                            B, Hkv, Tcap, NBcap, block_size, top_k, rule, scale, out, o_sb, cand_idx, cand_val,
-                           sel_out, cnt_out, sel_cap, err, s));
+                           sel_out, cnt_out, sel_cap, err, s, sd::SlotMap<E>(), nx));
     } else {
       return SD_ERR_UNSUPPORTED;
     }

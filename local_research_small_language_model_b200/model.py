@@ -136,7 +136,23 @@ class TransformerBlock(nn.Module):
             # compute them on the side stream while this layer's attention and
             # FFN run on the main stream
             side = getattr(self, "side_stream", None)
-            if next_layer_block is not None and isinstance(next_kv_cache, B200OffloadKVCache):
+            next_cand = None
+            if getattr(self, "chain_next", False) and next_layer_block is not None \
+                    and isinstance(next_kv_cache, B200KVCache) and isinstance(kv_cache, B200KVCache) \
+                    and next_layer_block.attention.mode == "forecast" \
+                    and next_layer_block.attention.rule == a.rule \
+                    and next_layer_block.attention.top_k_blocks == a.top_k_blocks \
+                    and next_layer_block.attention.block_size == a.block_size:
+                # this layer's kernel ends by computing the next layer's
+                # candidates: no side stream, no extra launch
+                nc = next_kv_cache
+                if getattr(nc, "cand", None) is None:
+                    nc.cand = (torch.empty(b, a.n_kv_head, a.top_k_blocks, dtype=torch.int32, device=x.device),
+                               torch.empty(b, a.n_kv_head, a.top_k_blocks, dtype=torch.float32, device=x.device))
+                next_cand = (nc.proto_sum, proj[:, nq:], nc.cand)
+                nc.cand_ready = True
+                nc.cand_event = None
+            elif next_layer_block is not None and isinstance(next_kv_cache, B200OffloadKVCache):
                 # offloaded next layer: candidates + host -> device staging of
                 # its blocks on the transfer stream (transformer.py:110-115)
                 ev = (probe["cstart"], probe["cend"]) if probe is not None and "cstart" in probe else None
@@ -181,7 +197,8 @@ class TransformerBlock(nn.Module):
                 return x2.view(b, 1, c), current_forecast
             cand = None
             if getattr(kv_cache, "cand_ready", False):
-                torch.cuda.current_stream().wait_event(kv_cache.cand_event)  # join the side stream
+                if kv_cache.cand_event is not None:
+                    torch.cuda.current_stream().wait_event(kv_cache.cand_event)  # join the side stream
                 cand = kv_cache.cand if f is not None else None
             kv_cache.cand_ready = False
             if probe is not None:
@@ -190,7 +207,8 @@ class TransformerBlock(nn.Module):
                                    kv_cache.k_store, kv_cache.v_store, kv_cache.proto_sum, a.n_head, a.n_kv_head,
                                    a.block_size, a.top_k_blocks, a.rule,
                                    sel_out=probe["sel"] if probe is not None else None,
-                                   cnt_out=probe["cnt"] if probe is not None else None, cand=cand)
+                                   cnt_out=probe["cnt"] if probe is not None else None, cand=cand,
+                                   next_cand=next_cand)
             if probe is not None:
                 probe["end"].record()
             kv_cache.advance(1, device=not getattr(kv_cache, "shared_len", False))
@@ -230,13 +248,23 @@ class SparDAB200Model(nn.Module):
             nn.init.normal_(module.weight, mean=0.0, std=self.config.initializer_range)
 
     def allocate_caches(self, batch: int, max_seq_len: int, dtype: Optional[torch.dtype] = None,
-                        device=None, overlap_selection: bool = True, offload: bool = False) -> List:
+                        device=None, overlap_selection: bool = True, offload: bool = False,
+                        selection: Optional[str] = None) -> List:
         """One cache per layer, sharing one device length array so a decode
         step bumps all lengths with a single launch.  With
-        ``overlap_selection`` each decode step scores layer L+1's prototypes on
-        a side stream while layer L's attention and FFN run.  With ``offload``
+        ``overlap_selection`` layer L+1's candidates for each decode step are
+        computed ahead of its kernel (by default at the end of layer L's fused
+        kernel).  With ``offload``
         the K/V rows live in pinned host memory (B200OffloadKVCache) and the
-        side stream also stages layer L+1's selected blocks into device slots."""
+        side stream also stages layer L+1's selected blocks into device slots.
+        ``selection`` overrides ``overlap_selection``: "kernel" (each fused
+        kernel scores its own blocks), "side-stream" (layer L+1's candidates on
+        a side stream during layer L) or "chain" (layer L's fused kernel ends
+        by computing layer L+1's candidates)."""
+        if selection is None:
+            selection = "chain" if overlap_selection else "kernel"
+        if selection not in ("kernel", "side-stream", "chain"):
+            raise ValueError(f"unknown selection mode {selection!r}")
         cfg = self.config
         device = device or self.embeddings.weight.device
         dtype = dtype or self.embeddings.weight.dtype
@@ -254,7 +282,10 @@ class SparDAB200Model(nn.Module):
             c.shared_len = True
             caches.append(c)
         self.rotary_emb._extend_cache(caches[0].tcap, device)
-        if overlap_selection and side is not None:
+        for layer in self.layers:
+            layer.chain_next = selection == "chain" and not offload
+            layer.side_stream = None
+        if (selection == "side-stream" or offload) and side is not None:
             for layer in self.layers:
                 layer.side_stream = side
         return caches

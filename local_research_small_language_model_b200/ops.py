@@ -218,9 +218,14 @@ def decode_layer(qkv: torch.Tensor, forecast: Optional[torch.Tensor], rope_cos: 
                  rule: str = "reference", scale: Optional[float] = None,
                  out: Optional[torch.Tensor] = None, sel_out: Optional[torch.Tensor] = None,
                  cnt_out: Optional[torch.Tensor] = None,
-                 cand: Optional[Tuple[torch.Tensor, torch.Tensor]] = None) -> torch.Tensor:
+                 cand: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
+                 next_cand: Optional[Tuple[torch.Tensor, torch.Tensor, Tuple[torch.Tensor, torch.Tensor]]] = None
+                 ) -> torch.Tensor:
     """Fused decode layer: RoPE + append + compressor update + selection +
     attention (model/attention/sparse.py:366-410 + :99-183 for T == 1).
+    next_cand (optional) = (next layer's proto_sum, next layer's forecast
+    rows [B,Hkv*D] (activation dtype), (cand_idx, cand_val) out): the kernel
+    also computes the next layer's candidates for its coming step.
     qkv [B,(Hq+2Hkv)*D] (pre-RoPE projections), forecast [B,Hkv,D] or None.
     sel_out [B,Hkv,cap] / cnt_out [B,Hkv] int32 (optional) receive each
     (sequence, kv head)'s selected block list.  cand (optional) is the
@@ -248,8 +253,16 @@ def decode_layer(qkv: torch.Tensor, forecast: Optional[torch.Tensor], rope_cos: 
            sel_out.data_ptr() if sel_out is not None else None,
            cnt_out.data_ptr() if cnt_out is not None else None,
            sel_out.shape[-1] if sel_out is not None else 0,
-           error_buffer(qkv.device).data_ptr(), _stream(qkv))
+           error_buffer(qkv.device).data_ptr(), *_next_args(next_cand, b, d), _stream(qkv))
     return out
+
+
+def _next_args(next_cand, b: int, d: int):
+    if next_cand is None:
+        return (None, None, 0, None, None)
+    proto, fc, (ci, cv) = next_cand
+    fc = _inner1(fc.reshape(b, -1))
+    return (proto.data_ptr(), fc.data_ptr(), fc.stride(0), ci.data_ptr(), cv.data_ptr())
 
 
 def decode_candidates(forecast: torch.Tensor, proto_sum: torch.Tensor, cur_len: torch.Tensor, n_kv_head: int,

@@ -107,16 +107,18 @@ def test_decode_engine_graph_matches_eager(dev):
     assert torch.equal(m1._lens, m2._lens)
 
 
+@pytest.mark.parametrize("mode", ["side-stream", "chain"])
 @pytest.mark.parametrize("rule", ["reference", "absolute"])
 @torch.no_grad()
-def test_overlapped_selection_matches_in_kernel_selection(dev, rule):
-    """Decode with layer L+1's candidates computed on the side stream during
-    layer L gives bit-identical logits to decode with selection in the kernel."""
+def test_overlapped_selection_matches_in_kernel_selection(dev, rule, mode):
+    """Decode with layer L+1's candidates computed ahead of time (on the side
+    stream during layer L, or at the end of layer L's fused kernel) gives
+    bit-identical logits to decode with selection in the kernel."""
     m1, sc = _model(dev, torch.bfloat16, rule=rule)
     m2, _ = _model(dev, torch.bfloat16, rule=rule)
     b, pre = 3, 1500
-    c1 = m1.allocate_caches(b, 2048, overlap_selection=False)
-    c2 = m2.allocate_caches(b, 2048, overlap_selection=True)
+    c1 = m1.allocate_caches(b, 2048, selection="kernel")
+    c2 = m2.allocate_caches(b, 2048, selection=mode)
     gen = torch.Generator(device="cpu").manual_seed(2)
     for ca, cb in zip(c1, c2):
         k = torch.randn(b, pre, 4, 64, generator=gen).to(dev, torch.bfloat16)
