@@ -75,6 +75,37 @@ __global__ void __launch_bounds__(256) rmsnorm_rows_kernel(const T *__restrict__
   }
 }
 
+// Same arithmetic for few rows (decode): one CTA per row, one 16-byte chunk
+// per thread, a single block-wide reduction.
+template <typename T>
+__global__ void rmsnorm_chunk_kernel(const T *__restrict__ x, int64_t x_rs, const T *__restrict__ w, int C,
+                                     float eps, T *__restrict__ out, int64_t o_rs) {
+  constexpr int kE = 16 / static_cast<int>(sizeof(T));
+  __shared__ float red[32];
+  const uint4 u = reinterpret_cast<const uint4 *>(x + blockIdx.x * x_rs)[threadIdx.x];
+  const uint4 g = reinterpret_cast<const uint4 *>(w)[threadIdx.x];
+  const T *e = reinterpret_cast<const T *>(&u);
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < kE; ++i) {
+    const float v = to_f(e[i]);
+    ss = fmaf(v, v, ss);
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+  for (int i = 0; i < static_cast<int>(blockDim.x >> 5); ++i) tot += red[i];
+  const float r = rsqrtf(tot / static_cast<float>(C) + eps);
+  const T *ge = reinterpret_cast<const T *>(&g);
+  uint4 o;
+  T *oe = reinterpret_cast<T *>(&o);
+#pragma unroll
+  for (int i = 0; i < kE; ++i) oe[i] = from_f<T>(round_to<T>(to_f(e[i]) * r) * to_f(ge[i]));
+  reinterpret_cast<uint4 *>(out + blockIdx.x * o_rs)[threadIdx.x] = o;
+}
+
 // gu rows hold [gate | up] (2F values); out = T(T(silu(gate)) * up).
 template <typename T>
 __global__ void silu_mul_kernel(const T *__restrict__ gu, int64_t g_rs, int F, T *__restrict__ out,
@@ -103,6 +134,15 @@ extern "C" int sd_rmsnorm(const void *x, int dtype, int64_t rows, int64_t C, int
                       sd::rmsnorm_rows_kernel<E><<<grid, 256, 0, s>>>(static_cast<const E *>(x), x_rs,
                                                                       static_cast<const E *>(w), (int)C, eps,
                                                                       static_cast<E *>(out), o_rs, rows));
+    return sd::check_launch();
+  }
+  const int64_t chunks = C * es / 16;
+  if ((C * es) % 16 == 0 && chunks % 32 == 0 && chunks <= 1024 && (x_rs * es) % 16 == 0 && (o_rs * es) % 16 == 0 &&
+      sd::aligned16(x) && sd::aligned16(w) && sd::aligned16(out)) {
+    SD_DISPATCH_DTYPE(dtype, E,
+                      sd::rmsnorm_chunk_kernel<E><<<static_cast<unsigned>(rows), static_cast<unsigned>(chunks), 0,
+                                                    s>>>(static_cast<const E *>(x), x_rs, static_cast<const E *>(w),
+                                                         (int)C, eps, static_cast<E *>(out), o_rs));
     return sd::check_launch();
   }
   const int threads = C >= 1024 ? 1024 : static_cast<int>(((C + 31) / 32) * 32);
