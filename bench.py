@@ -59,7 +59,9 @@ def parse():
                          "side stream during layer L, or at the end of layer L's fused kernel")
     ap.add_argument("--e2e-steps", type=int, default=1024)
     ap.add_argument("--probe-steps", type=int, default=64)
-    ap.add_argument("--cpu-seqs", type=int, default=2)
+    ap.add_argument("--cpu-seqs", type=int, default=1, help="sequences per CPU worker thread")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the config-3 prefill and standalone-kernel sub-measurements of the default run")
     ap.add_argument("--cpu-budget-s", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=12,
@@ -153,43 +155,67 @@ def gpu_id_for(dev_index: int) -> str:
 
 
 # ------------------------------------------------------------------ CPU leg
-def cpu_reference(ctx: int, seqs: int, budget_s: float, rule: str, max_steps: int = 1000, warmup: int = 1):
+def cpu_reference(ctx: int, seqs: int, budget_s: float, rule: str, max_steps: int = 1000, warmup: int = 1,
+                  workers: int = 0):
     """The reference's decode-step algorithm (oracle restatement, numpy fp32)
-    on the host cores: full 12-layer model, ``seqs`` sequences at ``ctx``
-    cached tokens, O(T) block compression every layer and step as the
-    reference does (model/attention/sparse.py:134-135)."""
+    on the host cores: full 12-layer model at ``ctx`` cached tokens, O(T)
+    block compression every layer and step as the reference does
+    (model/attention/sparse.py:134-135).
+
+    Every host core is used whatever the launcher set (torchrun exports
+    OMP_NUM_THREADS=1): ``workers`` threads (default: all cores, at most 32)
+    each decode their own ``seqs`` sequences with their own caches, BLAS pools
+    pinned to one thread each so the cores are not oversubscribed (numpy
+    releases the GIL inside its kernels).  The reported rate is sequences
+    decoded per second over all workers; it does not depend on the batch the
+    GPU arm runs, because each sequence's step is independent work."""
+    import concurrent.futures as cf
+
     import numpy as np
     from oracle import sparda_oracle as O
     from oracle.synthetic import SmallModelConfig, model_state
     try:
-        from threadpoolctl import threadpool_info
-        threads = max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
+        from threadpoolctl import threadpool_limits
     except Exception:
-        threads = os.cpu_count() or 1
+        threadpool_limits = None
+    workers = workers or min(os.cpu_count() or 1, 32)
     cfg = SmallModelConfig(vocab_size=32000, n_layer=12)
     m = O.OracleModel(model_state(cfg, seed=0), n_layer=12, block_size=64, top_k=8, max_seq_len=ctx + 64,
                       rule=rule, dtype=np.float32)
     rng = np.random.default_rng(5)
-    kc = [rng.standard_normal((seqs, 4, ctx + 64, 64), dtype=np.float32) for _ in range(12)]
-    vc = [rng.standard_normal((seqs, 4, ctx + 64, 64), dtype=np.float32) for _ in range(12)]
-    ids = rng.integers(0, cfg.vocab_size, size=seqs)
-    times = []
-    t_start = time.perf_counter()
-    i = 0
-    while i < max_steps + warmup:
-        t0 = time.perf_counter()
+    kc0 = [rng.standard_normal((seqs, 4, ctx + 64, 64), dtype=np.float32) for _ in range(12)]
+    vc0 = [rng.standard_normal((seqs, 4, ctx + 64, 64), dtype=np.float32) for _ in range(12)]
+    state = [([c.copy() for c in kc0], [c.copy() for c in vc0], rng.integers(0, cfg.vocab_size, size=seqs))
+             for _ in range(workers)]
+    del kc0, vc0
+
+    def one(w):
+        kc, vc, ids = state[w]
         logits = m.decode_step(ids, kc, vc, ctx)  # fixed position: each step decodes token ctx
-        ids = logits.argmax(-1)
-        if i >= warmup:
-            times.append(time.perf_counter() - t0)
-        i += 1
-        if time.perf_counter() - t_start > budget_s and len(times) >= 2:
-            break
+        state[w] = (kc, vc, logits.argmax(-1))
+
+    import contextlib
+    limits = threadpool_limits(limits=1) if threadpool_limits is not None else contextlib.nullcontext()
+    with limits, cf.ThreadPoolExecutor(max_workers=workers) as ex:
+        times = []
+        t_start = time.perf_counter()
+        i = 0
+        while i < max_steps + warmup:
+            t0 = time.perf_counter()
+            list(ex.map(one, range(workers)))
+            if i >= warmup:
+                times.append(time.perf_counter() - t0)
+            i += 1
+            if time.perf_counter() - t_start > budget_s and len(times) >= 2:
+                break
     step_s = statistics.mean(times)
-    return {"value": seqs / step_s, "unit": "tok/s", "cores": int(threads), "kind": "port",
-            "sample": f"{seqs} sequences x {len(times)} decode steps at {ctx} cached tokens, 12 layers, fp32 numpy "
-                      f"(oracle/sparda_oracle.py OracleModel); rate per sequence scales linearly to B=64",
-            "step_s": step_s, "steps": len(times)}
+    total = seqs * workers
+    return {"value": total / step_s, "unit": "tok/s", "cores": int(workers), "kind": "port",
+            "sample": f"{workers} threads x {seqs} sequence(s) each = {total} sequences x {len(times)} decode steps "
+                      f"at {ctx} cached tokens, 12 layers, fp32 numpy (oracle/sparda_oracle.py OracleModel, the "
+                      f"reference algorithm restated; the reference's own PyTorch code cannot travel to the GPU "
+                      f"box); rate = sequences decoded per second, independent of the GPU arm's batch",
+            "step_s": step_s, "steps": len(times), "sequences": total}
 
 
 # ------------------------------------------------------------------ GPU leg
@@ -512,6 +538,88 @@ def run_prefill(args, rank, world, local):
     }
 
 
+def _event_time_s(fn, reps=10, warm=3):
+    """Average device time of fn() over `reps` launches (CUDA events on the
+    current stream, after `warm` untimed calls)."""
+    import torch
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / 1000.0 / reps
+
+
+def fp32_simt_peak_tflops(dev_index: int) -> float:
+    """Nominal fp32 CUDA-core rate: SMs x 128 lanes x 2 flops x max SM clock."""
+    import torch
+    props = torch.cuda.get_device_properties(dev_index)
+    mhz = 1965.0
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as fh:
+            mhz = float(json.load(fh).get("sm_max_mhz", mhz))
+    except Exception:
+        pass
+    return props.multi_processor_count * 128 * 2 * mhz * 1e6 / 1e12
+
+
+def run_kernels(local: int):
+    """Standalone device time of the path's other kernels on BASELINE-sized
+    inputs, against the HBM roofline (algorithmic bytes per launch / time):
+    the compressor over one config-2 layer cache (64 x 16,384 tokens, bf16),
+    the block gather of 10 blocks per (sequence, kv head) from that cache, the
+    config-3 prefill selector (32,768 forecast rows x 512 blocks, fp32 scores +
+    top-8 in registers; fp32 CUDA-core bound) and the config-3 block-list
+    builder.  Inputs exceed the 126 MB L2 except the selector's, whose bound is
+    arithmetic."""
+    import torch
+    from local_research_small_language_model_b200 import ops
+    dev = torch.device("cuda", local)
+    hbm, src = read_peaks()
+    g = torch.Generator(device=dev).manual_seed(5)
+    out = {}
+    B, T, H = 64, 16384, 4
+    k_store = torch.randn(B, H, T, 64, generator=g, device=dev, dtype=torch.bfloat16)
+    v_store = torch.randn(B, H, T, 64, generator=g, device=dev, dtype=torch.bfloat16)
+    k_tok = k_store.permute(0, 2, 1, 3)  # the reference's [B, T, H, D] view of the block-major store
+    s = _event_time_s(lambda: ops.compress_blocks(k_tok, 64))
+    by = k_store.numel() * 2 + B * (T // 64) * H * 64 * 4
+    out["compress_blocks"] = {"kernel": "sd::compress_blocks_kernel (sd_compress_blocks)", "us": round(s * 1e6, 2),
+                              "bytes": by, "gbs": round(by / s / 1e9, 1), "frac": round(by / s / 1e9 / hbm, 4),
+                              "shape": "K [64, 16384, 4, 64] bf16 -> prototypes fp32 [64, 256, 4, 64]"}
+    idx = torch.randint(0, T // 64, (B, H, 10), generator=g, device=dev)
+    s = _event_time_s(lambda: ops.gather_kv_blocks(k_store, v_store, idx, 64))
+    by = 2 * 2 * B * H * 10 * 64 * 64 * 2  # K and V rows read and written
+    out["gather_kv_blocks"] = {"kernel": "sd::gather_kv_kernel (sd_gather_kv_blocks)", "us": round(s * 1e6, 2),
+                               "bytes": by, "gbs": round(by / s / 1e9, 1), "frac": round(by / s / 1e9 / hbm, 4),
+                               "shape": "10 blocks of 64 rows per (sequence, kv head), 64 x 4, bf16"}
+    del k_store, v_store, k_tok
+    Tp = 32768
+    f = torch.randn(1, Tp, H, 64, generator=g, device=dev, dtype=torch.bfloat16)
+    reps = torch.randn(1, Tp // 64, H, 64, generator=g, device=dev, dtype=torch.float32)
+    s = _event_time_s(lambda: ops.select_blocks(f, reps, 8, 64, False, return_scores=False))
+    fl = 2 * Tp * H * (Tp // 64) * 64
+    peak32 = fp32_simt_peak_tflops(local)
+    out["select_blocks_prefill"] = {"kernel": "sd::select_rows_tiled_kernel (sd_select_blocks, no score tensor)",
+                                    "us": round(s * 1e6, 2), "flops": fl, "tflops": round(fl / s / 1e12, 2),
+                                    "peak_fp32_simt_tflops": round(peak32, 1),
+                                    "frac": round(fl / s / 1e12 / peak32, 4),
+                                    "shape": "forecast [1, 32768, 4, 64] bf16 x prototypes [1, 512, 4, 64] fp32"}
+    _, topk = ops.select_blocks(f, reps, 8, 64, False, return_scores=False)
+    s = _event_time_s(lambda: ops.prefill_lists("chunked_forecast", 1, H, Tp, 64, 8, topk, True, device=dev))
+    by = topk.numel() * 8 + H * (Tp // 64) * (10 + 1) * 4
+    out["prefill_lists"] = {"kernel": "sd::prefill_lists_kernel (sd_prefill_lists, chunked forecast)",
+                            "us": round(s * 1e6, 2), "bytes": by, "gbs": round(by / s / 1e9, 1),
+                            "frac": round(by / s / 1e9 / hbm, 4),
+                            "shape": "top-8 of 32768 rows x 4 heads -> 512 lists per head"}
+    out["peak_source"] = src
+    return out
+
+
 def max_over_ranks_simple(x):
     from local_research_small_language_model_b200.sharding import max_over_ranks
     return max_over_ranks(x)
@@ -540,8 +648,10 @@ def main():
                "n_gpus": world, "steps": r["steps"], "warmup": min(args.warmup, 2),
                "ms_per_step": round(r["step_s"] * 1000.0, 3), "higher_is_better": True, "scaling": "weak",
                "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-               "config": {"workload": "BASELINE config 2 decode step, bounded CPU sample", "global_batch": args.batch,
-                          "seq_len": args.ctx, "selector_rule": args.rule},
+               "config": {"workload": "BASELINE config 2 decode step (the GPU arm's workload), timed on a bounded "
+                                      "sample of its sequences on the host cores",
+                          "global_batch": args.batch * world, "per_gpu_batch": args.batch,
+                          "sample_sequences": r["sequences"], "seq_len": args.ctx, "selector_rule": args.rule},
                "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
                "e2e": {"value": round(r["value"], 3), "unit": "tok/s", "h2d_bytes_per_step": 0,
                        "d2h_bytes_per_step": 0}}
@@ -556,6 +666,15 @@ def main():
                                 device_id=torch.device("cuda", local))
     try:
         res = run_prefill(args, rank, world, local) if args.prefill else run_b200(args, rank, world, local)
+        if world == 1 and not args.prefill and not args.offload and not args.no_extras:
+            # BASELINE config 3 (prefill of one 32K-token sequence) and the
+            # standalone path kernels, so the default run records them too
+            pa = argparse.Namespace(**vars(args))
+            pa.ctx, pa.steps, pa.warmup, pa.layers = 32768, 2, 1, args.layers
+            pre = run_prefill(pa, rank, world, local)
+            res["prefill"] = {k: pre[k] for k in ("metric", "value", "unit", "ms_per_step", "steps", "warmup",
+                                                  "config", "roofline", "clocks")}
+            res["kernels"] = run_kernels(local)
         if rank == 0:
             if world == 1 and not args.no_cpu_baseline and not args.prefill:
                 r = cpu_reference(args.ctx, args.cpu_seqs, args.cpu_budget_s, args.rule)

@@ -164,7 +164,10 @@ SD_API int sd_kv_append(const void *xk, const void *xv, int dtype, int64_t B, in
  * forecast rows (this layer's forecast projection, activation dtype, row
  * stride next_f_sb) and its candidate outputs [B,Hkv,top_k]: the kernel ends
  * by computing what sd_decode_candidates would for the next layer's coming
- * step, with no separate launch or stream. */
+ * step, with no separate launch or stream.  The next layer's cache must have
+ * this layer's geometry (B, Hkv, NBcap, head_dim, block_size): its sums are
+ * indexed as [B,Hkv,NBcap,D] with this call's sizes, and nothing on the
+ * device can check that. */
 SD_API int sd_decode_layer(const void *qkv, int dtype, int64_t qkv_sb, const void *forecast,
                     int f_dtype, int64_t f_sb, const float *rope_cos, const float *rope_sin,
                     int64_t max_pos, const int32_t *cur_len, void *k_cache, void *v_cache,

@@ -77,11 +77,16 @@ __global__ void __launch_bounds__(256) rmsnorm_rows_kernel(const T *__restrict__
 
 // Same arithmetic for few rows (decode): one CTA per row, one 16-byte chunk
 // per thread, a single block-wide reduction.
+// Launch contract: blockDim.x == C * sizeof(T) / 16 exactly (every thread owns
+// one 16-byte chunk of the row) and blockDim.x is a multiple of 32, at most
+// 1024; rows and the gain are 16-byte aligned.  sd_rmsnorm checks all of this
+// before choosing this kernel; a launch that breaks it returns without writing.
 template <typename T>
 __global__ void rmsnorm_chunk_kernel(const T *__restrict__ x, int64_t x_rs, const T *__restrict__ w, int C,
                                      float eps, T *__restrict__ out, int64_t o_rs) {
   constexpr int kE = 16 / static_cast<int>(sizeof(T));
   __shared__ float red[32];
+  if (static_cast<int>(blockDim.x) * kE != C || (blockDim.x & 31u) != 0) return;  // contract broken: no writes
   const uint4 u = reinterpret_cast<const uint4 *>(x + blockIdx.x * x_rs)[threadIdx.x];
   const uint4 g = reinterpret_cast<const uint4 *>(w)[threadIdx.x];
   const T *e = reinterpret_cast<const T *>(&u);

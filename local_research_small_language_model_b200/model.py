@@ -142,7 +142,9 @@ class TransformerBlock(nn.Module):
                     and next_layer_block.attention.mode == "forecast" \
                     and next_layer_block.attention.rule == a.rule \
                     and next_layer_block.attention.top_k_blocks == a.top_k_blocks \
-                    and next_layer_block.attention.block_size == a.block_size:
+                    and a.top_k_blocks <= 32 \
+                    and next_layer_block.attention.block_size == a.block_size \
+                    and next_kv_cache.proto_sum.shape == kv_cache.proto_sum.shape:
                 # this layer's kernel ends by computing the next layer's
                 # candidates: no side stream, no extra launch
                 nc = next_kv_cache

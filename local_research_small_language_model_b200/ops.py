@@ -243,6 +243,20 @@ def decode_layer(qkv: torch.Tensor, forecast: Optional[torch.Tensor], rope_cos: 
         fargs = (f.data_ptr(), dtype_code(f), f.stride(0))
     else:
         fargs = (None, dtype_code(k_store), 0)
+    if next_cand is not None:
+        # the kernel indexes the next layer's sums with this layer's geometry
+        nproto, nfc, (nci, ncv) = next_cand
+        _cuda(nproto, nfc, nci, ncv)
+        if nproto.shape != proto_sum.shape or nproto.dtype != torch.float32 or not nproto.is_contiguous():
+            raise ValueError(f"next layer's block sums {tuple(nproto.shape)} must match this layer's "
+                             f"{tuple(proto_sum.shape)} (fp32, contiguous)")
+        if nfc.reshape(b, -1).shape[1] != n_kv_head * d or nfc.dtype != qkv.dtype:
+            raise ValueError(f"next layer's forecast rows must hold {n_kv_head * d} values of {qkv.dtype}")
+        if top_k > 32:
+            raise ValueError("chained candidates support top_k <= 32")
+        for tt in (nci, ncv):
+            if tuple(tt.shape) != (b, n_kv_head, top_k) or not tt.is_contiguous():
+                raise ValueError(f"candidate outputs must be contiguous [{b}, {n_kv_head}, {top_k}]")
     sc = 1.0 / math.sqrt(d) if scale is None else scale
     L.call("sd_decode_layer", qkv.data_ptr(), dtype_code(qkv), qkv.stride(0), *fargs, rope_cos.data_ptr(),
            rope_sin.data_ptr(), rope_cos.shape[0], cur_len.data_ptr(), k_store.data_ptr(), v_store.data_ptr(),

@@ -109,9 +109,15 @@ def select_blocks(forecast, reps, top_k: int, block_size: int, is_causal: bool =
 # ---------------------------------------------------------------------------
 
 def rope_tables(head_dim: int, max_seq_len: int, theta: float = 10000.0):
-    """precompute_rope_freqs (model/rope.py:8-23), in float32 like the reference."""
-    inv = 1.0 / (theta ** (np.arange(0, head_dim, 2, dtype=np.float32) / head_dim))
-    inv = inv.astype(np.float32)
+    """precompute_rope_freqs (model/rope.py:8-23), in float32 like the reference.
+
+    theta ** (2i / d) is rounded once to float32 (torch's float32 pow returns
+    the correctly rounded power), then inverted in float32 as the reference's
+    ``1.0 / tensor`` is.  A 1-ulp error in an inverse frequency becomes a phase
+    error of position x ulp, about 1e-3 rad at 16K positions, so the table must
+    be built exactly this way to match the reference at long contexts."""
+    p = (theta ** (np.arange(0, head_dim, 2, dtype=np.float64) / head_dim)).astype(np.float32)
+    inv = (np.float32(1.0) / p).astype(np.float32)
     t = np.arange(max_seq_len, dtype=np.float32)
     freqs = np.outer(t, inv).astype(np.float32)
     return np.cos(freqs).astype(np.float32), np.sin(freqs).astype(np.float32)
@@ -459,6 +465,7 @@ class OracleModel:
         self.n_layer, self.n_head, self.n_kv_head, self.head_dim = n_layer, n_head, n_kv_head, head_dim
         self.block_size, self.top_k, self.eps, self.rule, self.dtype = block_size, top_k, norm_eps, rule, dtype
         self.cos, self.sin = rope_tables(head_dim, max_seq_len, rope_theta)
+        self.last_sel = [None] * n_layer  # (sel, cnt) of every layer in the last decode step
 
     def decode_step(self, ids: np.ndarray, k_caches, v_caches, cur_len: int) -> np.ndarray:
         """One decode step: writes position ``cur_len`` of every cache and
@@ -486,6 +493,7 @@ class OracleModel:
                 reps = compress_blocks(kc[:, :, :L].transpose(0, 2, 1, 3), self.block_size, dt)
             sel, cnt = decode_select(prev_f, reps, L, self.block_size, self.top_k, b, hkv,
                                      "forecast", self.rule, dt)
+            self.last_sel[li] = (sel, cnt)
             a = decode_attention(q[:, 0], kc, vc, sel, cnt, L, self.block_size, dtype=dt)
             x = x + a.reshape(b, hq * d).astype(dt) @ s[p + "attention.wo.weight"].T
             hn = rmsnorm(x, s[p + "ffn_norm.weight"], self.eps).astype(dt)
@@ -494,4 +502,35 @@ class OracleModel:
             x = x + ((gt / (1.0 + np.exp(-gt))) * up) @ s[p + "ffn.w_down.weight"].T
             prev_f = fc
         x = rmsnorm(x, s["final_norm.weight"], self.eps)
+        return x @ s["embeddings.weight"].T
+
+    def prefill(self, ids: np.ndarray, k_caches, v_caches) -> np.ndarray:
+        """Prompt forward into empty caches (model.py:79-157 with T > 1 and
+        T <= 8192): every layer runs the masked path (sparse.py:185-282) with
+        the previous layer's forecast and writes positions 0..T-1 of its cache.
+        ids [B, T]; returns the last position's logits [B, V]."""
+        s, dt = self.s, self.dtype
+        b, t = ids.shape
+        hq, hkv, d = self.n_head, self.n_kv_head, self.head_dim
+        x = s["embeddings.weight"][ids]  # [B, T, C]
+        prev_f = None
+        for li in range(self.n_layer):
+            p = f"layers.{li}."
+            h = rmsnorm(x, s[p + "attn_norm.weight"], self.eps).astype(dt)
+            fc = (h @ s[p + "forecast.wf.weight"].T).reshape(b, t, hkv, d)
+            q = apply_rope((h @ s[p + "attention.wq.weight"].T).reshape(b, t, hq, d), self.cos, self.sin, 0)
+            k = apply_rope((h @ s[p + "attention.wk.weight"].T).reshape(b, t, hkv, d), self.cos, self.sin, 0)
+            v = (h @ s[p + "attention.wv.weight"].T).reshape(b, t, hkv, d)
+            q, k = q.astype(dt).transpose(0, 2, 1, 3), k.astype(dt).transpose(0, 2, 1, 3)
+            v = v.transpose(0, 2, 1, 3)
+            k_caches[li][:, :, :t] = k
+            v_caches[li][:, :, :t] = v
+            a = masked_prefill(q, k, v, prev_f, self.block_size, self.top_k, li, dtype=dt)
+            x = x + a.transpose(0, 2, 1, 3).reshape(b, t, hq * d).astype(dt) @ s[p + "attention.wo.weight"].T
+            hn = rmsnorm(x, s[p + "ffn_norm.weight"], self.eps).astype(dt)
+            gt = hn @ s[p + "ffn.w_gate.weight"].T
+            up = hn @ s[p + "ffn.w_up.weight"].T
+            x = x + ((gt / (1.0 + np.exp(-gt))) * up) @ s[p + "ffn.w_down.weight"].T
+            prev_f = fc
+        x = rmsnorm(x[:, -1], s["final_norm.weight"], self.eps)
         return x @ s["embeddings.weight"].T

@@ -273,6 +273,178 @@ def model_cases(torch, out):
     np.savez(os.path.join(out, "model_decode.npz"), ids=ids.astype(np.int32), **logits)
 
 
+@contextlib.contextmanager
+def absolute_rule():
+    """Decode-time selection by the query's absolute position, produced by the
+    reference's own ForecastBlockSelector (model/forecast.py:89-130).  In
+    decode the reference passes one forecast row with is_causal=True, so its
+    mask (forecast.py:120-126) compares blocks with row index 0.  Placed at its
+    absolute row L-1 instead, the same mask hides blocks j > (L-1) // bs, i.e.
+    none of the cached blocks; the wrapper therefore calls the original method
+    with is_causal=False for single-row calls.  Multi-row calls (prefill) are
+    passed through unchanged."""
+    from model.forecast import ForecastBlockSelector
+    orig = ForecastBlockSelector.forward
+
+    def forward(self, forecast, block_reps, top_k, is_causal=True):
+        if forecast.shape[1] == 1:
+            is_causal = False
+        return orig(self, forecast, block_reps, top_k, is_causal)
+
+    ForecastBlockSelector.forward = forward
+    try:
+        yield
+    finally:
+        ForecastBlockSelector.forward = orig
+
+
+DECODE_BIG_CASES = [
+    # name, B, L (tokens after the append), rule, seed
+    ("L16385_abs", 2, 16385, "absolute", 800),
+    ("L16448_abs", 2, 16448, "absolute", 801),
+    ("L16400_ref", 2, 16400, "reference", 802),
+    ("L1000_abs", 2, 1000, "absolute", 803),
+    ("L641_abs", 2, 641, "absolute", 804),
+]
+
+
+def decode_big_inputs(b, L, seed):
+    """Inputs of one decode step at BASELINE config-2 lengths, pre-RoPE: the
+    cached prefix K/V [B, L-1, 4, 64] (already rotated, as a cache holds them),
+    the new token's q [B, 12, 64], k and v [B, 4, 64], and layer L-1's
+    forecast [B, 1, 4, 64]."""
+    return (normal((b, L - 1, 4, 64), seed=seed), normal((b, L - 1, 4, 64), seed=seed + 1),
+            normal((b, 12, 64), seed=seed + 2), normal((b, 4, 64), seed=seed + 3),
+            normal((b, 4, 64), seed=seed + 4), normal((b, 1, 4, 64), seed=seed + 5))
+
+
+def decode_big_cases(torch, out):
+    """One decode step of SparseAttention._forward_decode_gather
+    (model/attention/sparse.py:99-183) at up to 16,448 cached tokens, with the
+    new token rotated by the reference's RotaryEmbedding (model/rope.py:34-98)
+    at its position and appended to the cache first, as SparseAttention.forward
+    does (sparse.py:390-399).  Captures the selected lists it gathered."""
+    import model.attention.sparse as sp
+    from model.rope import RotaryEmbedding
+    a = _attn(torch)
+    res = {}
+    for name, b, L, rule, seed in DECODE_BIG_CASES:
+        kp, vp, q, kn, vn, f = (torch.from_numpy(x) for x in decode_big_inputs(b, L, seed))
+        rot = RotaryEmbedding(64, L + 64)
+        qr, kr = rot(q[:, None], kn[:, None], offset=L - 1)
+        k_all = torch.cat([kp, kr], dim=1).transpose(1, 2)  # [B, 4, L, 64]
+        v_all = torch.cat([vp, vn[:, None]], dim=1).transpose(1, 2)
+        ctx = absolute_rule() if rule == "absolute" else contextlib.nullcontext()
+        with ctx, capture(sp, torch) as rec, torch.no_grad():
+            o = a._forward_decode_gather(qr.transpose(1, 2), k_all, v_all, L, forecast_vector=f)
+        res[name + "_out"] = o.reshape(b, 12, 64).numpy()
+        res[name + "_sel"] = rec["idx"][0].numpy().astype(np.int32)
+        res[name + "_valid"] = rec["mask"][0].numpy()[:, ::3, 0, ::64] == 0
+    np.savez(os.path.join(out, "decode_big.npz"), **res)
+
+
+MODEL_SPARSE_PREFILL = 700
+MODEL_SPARSE_STEPS = 72        # decode positions 700..771: 11 to 13 blocks, past the dense fallback
+MODEL_SPARSE_LOGIT_EVERY = 4
+
+
+def model_sparse_cases(torch, out):
+    """Full SparDAResearchModel with the sparse backend and the absolute
+    decode rule (absolute_rule above): a 700-token prefill (masked path,
+    sparse.py:185-282), then 72 decode steps in the sparse regime, where layer
+    L's forecast selects layer L+1's blocks (model/model.py:100-139,
+    model/transformer.py:76-131).  Stores the prefill's last logits, the logits
+    of every 4th decode step and every layer's selected lists."""
+    import model.attention.sparse as sp
+    from model.config import ModelConfig
+    from model.model import SparDAResearchModel
+    from model.attention.base import KVCache
+    sc = SmallModelConfig()
+    cfg = ModelConfig(vocab_size=sc.vocab_size, n_layer=sc.n_layer, context_length=sc.context_length,
+                      block_size=sc.block_size, top_k_blocks=sc.top_k_blocks, attention_backend="sparse")
+    m = SparDAResearchModel(cfg).eval()
+    m.load_state_dict({k: torch.from_numpy(v) for k, v in model_state(sc, seed=9).items()}, strict=True)
+    b, p, n = 2, MODEL_SPARSE_PREFILL, MODEL_SPARSE_STEPS
+    ids = np.random.default_rng(10).integers(0, sc.vocab_size, size=(b, p + n))
+    caches = [KVCache(b, 1024, 4, 64, torch.device("cpu"), torch.float32) for _ in range(sc.n_layer)]
+    res = {"ids": ids.astype(np.int32)}
+    sels, valids = [], []
+    with absolute_rule(), torch.no_grad():
+        o = m(torch.from_numpy(ids[:, :p]), kv_caches=caches)["logits"]
+        res["prefill_last"] = o[:, -1].numpy()
+        for s in range(n):
+            with capture(sp, torch) as rec:
+                o = m(torch.from_numpy(ids[:, p + s:p + s + 1]), kv_caches=caches)["logits"][:, 0]
+            if s % MODEL_SPARSE_LOGIT_EVERY == 0 or s == n - 1:
+                res[f"step{s}"] = o.numpy()
+            assert len(rec["idx"]) == sc.n_layer
+            sels.append(np.stack([i.numpy() for i in rec["idx"]]))           # [layers, B, 4, MS]
+            valids.append(np.stack([(mk.numpy()[:, ::3, 0, ::64] == 0) for mk in rec["mask"]]))
+    res["sel"] = np.stack(sels).astype(np.int16)   # [steps, layers, B, 4, MS]
+    res["valid"] = np.stack(valids)
+    np.savez(os.path.join(out, "model_sparse.npz"), **res)
+
+
+CHUNKED_BIG = ("T32768", 1, 32768, 610)
+CHUNKED_BIG_ROW_EVERY = 257
+
+
+def chunked_big_cases(torch, out):
+    """_forward_chunked_gather (sparse.py:284-364) at BASELINE config 3's
+    length (T=32,768, 512 q-blocks), fp32: the per-q-block lists the reference
+    gathered (its truncation of the union is implementation-defined, so
+    attention parity is checked on these lists), every 257th output row and
+    every row's sum."""
+    import model.attention.sparse as sp
+    name, b, t, seed = CHUNKED_BIG
+    a = _attn(torch)
+    q = torch.from_numpy(normal((b, 12, t, 64), seed=seed))
+    k = torch.from_numpy(normal((b, 4, t, 64), seed=seed + 1))
+    v = torch.from_numpy(normal((b, 4, t, 64), seed=seed + 2))
+    f = torch.from_numpy(normal((b, t, 4, 64), seed=seed + 3))
+    with capture(sp, torch) as rec, torch.no_grad():
+        o = a._forward_chunked_gather(q, k, v, t, forecast_vector=f)
+    o = o.reshape(b, t, 12, 64).double().numpy()
+    sel = np.stack([i.numpy() for i in rec["idx"]], axis=2)
+    valid = np.stack([(m[:, ::3, -1, ::64] == 0).numpy() for m in rec["mask"]], axis=2)
+    np.savez(os.path.join(out, "chunked_big.npz"), sel=sel.astype(np.int16), valid=valid,
+             rows=o[:, ::CHUNKED_BIG_ROW_EVERY].astype(np.float32), row_sum=o.sum(axis=(2, 3)))
+
+
+def prefetch_abs_cases(torch, out):
+    """AsyncForecastOffloadAttention.prefetch (async_offload.py:190-260) with
+    the absolute decode rule: the blocks it selects before the new token is
+    appended, from prototypes that cover the cached tokens only."""
+    from model.config import ModelConfig
+    from model.attention.async_offload import AsyncForecastOffloadAttention, AsyncOffloadedKVCache
+    res = {}
+    with absolute_rule():
+        for name, b, L, li, seed in PREFETCH_ABS_CASES:
+            cfg = ModelConfig(block_size=64, top_k_blocks=8, attention_backend="async_offload")
+            attn = AsyncForecastOffloadAttention(cfg, layer_idx=li)
+            cache = AsyncOffloadedKVCache(b, L + 64, 4, 64, torch.device("cpu"), torch.float32, pin_memory=False)
+            k = torch.from_numpy(normal((b, L, 4, 64), seed=seed))
+            v = torch.from_numpy(normal((b, L, 4, 64), seed=seed + 1))
+            cache.update(k, v)
+            f = torch.from_numpy(normal((b, 1, 4, 64), seed=seed + 2))
+            with torch.no_grad():
+                attn.prefetch(f, cache)
+            res[name + "_small"] = np.array(attn.prefetched_is_small_context)
+            if attn.prefetched_sel_indices is not None:
+                res[name + "_sel"] = attn.prefetched_sel_indices.numpy().astype(np.int32)
+                res[name + "_val"] = attn.prefetched_val.numpy()
+    np.savez(os.path.join(out, "prefetch_abs.npz"), **res)
+
+
+PREFETCH_ABS_CASES = [
+    # name, B, cached tokens, layer_idx, seed
+    ("L1000", 2, 1000, 1, 720),
+    ("L1023", 2, 1023, 1, 721),
+    ("L1024", 2, 1024, 1, 722),
+    ("L3000", 2, 3000, 1, 723),
+]
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True)
@@ -281,7 +453,8 @@ def main():
     args = ap.parse_args()
     torch = _setup(args.reference)
     jobs = [config1, compressor_cases, selector_cases, decode_cases, masked_cases, chunked_cases,
-            prefetch_cases, model_cases]
+            prefetch_cases, model_cases, decode_big_cases, model_sparse_cases, chunked_big_cases,
+            prefetch_abs_cases]
     for job in jobs:
         if args.only and job.__name__ not in args.only.split(","):
             continue

@@ -82,9 +82,10 @@ def test_install_swaps_attention_modules():
 
 def test_install_into_reference_model():
     """The reference's own model accepts the backend (module swap; CPU only,
-    so no forward).  Skipped where the reference checkout is absent."""
-    ref = "/root/reference"
-    if not os.path.isdir(os.path.join(ref, "model")):
+    so no forward).  SPARDA_REFERENCE names the reference checkout; skipped
+    where it is unset or absent."""
+    ref = os.environ.get("SPARDA_REFERENCE", "")
+    if not ref or not os.path.isdir(os.path.join(ref, "model")):
         pytest.skip("reference checkout not present")
     import sys
     sys.path.insert(0, ref)

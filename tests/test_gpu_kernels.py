@@ -63,7 +63,8 @@ def _finite_slots_equal(scores, ref_idx, idx, gap=1e-5):
     nxt = np.concatenate([vals[..., 1:], np.full(vals.shape[:-1] + (1,), -np.inf)], axis=-1)
     prv = np.concatenate([np.full(vals.shape[:-1] + (1,), np.inf), vals[..., :-1]], axis=-1)
     scale = np.maximum(np.abs(vals), 1e-30)
-    clear = ((vals - nxt) > gap * scale) & ((prv - vals) > gap * scale)
+    with np.errstate(invalid="ignore"):  # -inf - -inf at the non-finite slots, which `ok` drops
+        clear = ((vals - nxt) > gap * scale) & ((prv - vals) > gap * scale)
     sel = ok & clear
     return np.array_equal(ref_idx[sel], idx[sel]), sel.mean()
 
@@ -331,12 +332,17 @@ def test_decode_layer_rope_bitexact_bf16(dev):
 
 # ------------------------------------------------------------------ decode-step row kernels
 @pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
-@pytest.mark.parametrize("rows", [64, 1000])
-def test_rmsnorm_matches_reference_formula(dev, dt, rows):
-    """model/norm.py:15-21: fp32 normalisation, cast, gain multiply in dtype
-    (64 rows: block-per-row kernel; 1000 rows: warp-per-row kernel)."""
-    x = t(normal((rows, 768), seed=1), dev, dt)
-    w = t(1.0 + 0.1 * normal((768,), seed=2), dev, dt)
+@pytest.mark.parametrize("rows,c,offset", [(64, 768, 0), (1000, 768, 0), (64, 1000, 0), (64, 768, 3)])
+def test_rmsnorm_matches_reference_formula(dev, dt, rows, c, offset):
+    """model/norm.py:15-21: fp32 normalisation, cast, gain multiply in dtype.
+    Each case reaches a different kernel of sd_rmsnorm: 64 rows of 768 -> the
+    one-16-byte-chunk-per-thread kernel (rmsnorm_chunk_kernel); 1000 rows ->
+    the warp-per-row kernel (rmsnorm_rows_kernel); C=1000 (not a multiple of
+    256 bf16 values) and a row view starting 3 elements in (unaligned) -> the
+    generic block-per-row kernel (rmsnorm_kernel)."""
+    base = t(normal((rows, c + offset), seed=1), dev, dt)
+    x = base[:, offset:]
+    w = t(1.0 + 0.1 * normal((c,), seed=2), dev, dt)
     ref = (x.float() * torch.rsqrt(x.float().pow(2).mean(-1, keepdim=True) + 1e-6)).type_as(x) * w
     got = ops.rmsnorm(x, w, 1e-6)
     tol = 1e-6 if dt == torch.float32 else 8e-3  # one bf16 ulp of the normalised value

@@ -215,3 +215,126 @@ def test_model_decode_logits(golden):
         lg = m.decode_step(ids[:, s], kc, vc, s)
         if s in MODEL_STEPS:
             np.testing.assert_allclose(lg, g[f"step{s}"], rtol=0, atol=2e-4)
+
+
+# ---------------------------------------------------------------- BASELINE-sized and sparse-regime goldens
+def _decode_big_oracle(b, L, rule, seed):
+    """The oracle fed the same step the golden generator ran: the prefix cache,
+    the new token rotated at position L-1 and appended, then selection +
+    attention.  Returns (q_rot [B,12,64], k_all, v_all [B,4,L,64], sel, cnt)."""
+    from tests.golden.make_golden import decode_big_inputs
+    kp, vp, q, kn, vn, f = decode_big_inputs(b, L, seed)
+    cos, sin = O.rope_tables(64, L + 64)
+    qr = O.apply_rope(q[:, None].astype(np.float64), cos, sin, L - 1)[:, 0]
+    kr = O.apply_rope(kn[:, None].astype(np.float64), cos, sin, L - 1)[:, 0]
+    k_all = np.concatenate([kp, kr[:, None].astype(np.float32)], axis=1).transpose(0, 2, 1, 3)
+    v_all = np.concatenate([vp, vn[:, None]], axis=1).transpose(0, 2, 1, 3)
+    reps = O.compress_blocks(k_all.transpose(0, 2, 1, 3), 64)
+    sel, cnt = O.decode_select(f, reps, L, 64, 8, b, 4, "forecast", rule)
+    return qr, k_all, v_all, sel, cnt
+
+
+@pytest.mark.parametrize("case", ["L16385_abs", "L16448_abs", "L16400_ref", "L1000_abs", "L641_abs"])
+def test_decode_big_cases(golden, case):
+    """Decode steps at BASELINE config-2 lengths (16,385-16,448 cached tokens).
+    Absolute rule: every score is finite, so the oracle's selected set equals
+    the reference's and its output matches unconditioned.  Reference rule:
+    attention on the reference's captured lists (its -inf tie order is
+    implementation-defined) and the sink/current blocks in both sets."""
+    from tests.golden.make_golden import DECODE_BIG_CASES
+    name, b, L, rule, seed = [c for c in DECODE_BIG_CASES if c[0] == case][0]
+    g = golden("decode_big")
+    qr, k_all, v_all, sel, cnt = _decode_big_oracle(b, L, rule, seed)
+    rsel, rcnt = _ref_lists(g[case + "_sel"], g[case + "_valid"])
+    curr = (L - 1) // 64
+    out_ref_lists = O.decode_attention(qr, k_all, v_all, rsel, rcnt, L, 64)
+    np.testing.assert_allclose(out_ref_lists, g[case + "_out"], rtol=0, atol=2e-6)
+    for ix in np.ndindex(b, 4):
+        ref_set = set(rsel[ix][:rcnt[ix]].tolist())
+        mine = set(sel[ix][:cnt[ix]].tolist())
+        assert {0, curr} <= ref_set and {0, curr} <= mine
+        if rule == "absolute":
+            assert mine == ref_set, ix
+    if rule == "absolute":
+        out = O.decode_attention(qr, k_all, v_all, sel, cnt, L, 64)
+        np.testing.assert_allclose(out, g[case + "_out"], rtol=0, atol=2e-6)
+
+
+def test_model_sparse_regime_logits(golden):
+    """Oracle model (prefill, then decode with the absolute rule) vs the
+    reference model past the dense fallback: layer L's forecast selects layer
+    L+1's blocks in every decode step.  Logits and every layer's selected set."""
+    from tests.golden.make_golden import MODEL_SPARSE_PREFILL, MODEL_SPARSE_STEPS
+    g = golden("model_sparse")
+    sc = SmallModelConfig()
+    m = O.OracleModel(model_state(sc, seed=9), n_layer=sc.n_layer, max_seq_len=1024, rule="absolute",
+                      dtype=np.float64)
+    ids = g["ids"].astype(np.int64)
+    b = ids.shape[0]
+    p = MODEL_SPARSE_PREFILL
+    kc = [np.zeros((b, 4, 1024, 64)) for _ in range(sc.n_layer)]
+    vc = [np.zeros((b, 4, 1024, 64)) for _ in range(sc.n_layer)]
+    np.testing.assert_allclose(m.prefill(ids[:, :p], kc, vc), g["prefill_last"], rtol=0, atol=2e-4)
+    sel_ref = g["sel"].astype(np.int64)
+    for s in range(MODEL_SPARSE_STEPS):
+        lg = m.decode_step(ids[:, p + s], kc, vc, p + s)
+        if f"step{s}" in g:
+            np.testing.assert_allclose(lg, g[f"step{s}"], rtol=0, atol=2e-4, err_msg=f"step {s}")
+        curr = (p + s) // 64
+        for li in range(sc.n_layer):
+            rsel, rcnt = _ref_lists(sel_ref[s, li], g["valid"][s, li])
+            sel, cnt = m.last_sel[li]
+            for ix in np.ndindex(b, 4):
+                st = set(rsel[ix][:rcnt[ix]].tolist())
+                assert {0, curr} <= st and len(st) <= 10
+                assert set(sel[ix][:cnt[ix]].tolist()) == st, (s, li, ix)
+
+
+def test_chunked_prefill_32k(golden):
+    """Config-3 length (T=32,768): oracle attention on the reference's own
+    per-q-block lists vs its output rows, and the oracle's lists equal the
+    reference's wherever the union needs no truncation."""
+    from tests.golden.make_golden import CHUNKED_BIG, CHUNKED_BIG_ROW_EVERY
+    name, b, t, seed = CHUNKED_BIG
+    g = golden("chunked_big")
+    q = normal((b, 12, t, 64), seed=seed)
+    k = normal((b, 4, t, 64), seed=seed + 1)
+    v = normal((b, 4, t, 64), seed=seed + 2)
+    f = normal((b, t, 4, 64), seed=seed + 3)
+    rsel, rcnt = _ref_lists(g["sel"].astype(np.int64), g["valid"])
+    out = O.chunked_attention(q, k, v, rsel, rcnt, 64).transpose(0, 2, 1, 3)
+    np.testing.assert_allclose(out[:, ::CHUNKED_BIG_ROW_EVERY], g["rows"], rtol=0, atol=2e-5)
+    np.testing.assert_allclose(out.sum(axis=(2, 3)), g["row_sum"], rtol=0, atol=5e-4)
+    reps = O.compress_blocks(k.transpose(0, 2, 1, 3), 64)
+    sel, cnt, union = O.chunked_select(f, reps, t, 64, 8, b, 4, "forecast")
+    nb = O.num_blocks(t, 64)
+    n_same = n_trunc = 0
+    for ix in np.ndindex(b, 4, nb):
+        u = set(np.nonzero(union[ix])[0].tolist())
+        ref_set = set(rsel[ix][:rcnt[ix]].tolist())
+        mine = set(sel[ix][:cnt[ix]].tolist())
+        assert ref_set <= u and len(ref_set) == min(10, len(u))
+        if len(u) <= 10:
+            assert mine == ref_set
+            n_same += 1
+        else:
+            n_trunc += 1
+    assert n_same > 0 and n_trunc > 0
+
+
+@pytest.mark.parametrize("case", ["L1000", "L1023", "L1024", "L3000"])
+def test_prefetch_selection_absolute(golden, case):
+    """The reference's prefetch selection (before the append, async_offload.py:
+    241-260) under the absolute rule: every score is finite, so the oracle's
+    selected set equals the reference's."""
+    from tests.golden.make_golden import PREFETCH_ABS_CASES
+    name, b, L, li, seed = [c for c in PREFETCH_ABS_CASES if c[0] == case][0]
+    g = golden("prefetch_abs")
+    k = normal((b, L, 4, 64), seed=seed)
+    f = normal((b, 1, 4, 64), seed=seed + 2)
+    small, sel, cnt = O.prefetch_select(f, k, L, 64, 8, li, rule="absolute")
+    assert bool(small) == bool(g[case + "_small"])
+    assert not small
+    rsel, rcnt = _ref_lists(g[case + "_sel"], g[case + "_val"] > 0.5)
+    for ix in np.ndindex(b, 4):
+        assert set(sel[ix][:cnt[ix]].tolist()) == set(rsel[ix][:rcnt[ix]].tolist()), ix
