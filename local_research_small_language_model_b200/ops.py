@@ -212,6 +212,17 @@ def kv_append(xk: torch.Tensor, xv: torch.Tensor, k_store: torch.Tensor, v_store
            k_store.shape[2], proto_sum.shape[2], start, block_size, _stream(xk))
 
 
+def _rope_tables(cos: torch.Tensor, sin: torch.Tensor, head_dim: int, need: int) -> None:
+    """The fused decode kernels read fp32 tables [max_pos, head_dim / 2] at the
+    new token's position; anything else would be read as fp32 and past its end."""
+    for tb in (cos, sin):
+        if tb.dtype != torch.float32 or not tb.is_contiguous() or tb.dim() != 2 or tb.shape[1] != head_dim // 2:
+            raise TypeError(f"RoPE tables must be contiguous fp32 [max_pos, {head_dim // 2}], got "
+                            f"{tb.dtype} {tuple(tb.shape)}")
+    if cos.shape != sin.shape or cos.shape[0] < need:
+        raise ValueError(f"RoPE tables cover {cos.shape[0]} positions; the cache needs {need}")
+
+
 def decode_layer(qkv: torch.Tensor, forecast: Optional[torch.Tensor], rope_cos: torch.Tensor,
                  rope_sin: torch.Tensor, cur_len: torch.Tensor, k_store: torch.Tensor, v_store: torch.Tensor,
                  proto_sum: torch.Tensor, n_head: int, n_kv_head: int, block_size: int, top_k: int,
@@ -232,6 +243,7 @@ def decode_layer(qkv: torch.Tensor, forecast: Optional[torch.Tensor], rope_cos: 
     (cand_idx, cand_val) pair decode_candidates produced for this step.
     Returns [B,Hq*D]."""
     _cuda(qkv, forecast, rope_cos, rope_sin, cur_len, k_store, v_store, proto_sum)
+    _rope_tables(rope_cos, rope_sin, k_store.shape[-1], k_store.shape[2])
     b = qkv.shape[0]
     d = k_store.shape[-1]
     qkv = _inner1(qkv)
@@ -327,6 +339,7 @@ def decode_layer_offload(qkv: torch.Tensor, forecast: Optional[torch.Tensor], ro
     attention reads the sink, current and prefetched slots.  Forecast steps
     need ``cand`` (and the slots offload_prefetch assigned to it)."""
     _cuda(qkv, forecast, rope_cos, rope_sin, cache.slot_k)
+    _rope_tables(rope_cos, rope_sin, cache.slot_k.shape[-1], cache.tcap)
     b = qkv.shape[0]
     d = cache.slot_k.shape[-1]
     hkv = cache.n_kv_head

@@ -58,6 +58,20 @@ class RotaryEmbedding(nn.Module):
             self.cos = cos.to(device)
             self.sin = sin.to(device)
 
+    def _apply(self, fn, *args, **kwargs):
+        """Module.to(dtype) would cast the tables too (the reference's buffers
+        become e.g. bf16 under model.to(torch.bfloat16)).  They stay fp32 here:
+        the fused decode kernel reads fp32 tables and rounds each entry to the
+        activation dtype, and apply_rotary_emb casts with type_as, so results
+        equal the reference's cast tables while the kernel never sees a 16-bit
+        buffer where it expects fp32."""
+        super()._apply(fn, *args, **kwargs)
+        if self.cos.dtype != torch.float32 or self.sin.dtype != torch.float32:
+            cos, sin = precompute_rope_freqs(self.head_dim, self.max_seq_len, self.theta)
+            self.cos = cos.to(self.cos.device)
+            self.sin = sin.to(self.sin.device)
+        return self
+
     def ensure(self, seq_len: int) -> None:
         """Grows the tables so positions < seq_len are covered."""
         self._extend_cache(seq_len, self.cos.device)

@@ -103,3 +103,22 @@ def test_install_into_reference_model():
 def test_selector_rule_validation():
     with pytest.raises(ValueError):
         sd.B200SparseAttention(sd.ModelConfig(), 1, rule="bogus")
+
+
+def test_rope_tables_stay_fp32_under_module_cast():
+    """model.to(bfloat16) must not turn the RoPE tables into 16-bit buffers: the
+    fused decode kernel reads them as fp32 (a 16-bit table would be misread and
+    read past its end).  The boundary check rejects such tables outright."""
+    from local_research_small_language_model_b200 import ops
+    rot = sd.RotaryEmbedding(64, 256).to(torch.bfloat16)
+    assert rot.cos.dtype == torch.float32 and rot.sin.dtype == torch.float32
+    ref_cos, _ = sd.rope.precompute_rope_freqs(64, 256)
+    assert torch.equal(rot.cos, ref_cos)
+    from local_research_small_language_model_b200.model import SparDAB200Model
+    m = SparDAB200Model(sd.ModelConfig(n_layer=1, vocab_size=64)).to(torch.bfloat16)
+    assert m.rotary_emb.cos.dtype == torch.float32
+    with pytest.raises(TypeError):
+        ops._rope_tables(rot.cos.to(torch.bfloat16), rot.sin.to(torch.bfloat16), 64, 128)
+    with pytest.raises(ValueError):
+        ops._rope_tables(rot.cos, rot.sin, 64, 1024)
+    ops._rope_tables(rot.cos, rot.sin, 64, 256)
