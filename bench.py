@@ -57,6 +57,8 @@ def parse():
     ap.add_argument("--selection", choices=["kernel", "side-stream", "chain"], default="chain",
                     help="forecast selection inside the fused decode kernel, layer L+1's candidates computed on a "
                          "side stream during layer L, or at the end of layer L's fused kernel")
+    ap.add_argument("--pdl", choices=["on", "off"], default="off",
+                    help="programmatic dependent launch of the library's decode-step kernels")
     ap.add_argument("--e2e-steps", type=int, default=1024)
     ap.add_argument("--probe-steps", type=int, default=64)
     ap.add_argument("--cpu-seqs", type=int, default=1, help="sequences per CPU worker thread")
@@ -229,6 +231,7 @@ def run_b200(args, rank, world, local):
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     torch.manual_seed(1234 + rank)
+    ops.set_programmatic_launch(args.pdl == "on")
     B, ctx, W = args.batch, args.ctx, args.window
     cfg = ModelConfig(block_size=64, top_k_blocks=8, context_length=4096, selector_rule=args.rule,
                       n_layer=args.layers)
@@ -400,7 +403,7 @@ def run_b200(args, rank, world, local):
                    "model": "SparDA-102.45M (12L, 768, 12q/4kv x 64, SwiGLU 2048, vocab 32000)",
                    "global_batch": B * world, "per_gpu_batch": B, "seq_len": ctx,
                    "ctx_window": [ctx + 1, ctx + W], "block_size": 64, "top_k": 8,
-                   "selector_rule": args.rule, "selection": args.selection,
+                   "selector_rule": args.rule, "selection": args.selection, "pdl": args.pdl,
                    "parallelism": f"batch-shard x{world}, no collective",
                    "l2": "no flush: per-step working set (~0.9 GB of weights, prototypes and selected KV) "
                          "exceeds the 126 MB L2"},

@@ -249,6 +249,19 @@ SD_API int sd_silu_mul(const void *gu, int dtype, int64_t rows, int64_t F, int64
 /* lens[i] += delta for i < n (device int32 array). */
 SD_API int sd_advance_len(int32_t *lens, int n, int delta, void *stream);
 
+/* Programmatic dependent launch, process-wide, off by default; returns the
+ * previous setting.  When on, sd_decode_layer, sd_rmsnorm, sd_silu_mul and
+ * sd_advance_len launch with programmatic stream serialization: a kernel may
+ * start while the kernel ahead of it on the stream is still running, and waits
+ * for that kernel's completion (griddepcontrol.wait) before it reads anything.
+ * sd_decode_layer's first warp reads the candidates, block sums, cached K/V
+ * tiles and cur_len before that wait, so with the switch on those inputs must
+ * have been written by kernels that finished before the kernel ahead of it
+ * started (true when that kernel was launched without this attribute, as a
+ * library GEMM is).  No counterpart in the reference (a launch-latency
+ * optimisation of the CUDA path). */
+SD_API int sd_set_programmatic_launch(int enable);
+
 /* ---- offloaded KV caches (model/attention/offload.py, async_offload.py) ----
  * The authoritative K/V rows live in pinned host memory host_k/host_v
  * [B, Hkv, host_tcap, 64] (block-major, read and written by the GPU through

@@ -1,11 +1,16 @@
 // Library-wide entry points: error text, version, last CUDA error, length bump.
 #include <math.h>
 
+#include <atomic>
+
 #include "sd_common.cuh"
 
 namespace sd {
 
 static thread_local int g_last_cuda_error = 0;
+static std::atomic<int> g_pdl{0};
+
+bool pdl_enabled() { return g_pdl.load(std::memory_order_relaxed) != 0; }
 
 void set_cuda_error(cudaError_t e) { g_last_cuda_error = static_cast<int>(e); }
 
@@ -32,6 +37,7 @@ int set_max_smem_raw(const void *func, size_t bytes) {
 }
 
 __global__ void advance_len_kernel(int32_t *lens, int n, int delta) {
+  pdl_wait();
   int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) lens[i] += delta;
 }
@@ -57,8 +63,10 @@ int sd_last_cuda_error(void) { return sd::g_last_cuda_error; }
 
 int sd_advance_len(int32_t *lens, int n, int delta, void *stream) {
   if (!lens || n <= 0) return SD_ERR_INVALID;
-  sd::advance_len_kernel<<<(n + 127) / 128, 128, 0, static_cast<cudaStream_t>(stream)>>>(lens, n, delta);
-  return sd::check_launch();
+  return sd::launch(sd::advance_len_kernel, dim3((n + 127) / 128), dim3(128), 0, static_cast<cudaStream_t>(stream),
+                    sd::pdl_enabled(), lens, n, delta);
 }
+
+int sd_set_programmatic_launch(int enable) { return sd::g_pdl.exchange(enable != 0 ? 1 : 0); }
 
 }  // extern "C"

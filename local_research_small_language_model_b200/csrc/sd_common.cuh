@@ -26,6 +26,39 @@ template <typename K> int set_max_smem(K *func, size_t bytes) {
   return set_max_smem_raw(reinterpret_cast<const void *>(func), bytes);
 }
 
+// Programmatic dependent launch (sd_set_programmatic_launch): when enabled,
+// the kernels that support it are launched so they may start before the
+// kernel ahead of them on the stream has finished; each waits (pdl_wait) before
+// it reads anything that kernel wrote.
+bool pdl_enabled();
+
+// Launches kern<<<grid, block, smem, s>>>(args...), with programmatic stream
+// serialization when `pdl` is set; returns SD_OK or SD_ERR_CUDA.
+template <typename... KArgs, typename... Args>
+int launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl, Args &&...args) {
+  if (!pdl) {
+    kern<<<grid, block, smem, s>>>(static_cast<KArgs>(args)...);
+    return check_launch();
+  }
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+  if (e != cudaSuccess) {
+    set_cuda_error(e);
+    cudaGetLastError();
+    return SD_ERR_CUDA;
+  }
+  return check_launch();
+}
+
 // ---------------------------------------------------------------- conversions
 template <typename T> __device__ __forceinline__ float to_f(T x);
 template <> __device__ __forceinline__ float to_f<float>(float x) { return x; }
@@ -41,6 +74,11 @@ template <> __device__ __forceinline__ __half from_f<__half>(float x) { return _
 template <typename T> __device__ __forceinline__ float round_to(float x) { return to_f<T>(from_f<T>(x)); }
 
 // ---------------------------------------------------------------- PTX wrappers
+// Waits until the kernel ahead of this one on the stream has completed and its
+// writes are visible; returns at once when this kernel was not launched with
+// programmatic stream serialization.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -33,11 +33,29 @@ namespace sd {
 
 constexpr int kD = 64;          // head_dim the attention kernels implement
 constexpr int kRows = 64;       // rows per tile
-constexpr int kStages = 4;
-constexpr int kThreads = 128;
+constexpr int kStages = 5;
+constexpr int kThreads = 128;  // the attention warps
 constexpr int kWarps = kThreads / 32;
 constexpr int kMaxTiles = 256;
 constexpr float kLog2e = 1.4426950408889634f;
+
+// The attention warps (the first kThreads threads) synchronise on named
+// barrier 1, so a CTA may carry further warps (the fused kernel's next-layer
+// scoring warps) that never join these barriers.  With exactly kThreads
+// threads this is the same as __syncthreads().
+__device__ __forceinline__ void attn_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kThreads) : "memory"); }
+__device__ __forceinline__ bool attn_sync_or(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, 1, %2, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(v)), "n"(kThreads)
+      : "memory");
+  return r != 0;
+}
 
 template <typename T> __host__ __device__ constexpr bool is16() { return sizeof(T) == 2; }
 
@@ -199,7 +217,7 @@ __device__ __forceinline__ void issue_tile(AttnSmem<T, G> &S, int t, const Ld &l
 // Merges the per-warp states written to S.red and stores out[g*o_hs + d].
 template <typename T, int G>
 __device__ __forceinline__ void combine_store(AttnSmem<T, G> &S, T *out, int64_t o_hs) {
-  for (int e = threadIdx.x; e < G * kD; e += blockDim.x) {
+  for (int e = threadIdx.x; e < G * kD; e += kThreads) {
     const int g = e / kD, d = e - g * kD;
     float M = -INFINITY;
 #pragma unroll
@@ -230,7 +248,7 @@ __device__ __forceinline__ bool wait_tile(uint64_t *full, int t) {
 template <typename T, int G>
 __device__ __forceinline__ void drain(AttnSmem<T, G> &S, int t, int ntiles) {
   for (int u = t; u < ntiles && u < t + kStages; ++u) mbar_wait_bounded(&S.full[u % kStages], (u / kStages) & 1);
-  __syncthreads();
+  attn_sync();
 }
 
 // Writes the new token's K/V rows (S.newkv) into row `row` of staged tile t,
@@ -249,7 +267,7 @@ __device__ __forceinline__ void patch_tile_rows(AttnSmem<T, G> &S, int t, int ro
     // the stage is refilled by the async proxy later: order these writes first
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
-  __syncthreads();
+  attn_sync();
 }
 
 // ---------------------------------------------------------------- CUDA-core path
@@ -336,7 +354,7 @@ __device__ bool attend_simt(AttnSmem<T, G> &S, int ntiles, int pre_issued, const
         }
       }
     }
-    if (__syncthreads_or(!got)) {
+    if (attn_sync_or(!got)) {
       drain(S, t, ntiles);
       return false;
     }
@@ -352,7 +370,7 @@ __device__ bool attend_simt(AttnSmem<T, G> &S, int ntiles, int pre_issued, const
     rw[g * (kD + 2) + 2 + 2 * lane] = acc[g][0];
     rw[g * (kD + 2) + 3 + 2 * lane] = acc[g][1];
   }
-  __syncthreads();
+  attn_sync();
   combine_store(S, out, o_hs);
   return true;
 }
@@ -444,7 +462,7 @@ __device__ bool attend_mma(AttnSmem<T, G> &S, int ntiles, int pre_issued, const 
         mma16816<T>(o[2 * qd + 1], pa, r2, r3);
       }
     }
-    if (__syncthreads_or(!got)) {
+    if (attn_sync_or(!got)) {
       drain(S, t, ntiles);
       return false;
     }
@@ -463,7 +481,7 @@ __device__ bool attend_mma(AttnSmem<T, G> &S, int ntiles, int pre_issued, const 
       r[3 + 8 * n + 2 * tig] = o[n][1];
     }
   }
-  __syncthreads();
+  attn_sync();
   combine_store(S, out, o_hs);
   return true;
 }
@@ -584,7 +602,7 @@ template <typename T> struct SlotMap {
 };
 
 template <typename T, typename F, int G>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(2 * kThreads)
     decode_layer_kernel(const T *__restrict__ qkv, int64_t qkv_sb, const F *__restrict__ fc, int64_t f_sb,
                         const float *__restrict__ rcos, const float *__restrict__ rsin,
                         const int32_t *__restrict__ cur_len, T *k_cache, T *v_cache, float *proto_sum, int Hkv,
@@ -595,11 +613,7 @@ __global__ void __launch_bounds__(kThreads)
                         int32_t *sel_out, int32_t *cnt_out, int sel_cap, int32_t *err, const SlotMap<T> sm,
                         const NextCand nx) {
   extern __shared__ __align__(1024) char smem_raw[];
-  AttnSmem<T, G> S(smem_raw);
-  LayerTail X(S.tail, NBcap, top_k);
   const bool slots = sm.host_k != nullptr;
-  __shared__ int count, ntiles, pre, patch_t, patch_row;
-  __shared__ __align__(8) uint64_t proto_bar;  // completion of the staged prototype rows
   const int b = blockIdx.x / Hkv, h = blockIdx.x - (blockIdx.x / Hkv) * Hkv;
   const int Hq = Hkv * G;
   const int64_t pos = *cur_len;
@@ -612,8 +626,45 @@ __global__ void __launch_bounds__(kThreads)
   const int nb = curr + 1;
   const int ms = nb < top_k + 2 ? nb : top_k + 2;
   const int kk = top_k < nb ? top_k : nb;
-  const bool use_f = fc != nullptr && nb > ms;  // a forecast-driven selection is needed
   const int64_t bh = static_cast<int64_t>(b) * Hkv + h;
+
+  // -- next-layer scoring warps (present only when nx.proto != nullptr): the
+  //    next layer's candidates for its coming step, top-k over its blocks
+  //    0..curr-1 (it caches as many tokens as this layer; its sums do not
+  //    change before its own step, and its forecast is this layer's
+  //    projection).  They run from the kernel's start, beside the attention
+  //    warps' tile ring, and share nothing with them but the CTA.
+  if (threadIdx.x >= kThreads) {
+    __shared__ float nsv[kWarps * 32];
+    __shared__ int nsi[kWarps * 32];
+    const WarpGroup g{kWarps, static_cast<int>(blockDim.x >> 5) - kWarps, 2};
+    int32_t *oi = nx.cand_idx + bh * top_k;
+    float *ov = nx.cand_val + bh * top_k;
+    if (nb <= ms) {  // its step is dense: no candidates needed
+      for (int r = threadIdx.x - kThreads; r < top_k; r += g.nw * 32) {
+        oi[r] = -1;
+        ov[r] = -INFINITY;
+      }
+      return;
+    }
+    pdl_wait();  // the forecast rows come from the projection kernel ahead
+    const T *fr = static_cast<const T *>(nx.fc) + b * nx.f_sb + h * kD;
+    const int l16 = threadIdx.x & 15;
+    const float4 fv =
+        make_float4(to_f(fr[4 * l16]), to_f(fr[4 * l16 + 1]), to_f(fr[4 * l16 + 2]), to_f(fr[4 * l16 + 3]));
+    const int nsc = rule == SD_RULE_REFERENCE ? 1 : curr;
+    const float *base = nx.proto + bh * NBcap * kD;
+    group_score_topk([&](int j) { return base + static_cast<int64_t>(j) * kD; }, fv, curr, nsc, -1, sel_scale,
+                     top_k, oi, ov, nsv, nsi, g);
+    return;
+  }
+
+  AttnSmem<T, G> S(smem_raw);
+  LayerTail X(S.tail, NBcap, top_k);
+  __shared__ int count, ntiles, pre, patch_t, patch_row, disp_t;
+  __shared__ __align__(8) uint64_t proto_bar;  // completion of the staged prototype rows
+  const bool use_f = fc != nullptr && nb > ms;  // a forecast-driven selection is needed
+  const WarpGroup ag{0, kWarps, 1};             // the attention warps
   const T *kb = k_cache + bh * Tcap * kD;
   const T *vb = v_cache + bh * Tcap * kD;
   const BulkLoader<T> bulk{kb, vb, kD};
@@ -626,12 +677,16 @@ __global__ void __launch_bounds__(kThreads)
     }
   };
 
-  // -- 0. stage every tile that is known now: the whole list on dense and
-  //       static-window steps, the sink and current blocks otherwise
-  //       (warp 0 does it in parallel: lane s initialises stage barrier s and
-  //       issues tile s; with block_size <= 64 every block is one tile and
-  //       tile t's block is arithmetic, so no list is built here)
+  // -- 0. stage every tile that is known now (warp 0, in parallel lanes: lane
+  //       s initialises stage barrier s and issues tile s).  With block_size
+  //       <= 64 every block is one tile and tile t's block is known without a
+  //       list: the whole window on dense and static-window steps; on forecast
+  //       steps with precomputed candidates the sink, the current block and
+  //       every candidate in rank order (the candidate ranked last is loaded
+  //       too and dropped in phase 2 if the current block's fresh score
+  //       displaces it); with in-kernel selection the sink and current block.
   const bool one_tile = bs <= kRows;
+  const bool early_cands = use_f && one_tile && cand_idx != nullptr && kk <= 32;
   // In-kernel forecast selection stages the running sums of blocks
   // 0..nstage-1 (every cached block but the current one, whose sum changes
   // below) into the stage buffers 2..kStages-1, which hold no tile until the
@@ -640,6 +695,10 @@ __global__ void __launch_bounds__(kThreads)
   const int stage_cap = ProtoStage<T>::kRowsPerHalf * 2;
   const bool stage_protos = use_f && one_tile && cand_idx == nullptr && kk <= 32 && rule != SD_RULE_REFERENCE;
   const int nstage = stage_protos ? (curr < stage_cap ? curr : stage_cap) : 0;
+  // warp 0 keeps the precomputed candidates of its lanes (rank = lane) for
+  // the merge in phase 2
+  int cj = -1;
+  float cv = -INFINITY;
   if (threadIdx.x < 32) {
     const int lane = threadIdx.x;
     if (lane < kStages) mbar_init(&S.full[lane], 1);
@@ -655,7 +714,7 @@ __global__ void __launch_bounds__(kThreads)
         bulk_g2s(ProtoStage<T>::v_half(S), src + static_cast<int64_t>(n0) * kD, (nstage - n0) * kD * sizeof(float),
                  &proto_bar);
     }
-    int nt = 0;
+    int nt = 0, dt = -1, p = 0;
     if (one_tile) {
       int lo = 0;  // static window: {0} U {lo..curr}
       if (use_f) {
@@ -682,66 +741,120 @@ __global__ void __launch_bounds__(kThreads)
         S.tile_tok[t] = src * bs;
         S.tile_n[t] = static_cast<int>(n < bs ? n : bs);
       }
-    } else if (lane == 0) {
-      if (!use_f) {
-        if (nb <= ms) {
-          for (int j = 0; j < nb; ++j) X.list[j] = j;
-          count = nb;
-        } else {
-          count = assemble_decode_list(false, nullptr, 0, nb, curr, top_k, X.list);
+      __syncwarp();
+      // the tiles known without any load go out first
+      p = nt < kStages ? nt : kStages;
+      if (lane < p) issue(lane);
+      if (early_cands) {
+        // candidates are distinct blocks other than the current one; the sink
+        // is already staged, so it is skipped when it is a candidate
+        if (lane < kk) {
+          cj = cand_idx[bh * top_k + lane];
+          cv = cand_val[bh * top_k + lane];
         }
-        nt = build_tiles(X.list, count, L, bs, S.tile_tok, S.tile_n);
-      } else {
-        nt = add_block_tiles(0, L, bs, S.tile_tok, S.tile_n, 0);
-        nt = add_block_tiles(curr, L, bs, S.tile_tok, S.tile_n, nt);
+        const int cs = slots && lane < kk ? sm.cand_slot[bh * top_k + lane] : 0;
+        const bool keep = cj > 0 && cj < nb && cj != curr && cs >= 0 && (!slots || cs < sm.kslots);
+        const unsigned bal = __ballot_sync(0xffffffffu, keep);
+        const int slot = nt + __popc(bal & ((1u << lane) - 1u));
+        if (keep) {
+          const int64_t n = L - static_cast<int64_t>(cj) * bs;
+          S.tile_tok[slot] = (slots ? 2 + cs : cj) * bs;
+          S.tile_n[slot] = static_cast<int>(n < bs ? n : bs);
+        }
+        dt = __shfl_sync(0xffffffffu, keep ? slot : -1, kk - 1);  // tile of the last-ranked candidate
+        const int nt2 = nt + __popc(bal);
+        __syncwarp();
+        const int p2 = nt2 < kStages ? nt2 : kStages;
+        if (lane >= p && lane < p2) issue(lane);
+        nt = nt2;
+        p = p2;
       }
+    } else {
+      if (lane == 0) {
+        if (!use_f) {
+          if (nb <= ms) {
+            for (int j = 0; j < nb; ++j) X.list[j] = j;
+            count = nb;
+          } else {
+            count = assemble_decode_list(false, nullptr, 0, nb, curr, top_k, X.list);
+          }
+          nt = build_tiles(X.list, count, L, bs, S.tile_tok, S.tile_n);
+        } else {
+          nt = add_block_tiles(0, L, bs, S.tile_tok, S.tile_n, 0);
+          nt = add_block_tiles(curr, L, bs, S.tile_tok, S.tile_n, nt);
+        }
+      }
+      nt = __shfl_sync(0xffffffffu, nt, 0);
+      __syncwarp();
+      p = nt < kStages ? nt : kStages;
+      if (lane < p) issue(lane);
     }
-    nt = __shfl_sync(0xffffffffu, nt, 0);
-    __syncwarp();
-    const int p = nt < kStages ? nt : kStages;
-    if (lane < p) issue(lane);
     if (lane == 0) {
       pre = p;
       ntiles = nt;
+      disp_t = dt;
     }
   }
 
-  // -- 1. RoPE, append, compressor running sum
+  // -- 1. RoPE, append, compressor running sum, by warps 1..3 while warp 0
+  //       stages tiles: every thread issues all of its global loads before it
+  //       computes, so this phase costs one round trip.  Threads 32..95 take
+  //       element d of k, v, the block sum and the forecast; warp 3 takes q.
   const T *row = qkv + b * qkv_sb;
   const float *cr = rcos + pos * (kD / 2);
   const float *sr = rsin + pos * (kD / 2);
-  if (threadIdx.x < kD) {
-    const int d = threadIdx.x;
+  // q|k|v come from the projection kernel ahead on the stream; warp 0's tiles,
+  // candidates and sums were written by earlier kernels and need no wait
+  if (threadIdx.x >= 32) pdl_wait();
+  if (threadIdx.x >= 32 && threadIdx.x < 32 + kD) {
+    const int d = threadIdx.x - 32;
     const T *kr = row + static_cast<int64_t>(Hq + h) * kD;
-    const float x = to_f(kr[d]);
-    const float pr = to_f(kr[d < kD / 2 ? d + kD / 2 : d - kD / 2]);
-    const float y = rope_elem<T>(x, pr, d, cr[d & (kD / 2 - 1)], sr[d & (kD / 2 - 1)]);
+    float *ps = proto_sum + (bh * NBcap + curr) * kD + d;
+    const T kx = kr[d], kp = kr[d < kD / 2 ? d + kD / 2 : d - kD / 2];
     const T vv = row[static_cast<int64_t>(Hq + Hkv + h) * kD + d];
+    const float c = cr[d & (kD / 2 - 1)], sn = sr[d & (kD / 2 - 1)];
+    const float old = pos % bs == 0 ? 0.f : *ps;
+    const float fx = fc != nullptr ? to_f(fc[b * f_sb + h * kD + d]) : 0.f;
+    const float y = rope_elem<T>(to_f(kx), to_f(kp), d, c, sn);
     const int64_t off = (bh * Tcap + (slots ? bs + pos % bs : pos)) * kD + d;
     if (slots) {  // write-through to the host copy
       const int64_t hoff = (bh * sm.host_tcap + pos) * kD + d;
       sm.host_k[hoff] = from_f<T>(y);
-      sm.host_v[hoff] = row[static_cast<int64_t>(Hq + Hkv + h) * kD + d];
+      sm.host_v[hoff] = vv;
     }
     k_cache[off] = from_f<T>(y);
     v_cache[off] = vv;
     S.newkv[d] = from_f<T>(y);
     S.newkv[kD + d] = vv;
-    float *ps = proto_sum + (bh * NBcap + curr) * kD + d;
-    const float pn = (pos % bs == 0 ? 0.f : *ps) + y;
+    const float pn = old + y;
     *ps = pn;
     X.pnew[d] = pn;
-    if (fc != nullptr) X.f[d] = to_f(fc[b * f_sb + h * kD + d]);
-  } else {
-    for (int e = threadIdx.x - kD; e < G * kD; e += blockDim.x - kD) {
-      const int g = e / kD, d = e - g * kD;
-      const T *qr = row + static_cast<int64_t>(h * G + g) * kD;
-      const float x = to_f(qr[d]);
-      const float pr = to_f(qr[d < kD / 2 ? d + kD / 2 : d - kD / 2]);
-      S.q[e] = rope_elem<T>(x, pr, d, cr[d & (kD / 2 - 1)], sr[d & (kD / 2 - 1)]);
+    if (fc != nullptr) X.f[d] = fx;
+  } else if (threadIdx.x >= 32 + kD) {
+    constexpr int kQT = kThreads - 32 - kD;  // threads of the q part
+    constexpr int kPer = (G * kD + kQT - 1) / kQT;
+    const int q0 = threadIdx.x - 32 - kD;
+    T qx[kPer], qp[kPer];
+    float qc[kPer], qs[kPer];
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int e = q0 + i * kQT;
+      if (e < G * kD) {
+        const int g = e / kD, d = e - g * kD;
+        const T *qr = row + static_cast<int64_t>(h * G + g) * kD;
+        qx[i] = qr[d];
+        qp[i] = qr[d < kD / 2 ? d + kD / 2 : d - kD / 2];
+        qc[i] = cr[d & (kD / 2 - 1)];
+        qs[i] = sr[d & (kD / 2 - 1)];
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int e = q0 + i * kQT;
+      if (e < G * kD) S.q[e] = rope_elem<T>(to_f(qx[i]), to_f(qp[i]), e % kD, qc[i], qs[i]);
     }
   }
-  __syncthreads();
+  attn_sync();
 
   // -- 2. selection over this layer's prototypes (sum / bs)
   if (use_f) {
@@ -765,19 +878,28 @@ __global__ void __launch_bounds__(kThreads)
 #pragma unroll
         for (int o = 8; o > 0; o >>= 1) p += __shfl_xor_sync(0xffffffffu, p, o);
         const float vcur = curr < n_scored ? p * sel_scale : -INFINITY;
+        bool displaced = false;
         for (int r = lane; r < kk; r += 32) {
-          int j = cand_idx[bh * top_k + r];
-          float v = cand_val[bh * top_k + r];
+          // the candidates read in phase 0 (rank r = lane; kk > 32 reads the rest)
+          int j = early_cands ? cj : cand_idx[bh * top_k + r];
+          float v = early_cands ? cv : cand_val[bh * top_k + r];
           if (j < 0 || j >= nb || j == curr) {
             j = -1;
             v = -INFINITY;
           }
-          if (r == kk - 1 && (j < 0 || better(vcur, curr, v, j))) j = -1;  // displaced by the current block
+          if (r == kk - 1 && (j < 0 || better(vcur, curr, v, j))) {  // displaced by the current block
+            j = -1;
+            displaced = true;
+          }
           X.tk[r] = j;
         }
+        // the displaced candidate's tile (staged in phase 0) is not attended
+        if (__any_sync(0xffffffffu, displaced) && lane == 0 && disp_t >= 0) S.tile_n[disp_t] = 0;
       }
-      __syncthreads();
+      attn_sync();
     } else if (kk <= 32) {
+      __shared__ float asv[kWarps * 32];
+      __shared__ int asi[kWarps * 32];
       const float4 fq = reinterpret_cast<const float4 *>(X.f)[threadIdx.x & 15];
       const float *gsum = proto_sum + bh * NBcap * kD;
       if (nstage > 0) {
@@ -786,26 +908,28 @@ __global__ void __launch_bounds__(kThreads)
           mbar_wait_bounded(&proto_bar, 0);  // let the copy land before the region is reused
         }
         const float *kh = ProtoStage<T>::k_half(S), *vh = ProtoStage<T>::v_half(S);
-        auto row = [&](int j) -> const float * {
+        auto prow = [&](int j) -> const float * {
           if (j < nstage)
             return j < ProtoStage<T>::kRowsPerHalf ? kh + j * kD : vh + (j - ProtoStage<T>::kRowsPerHalf) * kD;
           return j == curr ? X.pnew : gsum + static_cast<int64_t>(j) * kD;
         };
-        cta_score_topk_rows(row, fq, nb, n_scored, -1, sel_scale, kk, X.tk, nullptr);
+        group_score_topk(prow, fq, nb, n_scored, -1, sel_scale, kk, X.tk, nullptr, asv, asi, ag);
         // the region is refilled with tiles by the async proxy next
         if (threadIdx.x == 0) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       } else {
-        cta_score_topk(gsum, kD, fq, nb, n_scored, -1, sel_scale, kk, X.tk, nullptr);
+        group_score_topk([&](int j) { return gsum + static_cast<int64_t>(j) * kD; }, fq, nb, n_scored, -1,
+                         sel_scale, kk, X.tk, nullptr, asv, asi, ag);
       }
     } else {
+      // top_k > 32: never launched with scoring warps, so the CTA is the
+      // attention warps and CTA-wide helpers apply
       score_blocks(proto_sum + bh * NBcap * kD, kD, kD, X.f, n_scored, sel_scale, X.sc);
       __syncthreads();
       cta_topk([&](int j) { return j < n_scored ? X.sc[j] : -INFINITY; }, nb, kk, X.tk);
     }
-    // tiles of the chosen blocks other than the sink and the current block
-    // (already staged), deduplicated and placed in ascending block order by
-    // one warp: a kept block's slot is the number of kept blocks below it
-    if (one_tile && kk <= 32) {
+    // in-kernel selection: tiles of the chosen blocks other than the sink and
+    // the current block (already staged), in rank order, placed by one warp
+    if (!early_cands && one_tile && kk <= 32) {
       if (threadIdx.x < 32) {
         const int lane = threadIdx.x;
         const int j = lane < kk ? X.tk[lane] : -1;
@@ -813,20 +937,21 @@ __global__ void __launch_bounds__(kThreads)
         const bool valid = j > 0 && j < nb && j != curr && cs >= 0 && (!slots || cs < sm.kslots);
         const unsigned same = __match_any_sync(0xffffffffu, valid ? j : -1 - lane);
         const bool keep = valid && (__ffs(same) - 1) == lane;
-        const int key = keep ? j : 0x7fffffff;
-        int rank = 0;
-#pragma unroll
-        for (int i = 0; i < 32; ++i) rank += __shfl_sync(0xffffffffu, key, i) < key;
+        const unsigned bal = __ballot_sync(0xffffffffu, keep);
         const int base = ntiles;
         if (keep) {
+          const int slot = base + __popc(bal & ((1u << lane) - 1u));
           const int64_t n = L - static_cast<int64_t>(j) * bs;
-          S.tile_tok[base + rank] = (slots ? 2 + cs : j) * bs;
-          S.tile_n[base + rank] = static_cast<int>(n < bs ? n : bs);
+          S.tile_tok[slot] = (slots ? 2 + cs : j) * bs;
+          S.tile_n[slot] = static_cast<int>(n < bs ? n : bs);
         }
-        const unsigned bal = __ballot_sync(0xffffffffu, keep);
+        __syncwarp();
         if (lane == 0) ntiles = base + __popc(bal);
       }
-    } else if (threadIdx.x == 0) {
+    } else if (!one_tile && threadIdx.x == 0) {
+      count = assemble_decode_list(true, X.tk, kk, nb, curr, top_k, X.list);
+      ntiles = build_tiles(X.list, count, L, bs, S.tile_tok, S.tile_n, ntiles, 0, curr);
+    } else if (one_tile && kk > 32 && threadIdx.x == 0) {
       count = assemble_decode_list(true, X.tk, kk, nb, curr, top_k, X.list);
       ntiles = build_tiles(X.list, count, L, bs, S.tile_tok, S.tile_n, ntiles, 0, curr);
     }
@@ -844,7 +969,7 @@ __global__ void __launch_bounds__(kThreads)
         }
     }
   }
-  __syncthreads();
+  attn_sync();
 
   // -- 3. attention over the selected blocks
   T *o = out + b * o_sb + static_cast<int64_t>(h * G) * kD;
@@ -868,29 +993,9 @@ __global__ void __launch_bounds__(kThreads)
         count = assemble_decode_list(false, nullptr, 0, nb, curr, top_k, X.list);
       }
     }
-    __syncthreads();
-    for (int i = threadIdx.x; i < sel_cap; i += blockDim.x) sel_out[bh * sel_cap + i] = i < count ? X.list[i] : -1;
+    attn_sync();
+    for (int i = threadIdx.x; i < sel_cap; i += kThreads) sel_out[bh * sel_cap + i] = i < count ? X.list[i] : -1;
     if (threadIdx.x == 0) cnt_out[bh] = count;
-  }
-
-  // -- 5. optional: the next layer's candidates for its coming step (top-k
-  //       over its blocks 0..curr-1; it caches as many tokens as this layer)
-  if (nx.proto != nullptr) {
-    int32_t *oi = nx.cand_idx + bh * top_k;
-    float *ov = nx.cand_val + bh * top_k;
-    if (nb <= ms) {  // its step is dense: no candidates needed
-      for (int r = threadIdx.x; r < top_k; r += blockDim.x) {
-        oi[r] = -1;
-        ov[r] = -INFINITY;
-      }
-    } else {
-      const T *fr = static_cast<const T *>(nx.fc) + b * nx.f_sb + h * kD;
-      const int l16 = threadIdx.x & 15;
-      const float4 fv = make_float4(to_f(fr[4 * l16]), to_f(fr[4 * l16 + 1]), to_f(fr[4 * l16 + 2]),
-                                    to_f(fr[4 * l16 + 3]));
-      const int nsc = rule == SD_RULE_REFERENCE ? 1 : curr;
-      cta_score_topk(nx.proto + bh * NBcap * kD, kD, fv, curr, nsc, -1, sel_scale, top_k, oi, ov);
-    }
   }
 }
 
@@ -956,12 +1061,15 @@ int launch_decode_layer(const void *qkv, int64_t qkv_sb, const void *fc, int64_t
   if (r != SD_OK) return r;
   auto kern = decode_layer_kernel<T, F, G>;
   if (set_max_smem(kern, smem) != SD_OK) return SD_ERR_CUDA;
-  kern<<<static_cast<unsigned>(B * Hkv), kThreads, smem, s>>>(
-      static_cast<const T *>(qkv), qkv_sb, static_cast<const F *>(fc), f_sb, rc, rs, cur_len,
-      static_cast<T *>(kc), static_cast<T *>(vc), ps, (int)Hkv, Tcap, NBcap, bs, top_k, rule,
-      scale / static_cast<float>(bs), scale * kLog2e, mk, mv, static_cast<T *>(out), o_sb, cand_idx, cand_val,
-      sel_out, cnt_out, sel_cap, err, sm, nx);
-  return check_launch();
+  // the next layer's candidates come from a second group of kThreads threads
+  const unsigned threads = nx.proto != nullptr ? 2 * kThreads : kThreads;
+  // offloaded caches depend on a prefetch joined through an event: no early start
+  const bool pdl = pdl_enabled() && sm.host_k == nullptr;
+  return launch(kern, dim3(static_cast<unsigned>(B * Hkv)), dim3(threads), smem, s, pdl,
+                static_cast<const T *>(qkv), qkv_sb, static_cast<const F *>(fc), f_sb, rc, rs, cur_len,
+                static_cast<T *>(kc), static_cast<T *>(vc), ps, (int)Hkv, Tcap, NBcap, bs, top_k, rule,
+                scale / static_cast<float>(bs), scale * kLog2e, mk, mv, static_cast<T *>(out), o_sb, cand_idx,
+                cand_val, sel_out, cnt_out, sel_cap, err, sm, nx);
 }
 
 }  // namespace sd

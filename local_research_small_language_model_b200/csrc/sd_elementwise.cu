@@ -10,6 +10,7 @@ namespace sd {
 template <typename T>
 __global__ void rmsnorm_kernel(const T *__restrict__ x, int64_t x_rs, const T *__restrict__ w, int C, float eps,
                                T *__restrict__ out, int64_t o_rs) {
+  pdl_wait();  // the input rows come from the kernel ahead
   const T *xr = x + blockIdx.x * x_rs;
   T *orow = out + blockIdx.x * o_rs;
   float ss = 0.f;
@@ -42,6 +43,7 @@ template <typename T>
 __global__ void __launch_bounds__(256) rmsnorm_rows_kernel(const T *__restrict__ x, int64_t x_rs,
                                                            const T *__restrict__ w, int C, float eps,
                                                            T *__restrict__ out, int64_t o_rs, int64_t rows) {
+  pdl_wait();  // the input rows come from the kernel ahead
   constexpr int kE = 16 / static_cast<int>(sizeof(T));  // elements per 16-byte chunk
   const int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -84,6 +86,7 @@ __global__ void __launch_bounds__(256) rmsnorm_rows_kernel(const T *__restrict__
 template <typename T>
 __global__ void rmsnorm_chunk_kernel(const T *__restrict__ x, int64_t x_rs, const T *__restrict__ w, int C,
                                      float eps, T *__restrict__ out, int64_t o_rs) {
+  pdl_wait();  // the input rows come from the kernel ahead
   constexpr int kE = 16 / static_cast<int>(sizeof(T));
   __shared__ float red[32];
   if (static_cast<int>(blockDim.x) * kE != C || (blockDim.x & 31u) != 0) return;  // contract broken: no writes
@@ -115,6 +118,7 @@ __global__ void rmsnorm_chunk_kernel(const T *__restrict__ x, int64_t x_rs, cons
 template <typename T>
 __global__ void silu_mul_kernel(const T *__restrict__ gu, int64_t g_rs, int F, T *__restrict__ out,
                                 int64_t o_rs) {
+  pdl_wait();  // the input rows come from the kernel ahead
   const T *g = gu + blockIdx.y * g_rs;
   T *o = out + blockIdx.y * o_rs;
   for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < F; c += gridDim.x * blockDim.x) {
@@ -131,31 +135,30 @@ extern "C" int sd_rmsnorm(const void *x, int dtype, int64_t rows, int64_t C, int
   if (!x || !w || !out || rows <= 0 || C <= 0) return SD_ERR_INVALID;
   if (rows > 0x7fffffff) return SD_ERR_UNSUPPORTED;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool pdl = sd::pdl_enabled();
   const int es = sd::dtype_size(dtype);
   if (rows >= 512 && (C * es) % 16 == 0 && (x_rs * es) % 16 == 0 && (o_rs * es) % 16 == 0 && sd::aligned16(x) &&
       sd::aligned16(w) && sd::aligned16(out)) {
     const unsigned grid = static_cast<unsigned>((rows + 7) / 8);
     SD_DISPATCH_DTYPE(dtype, E,
-                      sd::rmsnorm_rows_kernel<E><<<grid, 256, 0, s>>>(static_cast<const E *>(x), x_rs,
-                                                                      static_cast<const E *>(w), (int)C, eps,
-                                                                      static_cast<E *>(out), o_rs, rows));
-    return sd::check_launch();
+                      return sd::launch(sd::rmsnorm_rows_kernel<E>, dim3(grid), dim3(256), 0, s, pdl,
+                                        static_cast<const E *>(x), x_rs, static_cast<const E *>(w), (int)C, eps,
+                                        static_cast<E *>(out), o_rs, rows));
   }
   const int64_t chunks = C * es / 16;
   if ((C * es) % 16 == 0 && chunks % 32 == 0 && chunks <= 1024 && (x_rs * es) % 16 == 0 && (o_rs * es) % 16 == 0 &&
       sd::aligned16(x) && sd::aligned16(w) && sd::aligned16(out)) {
     SD_DISPATCH_DTYPE(dtype, E,
-                      sd::rmsnorm_chunk_kernel<E><<<static_cast<unsigned>(rows), static_cast<unsigned>(chunks), 0,
-                                                    s>>>(static_cast<const E *>(x), x_rs, static_cast<const E *>(w),
-                                                         (int)C, eps, static_cast<E *>(out), o_rs));
-    return sd::check_launch();
+                      return sd::launch(sd::rmsnorm_chunk_kernel<E>, dim3(static_cast<unsigned>(rows)),
+                                        dim3(static_cast<unsigned>(chunks)), 0, s, pdl, static_cast<const E *>(x), x_rs,
+                                        static_cast<const E *>(w), (int)C, eps, static_cast<E *>(out), o_rs));
   }
   const int threads = C >= 1024 ? 1024 : static_cast<int>(((C + 31) / 32) * 32);
   SD_DISPATCH_DTYPE(dtype, E,
-                    sd::rmsnorm_kernel<E><<<static_cast<unsigned>(rows), threads, 0, s>>>(
-                        static_cast<const E *>(x), x_rs, static_cast<const E *>(w), (int)C, eps,
-                        static_cast<E *>(out), o_rs));
-  return sd::check_launch();
+                    return sd::launch(sd::rmsnorm_kernel<E>, dim3(static_cast<unsigned>(rows)), dim3(threads), 0, s,
+                                      pdl, static_cast<const E *>(x), x_rs, static_cast<const E *>(w), (int)C, eps,
+                                      static_cast<E *>(out), o_rs));
+  return SD_OK;
 }
 
 extern "C" int sd_silu_mul(const void *gu, int dtype, int64_t rows, int64_t F, int64_t g_rs, void *out,
@@ -165,7 +168,8 @@ extern "C" int sd_silu_mul(const void *gu, int dtype, int64_t rows, int64_t F, i
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const unsigned gx = static_cast<unsigned>((F + 255) / 256 < 8 ? (F + 255) / 256 : 8);
   SD_DISPATCH_DTYPE(dtype, E,
-                    sd::silu_mul_kernel<E><<<dim3(gx, static_cast<unsigned>(rows)), 256, 0, s>>>(
-                        static_cast<const E *>(gu), g_rs, (int)F, static_cast<E *>(out), o_rs));
-  return sd::check_launch();
+                    return sd::launch(sd::silu_mul_kernel<E>, dim3(gx, static_cast<unsigned>(rows)), dim3(256), 0, s,
+                                      sd::pdl_enabled(), static_cast<const E *>(gu), g_rs, (int)F,
+                                      static_cast<E *>(out), o_rs));
+  return SD_OK;
 }

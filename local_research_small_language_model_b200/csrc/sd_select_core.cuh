@@ -96,6 +96,23 @@ __device__ __forceinline__ int assemble_decode_list(bool use_forecast, const int
   return n;
 }
 
+// ------------------------------------------------------------ warp groups
+// Whole warps [w0, w0 + nw) of a CTA that work together, synchronised by
+// named barrier `id` (0: the whole CTA through __syncthreads).  Lets one set of
+// warps score blocks while the others of the same CTA do something else.
+struct WarpGroup {
+  int w0, nw, id;
+  __device__ __forceinline__ int warp() const { return static_cast<int>(threadIdx.x >> 5) - w0; }
+  __device__ __forceinline__ void sync() const {
+    if (id == 0) {
+      __syncthreads();
+    } else {
+      asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nw * 32) : "memory");
+    }
+  }
+};
+__device__ __forceinline__ WarpGroup whole_cta() { return WarpGroup{0, static_cast<int>(blockDim.x >> 5), 0}; }
+
 // ------------------------------------------------------------ register top-k
 // Entry that is never chosen: loses every comparison, including -inf ties
 // (ties are ordered by ascending index).
@@ -173,15 +190,17 @@ template <int K2> __device__ __forceinline__ void merge_lanes(float &v, int &i) 
 // shuffle chain short; warp 0 merges the warps' lists the same way.  Writes
 // kk <= K2 (index, value) pairs best-first to out_idx (-1 when fewer than kk
 // entries exist) and out_val (nullable); NaN scores are never chosen.  All
-// threads of a CTA of at most 8 warps call it; it ends with a barrier.  fv:
-// the lane's float4 l16 of the fp32 forecast.  Rows are read with plain
+// threads of warp group g (at most 8 warps) call it; it ends with the group's
+// barrier.  sv, si: shared scratch of g.nw * K2 entries.  fv: the lane's
+// float4 l16 of the fp32 forecast.  Rows are read with plain
 // (coherent) loads: the fused decode kernel writes one of them earlier in the
 // same launch.
 template <int K2, typename Row>
 __device__ __forceinline__ void cta_score_topk_k2(Row row, float4 fv, int n, int n_scored, int excl, float mul,
-                                                  int kk, int *out_idx, float *out_val, float *sv, int *si) {
+                                                  int kk, int *out_idx, float *out_val, float *sv, int *si,
+                                                  const WarpGroup &g) {
   constexpr int kChunks = 4;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int lane = threadIdx.x & 31, warp = g.warp(), nw = g.nw;
   const int half = lane >> 4, l16 = lane & 15;
   if (n_scored > n) n_scored = n;
   float rv = -INFINITY;  // running best-first list of this warp (K2-lane groups)
@@ -246,7 +265,7 @@ __device__ __forceinline__ void cta_score_topk_k2(Row row, float4 fv, int n, int
     sv[warp * K2 + lane] = rv;
     si[warp * K2 + lane] = ri;
   }
-  __syncthreads();
+  g.sync();
   if (warp == 0) {
     const int total = nw * K2;
     float v = lane < total ? sv[lane] : -INFINITY;
@@ -261,7 +280,22 @@ __device__ __forceinline__ void cta_score_topk_k2(Row row, float4 fv, int n, int
       if (out_val) out_val[lane] = v;
     }
   }
-  __syncthreads();
+  g.sync();
+}
+
+// Scoring + top-kk (kk <= 32) by warp group g with caller-provided scratch
+// sv, si (g.nw * 32 entries each).
+template <typename Row>
+__device__ __forceinline__ void group_score_topk(Row row, float4 fv, int n, int n_scored, int excl, float mul, int kk,
+                                                 int *out_idx, float *out_val, float *sv, int *si,
+                                                 const WarpGroup &g) {
+  // two list widths keep the number of instantiations (and build time) small:
+  // a top-kk list is the first kk entries of the top-8 or top-32 list
+  if (kk <= 8) {
+    cta_score_topk_k2<8>(row, fv, n, n_scored, excl, mul, kk, out_idx, out_val, sv, si, g);
+  } else {
+    cta_score_topk_k2<32>(row, fv, n, n_scored, excl, mul, kk, out_idx, out_val, sv, si, g);
+  }
 }
 
 template <typename Row>
@@ -269,13 +303,7 @@ __device__ __forceinline__ void cta_score_topk_rows(Row row, float4 fv, int n, i
                                                     int kk, int *out_idx, float *out_val) {
   __shared__ float sv[8 * 32];  // the warps' lists, one buffer for every K2
   __shared__ int si[8 * 32];
-  // two list widths keep the number of instantiations (and build time) small:
-  // a top-kk list is the first kk entries of the top-8 or top-32 list
-  if (kk <= 8) {
-    cta_score_topk_k2<8>(row, fv, n, n_scored, excl, mul, kk, out_idx, out_val, sv, si);
-  } else {
-    cta_score_topk_k2<32>(row, fv, n, n_scored, excl, mul, kk, out_idx, out_val, sv, si);
-  }
+  group_score_topk(row, fv, n, n_scored, excl, mul, kk, out_idx, out_val, sv, si, whole_cta());
 }
 
 // cta_score_topk_rows over rows reps + j*r_sn (global memory).

@@ -443,3 +443,12 @@ def silu_mul(gu: torch.Tensor) -> torch.Tensor:
 def advance_len(lens: torch.Tensor, delta: int = 1) -> None:
     _cuda(lens)
     L.call("sd_advance_len", lens.data_ptr(), lens.numel(), delta, _stream(lens))
+
+
+def set_programmatic_launch(enable: bool) -> bool:
+    """Programmatic dependent launch for the decode-step kernels of this
+    library (sd_set_programmatic_launch): each may start while the kernel ahead
+    of it is finishing and waits for it before reading its output.  Meant for
+    the decode step, where every such kernel follows a library GEMM.  Returns
+    the previous setting."""
+    return bool(L.load().sd_set_programmatic_launch(int(bool(enable))))
