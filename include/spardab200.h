@@ -64,6 +64,15 @@ extern "C" {
 #define SD_RULE_REFERENCE 0
 #define SD_RULE_ABSOLUTE 1
 
+/* Selection timing, OR-ed into the `rule` of sd_decode_layer and
+ * sd_decode_layer_offload.  Default (flag clear): blocks are scored after the
+ * new token is appended, as SparseAttention and ForecastOffloadAttention do
+ * (model/attention/sparse.py:133-139, offload.py:175-227).  With the flag: the
+ * current block is scored with its sum before this step's token, and not at
+ * all when the token opens it, as AsyncForecastOffloadAttention.prefetch does
+ * (model/attention/async_offload.py:241-260, which selects one token ahead). */
+#define SD_SELECT_BEFORE_APPEND 0x100
+
 SD_API const char *sd_strerror(int code);
 SD_API int sd_version(void);
 /* cudaError_t of the last failing CUDA call made by this library on this thread. */

@@ -17,6 +17,7 @@ LIB_PATH = os.path.join(_HERE, "libspardab200.so")
 SD_OK = 0
 SD_DTYPE_F32, SD_DTYPE_BF16, SD_DTYPE_F16 = 0, 1, 2
 SD_RULE_REFERENCE, SD_RULE_ABSOLUTE = 0, 1
+SD_SELECT_BEFORE_APPEND = 0x100
 SD_KERR_TIMEOUT = 1
 
 _c_void_p = ctypes.c_void_p

@@ -46,7 +46,8 @@ class B200SparseAttention(BaseAttention):
     selector (see ops.RULES); the default reproduces the reference.
     """
 
-    def __init__(self, config, layer_idx: int, mode: Optional[str] = None, rule: Optional[str] = None):
+    def __init__(self, config, layer_idx: int, mode: Optional[str] = None, rule: Optional[str] = None,
+                 selection_timing: Optional[str] = None):
         super().__init__(config, layer_idx)
         self.block_size = config.block_size
         self.top_k_blocks = config.top_k_blocks
@@ -61,11 +62,18 @@ class B200SparseAttention(BaseAttention):
         self.rule = rule or getattr(config, "selector_rule", "reference")
         if self.rule not in ops.RULES:
             raise ValueError(f"unknown selector rule {self.rule!r}")
+        self.selection_timing = selection_timing or getattr(config, "selection_timing", "after_append")
+        if self.selection_timing not in ("after_append", "before_append"):
+            raise ValueError(f"unknown selection timing {self.selection_timing!r}")
         self.compressor = KVBlockCompressor(self.block_size, self.head_dim, config.forecast_dim)
         self.selector = ForecastBlockSelector(self.block_size, config.forecast_dim)
         self._packed = None
         self._packed_key = None
         self.last_profile = {}
+
+    @property
+    def before_append(self) -> bool:
+        return self.selection_timing == "before_append"
 
     # -- fused projection weight [wq; wk; wv], rebuilt when any weight changes
     def qkv_weight(self) -> torch.Tensor:
@@ -101,7 +109,7 @@ class B200SparseAttention(BaseAttention):
         f = forecast_vector if (self.mode == "forecast" and forecast_vector is not None) else None
         out = ops.decode_layer(qkv, f, rotary_emb.cos, rotary_emb.sin, cache.len_dev, cache.k_store,
                                cache.v_store, cache.proto_sum, self.n_head, self.n_kv_head, self.block_size,
-                               self.top_k_blocks, self.rule)
+                               self.top_k_blocks, self.rule, select_before_append=self.before_append)
         cache.advance(1, device=not getattr(cache, "shared_len", False))
         return self.wo(out.to(x.dtype)).view(b, 1, self.n_embd)
 
@@ -139,7 +147,8 @@ class B200SparseAttention(BaseAttention):
         f = forecast_vector if (self.mode == "forecast" and forecast_vector is not None) else None
         self.offload_ready(cache, f)
         out = ops.decode_layer_offload(qkv, f, rotary_emb.cos, rotary_emb.sin, cache, self.n_head, self.rule,
-                                       cand=cache.cand if f is not None else None)
+                                       cand=cache.cand if f is not None else None,
+                                       select_before_append=self.before_append)
         cache.prefetched = False
         cache.advance(1, device=not getattr(cache, "shared_len", False))
         return self.wo(out.to(x.dtype)).view(b, 1, self.n_embd)

@@ -29,6 +29,11 @@ class ModelConfig:
     # decode-time causal rule of the selector: "reference" (the reference's
     # literal behaviour, see ops.RULES) or "absolute"
     selector_rule: str = "reference"
+    # when decode scores the current block: "after_append" (SparseAttention and
+    # ForecastOffloadAttention, model/attention/sparse.py:133-139) or
+    # "before_append" (AsyncForecastOffloadAttention.prefetch,
+    # model/attention/async_offload.py:241-260)
+    selection_timing: str = "after_append"
 
     def __post_init__(self):
         assert self.n_embd == self.n_head * self.head_dim, (

@@ -554,6 +554,7 @@ __device__ __forceinline__ float rope_elem(float x, float partner, int d, float 
 struct LayerTail {
   float *f;     // [kD] forecast row (fp32)
   float *pnew;  // [kD] updated running sum of the current block
+  float *pold;  // [kD] its sum before this step's token
   float *sc;    // [NBcap] prototype scores
   int *list;    // [max(NBcap, top_k + 2)] selected blocks, ascending
   int *tk;      // [top_k] merged top-k
@@ -561,14 +562,15 @@ struct LayerTail {
   float *cv;    // [top_k + 1] candidate scores
   static size_t bytes(int64_t NBcap, int top_k) {
     const int64_t lst = NBcap > top_k + 2 ? NBcap : top_k + 2;
-    return sizeof(float) * (2 * kD + NBcap) + sizeof(int) * (lst + top_k) +
+    return sizeof(float) * (3 * kD + NBcap) + sizeof(int) * (lst + top_k) +
            (sizeof(int) + sizeof(float)) * (top_k + 1);
   }
   __device__ LayerTail(char *p, int64_t NBcap, int top_k) {
     const int64_t lst = NBcap > top_k + 2 ? NBcap : top_k + 2;
     f = reinterpret_cast<float *>(p);
     pnew = f + kD;
-    sc = pnew + kD;
+    pold = pnew + kD;
+    sc = pold + kD;
     list = reinterpret_cast<int *>(sc + NBcap);
     tk = list + lst;
     ci = tk + top_k;
@@ -614,6 +616,11 @@ __global__ void __launch_bounds__(2 * kThreads)
                         const NextCand nx) {
   extern __shared__ __align__(1024) char smem_raw[];
   const bool slots = sm.host_k != nullptr;
+  // SD_SELECT_BEFORE_APPEND: score the current block with its sum before this
+  // step's token, and not at all when the token opens it (the reference's
+  // async prefetch selects before the append, async_offload.py:241-260)
+  const bool pre_app = (rule & SD_SELECT_BEFORE_APPEND) != 0;
+  rule &= ~SD_SELECT_BEFORE_APPEND;
   const int b = blockIdx.x / Hkv, h = blockIdx.x - (blockIdx.x / Hkv) * Hkv;
   const int Hq = Hkv * G;
   const int64_t pos = *cur_len;
@@ -829,6 +836,7 @@ __global__ void __launch_bounds__(2 * kThreads)
     const float pn = old + y;
     *ps = pn;
     X.pnew[d] = pn;
+    X.pold[d] = old;
     if (fc != nullptr) X.f[d] = fx;
   } else if (threadIdx.x >= 32 + kD) {
     constexpr int kQT = kThreads - 32 - kD;  // threads of the q part
@@ -869,7 +877,7 @@ __global__ void __launch_bounds__(2 * kThreads)
         // in-kernel scoring (cta_score_topk) so both paths agree bit for bit
         const int lane = threadIdx.x;
         const float4 fq = reinterpret_cast<const float4 *>(X.f)[lane & 15];
-        const float4 pr = reinterpret_cast<const float4 *>(X.pnew)[lane & 15];
+        const float4 pr = reinterpret_cast<const float4 *>(pre_app ? X.pold : X.pnew)[lane & 15];
         float p = 0.f;
         p = fmaf(fq.x, pr.x, p);
         p = fmaf(fq.y, pr.y, p);
@@ -877,7 +885,8 @@ __global__ void __launch_bounds__(2 * kThreads)
         p = fmaf(fq.w, pr.w, p);
 #pragma unroll
         for (int o = 8; o > 0; o >>= 1) p += __shfl_xor_sync(0xffffffffu, p, o);
-        const float vcur = curr < n_scored ? p * sel_scale : -INFINITY;
+        const bool cur_scored = curr < n_scored && !(pre_app && pos % bs == 0);
+        const float vcur = cur_scored ? p * sel_scale : -INFINITY;
         bool displaced = false;
         for (int r = lane; r < kk; r += 32) {
           // the candidates read in phase 0 (rank r = lane; kk > 32 reads the rest)
@@ -902,6 +911,8 @@ __global__ void __launch_bounds__(2 * kThreads)
       __shared__ int asi[kWarps * 32];
       const float4 fq = reinterpret_cast<const float4 *>(X.f)[threadIdx.x & 15];
       const float *gsum = proto_sum + bh * NBcap * kD;
+      const float *cur_row = pre_app ? X.pold : X.pnew;
+      const int excl = pre_app && pos % bs == 0 ? curr : -1;  // a block the token opens is not scored yet
       if (nstage > 0) {
         if (!mbar_wait_bounded(&proto_bar, 0)) {
           report(err, SD_KERR_TIMEOUT);
@@ -911,19 +922,33 @@ __global__ void __launch_bounds__(2 * kThreads)
         auto prow = [&](int j) -> const float * {
           if (j < nstage)
             return j < ProtoStage<T>::kRowsPerHalf ? kh + j * kD : vh + (j - ProtoStage<T>::kRowsPerHalf) * kD;
-          return j == curr ? X.pnew : gsum + static_cast<int64_t>(j) * kD;
+          return j == curr ? cur_row : gsum + static_cast<int64_t>(j) * kD;
         };
-        group_score_topk(prow, fq, nb, n_scored, -1, sel_scale, kk, X.tk, nullptr, asv, asi, ag);
+        group_score_topk(prow, fq, nb, n_scored, excl, sel_scale, kk, X.tk, nullptr, asv, asi, ag);
         // the region is refilled with tiles by the async proxy next
         if (threadIdx.x == 0) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       } else {
-        group_score_topk([&](int j) { return gsum + static_cast<int64_t>(j) * kD; }, fq, nb, n_scored, -1,
-                         sel_scale, kk, X.tk, nullptr, asv, asi, ag);
+        group_score_topk([&](int j) { return j == curr ? cur_row : gsum + static_cast<int64_t>(j) * kD; }, fq, nb,
+                         n_scored, excl, sel_scale, kk, X.tk, nullptr, asv, asi, ag);
       }
     } else {
       // top_k > 32: never launched with scoring warps, so the CTA is the
       // attention warps and CTA-wide helpers apply
       score_blocks(proto_sum + bh * NBcap * kD, kD, kD, X.f, n_scored, sel_scale, X.sc);
+      __syncthreads();
+      if (pre_app && curr < n_scored && threadIdx.x < 32) {  // the current block's pre-append score
+        const int lane = threadIdx.x;
+        const float4 fq = reinterpret_cast<const float4 *>(X.f)[lane & 15];
+        const float4 pr = reinterpret_cast<const float4 *>(X.pold)[lane & 15];
+        float p = 0.f;
+        p = fmaf(fq.x, pr.x, p);
+        p = fmaf(fq.y, pr.y, p);
+        p = fmaf(fq.z, pr.z, p);
+        p = fmaf(fq.w, pr.w, p);
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) p += __shfl_xor_sync(0xffffffffu, p, o);
+        if (lane == 0) X.sc[curr] = pos % bs == 0 ? -INFINITY : p * sel_scale;
+      }
       __syncthreads();
       cta_topk([&](int j) { return j < n_scored ? X.sc[j] : -INFINITY; }, nb, kk, X.tk);
     }
@@ -1135,7 +1160,8 @@ extern "C" int sd_decode_layer(const void *qkv, int dtype, int64_t qkv_sb, const
   if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || block_size <= 0 || top_k <= 0 || Tcap <= 0 || NBcap <= 0 ||
       max_pos < Tcap)
     return SD_ERR_INVALID;
-  if (rule != SD_RULE_REFERENCE && rule != SD_RULE_ABSOLUTE) return SD_ERR_INVALID;
+  const int base_rule = rule & ~SD_SELECT_BEFORE_APPEND;
+  if (base_rule != SD_RULE_REFERENCE && base_rule != SD_RULE_ABSOLUTE) return SD_ERR_INVALID;
   if (NBcap * block_size < Tcap) return SD_ERR_INVALID;
   if ((sel_out == nullptr) != (cnt_out == nullptr) || (sel_out && sel_cap < top_k + 2)) return SD_ERR_INVALID;
   if ((cand_idx == nullptr) != (cand_val == nullptr)) return SD_ERR_INVALID;
@@ -1179,7 +1205,8 @@ extern "C" int sd_decode_layer_offload(const void *qkv, int dtype, int64_t qkv_s
   if (B <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv || top_k <= 0 || host_tcap <= 0 || NBcap <= 0 ||
       max_pos < host_tcap)
     return SD_ERR_INVALID;
-  if (rule != SD_RULE_REFERENCE && rule != SD_RULE_ABSOLUTE) return SD_ERR_INVALID;
+  const int base_rule = rule & ~SD_SELECT_BEFORE_APPEND;
+  if (base_rule != SD_RULE_REFERENCE && base_rule != SD_RULE_ABSOLUTE) return SD_ERR_INVALID;
   if (NBcap * block_size < host_tcap) return SD_ERR_INVALID;
   if ((sel_out == nullptr) != (cnt_out == nullptr) || (sel_out && sel_cap < top_k + 2)) return SD_ERR_INVALID;
   // the slots only hold what a prefetch staged: forecast steps need the

@@ -188,7 +188,8 @@ class TransformerBlock(nn.Module):
                 out = ops.decode_layer_offload(proj[:, :nq], f, rotary_emb.cos, rotary_emb.sin, kv_cache, a.n_head,
                                                a.rule, sel_out=probe["sel"] if probe is not None else None,
                                                cnt_out=probe["cnt"] if probe is not None else None,
-                                               cand=kv_cache.cand if f is not None else None)
+                                               cand=kv_cache.cand if f is not None else None,
+                                               select_before_append=a.before_append)
                 if probe is not None:
                     probe["end"].record()
                 kv_cache.prefetched = False
@@ -210,7 +211,7 @@ class TransformerBlock(nn.Module):
                                    a.block_size, a.top_k_blocks, a.rule,
                                    sel_out=probe["sel"] if probe is not None else None,
                                    cnt_out=probe["cnt"] if probe is not None else None, cand=cand,
-                                   next_cand=next_cand)
+                                   next_cand=next_cand, select_before_append=a.before_append)
             if probe is not None:
                 probe["end"].record()
             kv_cache.advance(1, device=not getattr(kv_cache, "shared_len", False))

@@ -17,6 +17,15 @@ RULES = {"reference": L.SD_RULE_REFERENCE, "absolute": L.SD_RULE_ABSOLUTE}
 _err_bufs = {}
 
 
+def rule_code(rule: str, select_before_append: bool = False) -> int:
+    """SD_RULE_* of a rule name, with SD_SELECT_BEFORE_APPEND or-ed in on request."""
+    try:
+        code = RULES[rule]
+    except KeyError:
+        raise ValueError(f"unknown selector rule {rule!r}") from None
+    return code | (L.SD_SELECT_BEFORE_APPEND if select_before_append else 0)
+
+
 def dtype_code(t: torch.Tensor) -> int:
     try:
         return _DT[t.dtype]
@@ -230,8 +239,8 @@ def decode_layer(qkv: torch.Tensor, forecast: Optional[torch.Tensor], rope_cos: 
                  out: Optional[torch.Tensor] = None, sel_out: Optional[torch.Tensor] = None,
                  cnt_out: Optional[torch.Tensor] = None,
                  cand: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
-                 next_cand: Optional[Tuple[torch.Tensor, torch.Tensor, Tuple[torch.Tensor, torch.Tensor]]] = None
-                 ) -> torch.Tensor:
+                 next_cand: Optional[Tuple[torch.Tensor, torch.Tensor, Tuple[torch.Tensor, torch.Tensor]]] = None,
+                 select_before_append: bool = False) -> torch.Tensor:
     """Fused decode layer: RoPE + append + compressor update + selection +
     attention (model/attention/sparse.py:366-410 + :99-183 for T == 1).
     next_cand (optional) = (next layer's proto_sum, next layer's forecast
@@ -241,6 +250,9 @@ def decode_layer(qkv: torch.Tensor, forecast: Optional[torch.Tensor], rope_cos: 
     sel_out [B,Hkv,cap] / cnt_out [B,Hkv] int32 (optional) receive each
     (sequence, kv head)'s selected block list.  cand (optional) is the
     (cand_idx, cand_val) pair decode_candidates produced for this step.
+    select_before_append: score the current block with its sum before this
+    step's token (AsyncForecastOffloadAttention's prefetch timing,
+    async_offload.py:241-260) instead of after the append (sparse.py:133-139).
     Returns [B,Hq*D]."""
     _cuda(qkv, forecast, rope_cos, rope_sin, cur_len, k_store, v_store, proto_sum)
     _rope_tables(rope_cos, rope_sin, k_store.shape[-1], k_store.shape[2])
@@ -273,7 +285,7 @@ def decode_layer(qkv: torch.Tensor, forecast: Optional[torch.Tensor], rope_cos: 
     L.call("sd_decode_layer", qkv.data_ptr(), dtype_code(qkv), qkv.stride(0), *fargs, rope_cos.data_ptr(),
            rope_sin.data_ptr(), rope_cos.shape[0], cur_len.data_ptr(), k_store.data_ptr(), v_store.data_ptr(),
            proto_sum.data_ptr(), b, n_head, n_kv_head, d, k_store.shape[2], proto_sum.shape[2], block_size, top_k,
-           RULES[rule], sc, out.data_ptr(), out.stride(0),
+           rule_code(rule, select_before_append), sc, out.data_ptr(), out.stride(0),
            cand[0].data_ptr() if cand is not None else None,
            cand[1].data_ptr() if cand is not None else None,
            sel_out.data_ptr() if sel_out is not None else None,
@@ -333,7 +345,8 @@ def decode_layer_offload(qkv: torch.Tensor, forecast: Optional[torch.Tensor], ro
                          rope_sin: torch.Tensor, cache, n_head: int, rule: str = "reference",
                          scale: Optional[float] = None, out: Optional[torch.Tensor] = None,
                          sel_out: Optional[torch.Tensor] = None, cnt_out: Optional[torch.Tensor] = None,
-                         cand: Optional[Tuple[torch.Tensor, torch.Tensor]] = None) -> torch.Tensor:
+                         cand: Optional[Tuple[torch.Tensor, torch.Tensor]] = None,
+                         select_before_append: bool = False) -> torch.Tensor:
     """decode_layer on an offloaded cache (sd_decode_layer_offload): the new
     token is written to the current-block slot and through to the host store;
     attention reads the sink, current and prefetched slots.  Forecast steps
@@ -355,7 +368,8 @@ def decode_layer_offload(qkv: torch.Tensor, forecast: Optional[torch.Tensor], ro
     L.call("sd_decode_layer_offload", qkv.data_ptr(), dtype_code(qkv), qkv.stride(0), *fargs, rope_cos.data_ptr(),
            rope_sin.data_ptr(), rope_cos.shape[0], cache.len_dev.data_ptr(), cache.host_k.data_ptr(),
            cache.host_v.data_ptr(), cache.tcap, cache.slot_k.data_ptr(), cache.slot_v.data_ptr(), cache.kslots,
-           cache.proto_sum.data_ptr(), b, n_head, hkv, d, cache.nbcap, cache.block_size, cache.kslots, RULES[rule],
+           cache.proto_sum.data_ptr(), b, n_head, hkv, d, cache.nbcap, cache.block_size, cache.kslots,
+           rule_code(rule, select_before_append),
            sc, out.data_ptr(), out.stride(0),
            cand[0].data_ptr() if cand is not None else None,
            cand[1].data_ptr() if cand is not None else None,

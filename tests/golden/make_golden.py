@@ -436,6 +436,70 @@ def prefetch_abs_cases(torch, out):
     np.savez(os.path.join(out, "prefetch_abs.npz"), **res)
 
 
+ASYNC_DECODE_CASES = [
+    # name, B, cached tokens before the first step, seed
+    ("L1000", 2, 1000, 740),
+    ("L1023", 2, 1023, 741),
+    ("L3000", 2, 3000, 742),
+]
+ASYNC_DECODE_STEPS = 3
+
+
+def async_attn_weights(seed):
+    """wq, wk, wv, wo of one attention layer, N(0, 0.02), numpy PCG64."""
+    return {"wq": normal((768, 768), seed=seed, scale=0.02), "wk": normal((256, 768), seed=seed + 1, scale=0.02),
+            "wv": normal((256, 768), seed=seed + 2, scale=0.02), "wo": normal((768, 768), seed=seed + 3, scale=0.02)}
+
+
+def async_decode_inputs(b, L, seed, step):
+    """Cached K/V [B, L, 4, 64] (before the first step) and step `step`'s
+    x [B, 1, 768] and forecast [B, 1, 4, 64]."""
+    return (normal((b, L, 4, 64), seed=seed + 10), normal((b, L, 4, 64), seed=seed + 11),
+            normal((b, 1, 768), seed=seed + 20 + step), normal((b, 1, 4, 64), seed=seed + 30 + step))
+
+
+def async_decode_cases(torch, out):
+    """AsyncForecastOffloadAttention decode steps (model/attention/async_offload.py:
+    170-519) with the absolute rule: prefetch (selection before the append,
+    :241-260), then the decode that consumes it (:296-390, validity mask
+    :466-490).  On CPU the reference creates no transfer event, which would
+    route the decode to its synchronous fallback (:392-460); a placeholder
+    event object routes it through the prefetch-consuming branch (the event is
+    only used for a stream wait that the CPU path skips, :324-325).
+    Three consecutive steps per case; the output, and the prefetched lists."""
+    from model.config import ModelConfig
+    from model.attention.async_offload import AsyncForecastOffloadAttention, AsyncOffloadedKVCache
+    from model.rope import RotaryEmbedding
+
+    class _Placeholder:
+        pass
+
+    res = {}
+    with absolute_rule():
+        for name, b, L, seed in ASYNC_DECODE_CASES:
+            cfg = ModelConfig(block_size=64, top_k_blocks=8, attention_backend="async_offload")
+            attn = AsyncForecastOffloadAttention(cfg, layer_idx=1)
+            w = async_attn_weights(seed)
+            with torch.no_grad():
+                for nm, val in w.items():
+                    getattr(attn, nm).weight.copy_(torch.from_numpy(val))
+            cache = AsyncOffloadedKVCache(b, L + 64, 4, 64, torch.device("cpu"), torch.float32, pin_memory=False)
+            k, v, _, _ = async_decode_inputs(b, L, seed, 0)
+            cache.update(torch.from_numpy(k), torch.from_numpy(v))
+            rot = RotaryEmbedding(64, L + 128)
+            for s in range(ASYNC_DECODE_STEPS):
+                _, _, x, f = async_decode_inputs(b, L, seed, s)
+                with torch.no_grad():
+                    attn.prefetch(torch.from_numpy(f), cache)
+                    assert not attn.prefetched_is_small_context
+                    res[f"{name}_s{s}_sel"] = attn.prefetched_sel_indices.numpy().astype(np.int32)
+                    res[f"{name}_s{s}_val"] = attn.prefetched_val.numpy()
+                    attn.prefetch_event = _Placeholder()
+                    o = attn(torch.from_numpy(x), rot, kv_cache=cache, forecast_vector=torch.from_numpy(f))
+                res[f"{name}_s{s}_out"] = o.numpy()
+    np.savez(os.path.join(out, "async_decode.npz"), **res)
+
+
 PREFETCH_ABS_CASES = [
     # name, B, cached tokens, layer_idx, seed
     ("L1000", 2, 1000, 1, 720),
@@ -454,7 +518,7 @@ def main():
     torch = _setup(args.reference)
     jobs = [config1, compressor_cases, selector_cases, decode_cases, masked_cases, chunked_cases,
             prefetch_cases, model_cases, decode_big_cases, model_sparse_cases, chunked_big_cases,
-            prefetch_abs_cases]
+            prefetch_abs_cases, async_decode_cases]
     for job in jobs:
         if args.only and job.__name__ not in args.only.split(","):
             continue

@@ -338,3 +338,54 @@ def test_prefetch_selection_absolute(golden, case):
     rsel, rcnt = _ref_lists(g[case + "_sel"], g[case + "_val"] > 0.5)
     for ix in np.ndindex(b, 4):
         assert set(sel[ix][:cnt[ix]].tolist()) == set(rsel[ix][:rcnt[ix]].tolist()), ix
+
+
+def _async_decode_oracle(case):
+    """Oracle restatement of the reference's async decode steps: the prefetch
+    selection before the append (prefetch_select), then attention over those
+    blocks with the new token in place (async_offload.py:296-390, :466-490),
+    wq/wk/wv/wo and RoPE (model/rope.py:34-65) around it."""
+    from tests.golden.make_golden import ASYNC_DECODE_CASES, ASYNC_DECODE_STEPS, async_attn_weights, \
+        async_decode_inputs
+    name, b, L, seed = [c for c in ASYNC_DECODE_CASES if c[0] == case][0]
+    w = async_attn_weights(seed)
+    k0, v0, _, _ = async_decode_inputs(b, L, seed, 0)
+    kc = np.zeros((b, 4, L + 64, 64))
+    vc = np.zeros((b, 4, L + 64, 64))
+    kc[:, :, :L] = k0.transpose(0, 2, 1, 3)
+    vc[:, :, :L] = v0.transpose(0, 2, 1, 3)
+    cos, sin = O.rope_tables(64, L + 128)
+    outs, sels = [], []
+    for s in range(ASYNC_DECODE_STEPS):
+        cur = L + s
+        _, _, x, f = async_decode_inputs(b, L, seed, s)
+        small, sel, cnt = O.prefetch_select(f, kc[:, :, :cur].transpose(0, 2, 1, 3), cur, 64, 8, 1, rule="absolute")
+        assert not small
+        x32 = x.astype(np.float32)
+        q = (x32 @ w["wq"].T).reshape(b, 1, 12, 64)
+        k = (x32 @ w["wk"].T).reshape(b, 1, 4, 64)
+        v = (x32 @ w["wv"].T).reshape(b, 1, 4, 64)
+        q = O.apply_rope(q.astype(np.float64), cos, sin, cur)
+        k = O.apply_rope(k.astype(np.float64), cos, sin, cur)
+        kc[:, :, cur] = k[:, 0]
+        vc[:, :, cur] = v[:, 0]
+        a = O.decode_attention(q[:, 0], kc, vc, sel, cnt, cur + 1, 64)
+        outs.append(a.reshape(b, 1, 768) @ w["wo"].T.astype(np.float64))
+        sels.append((sel, cnt))
+    return outs, sels
+
+
+@pytest.mark.parametrize("case", ["L1000", "L1023", "L3000"])
+def test_async_decode_vs_reference(golden, case):
+    """AsyncForecastOffloadAttention's prefetch-consuming decode, three steps:
+    the oracle's selection (before the append, absolute rule) equals the
+    reference's prefetched lists and its output matches."""
+    from tests.golden.make_golden import ASYNC_DECODE_STEPS
+    g = golden("async_decode")
+    outs, sels = _async_decode_oracle(case)
+    for s in range(ASYNC_DECODE_STEPS):
+        rsel, rcnt = _ref_lists(g[f"{case}_s{s}_sel"], g[f"{case}_s{s}_val"] > 0.5)
+        sel, cnt = sels[s]
+        for ix in np.ndindex(*cnt.shape):
+            assert set(sel[ix][:cnt[ix]].tolist()) == set(rsel[ix][:rcnt[ix]].tolist()), (s, ix)
+        np.testing.assert_allclose(outs[s], g[f"{case}_s{s}_out"], rtol=0, atol=2e-6)
