@@ -62,6 +62,9 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=1024)
     ap.add_argument("--probe-steps", type=int, default=64)
     ap.add_argument("--cpu-seqs", type=int, default=1, help="sequences per CPU worker thread")
+    ap.add_argument("--kernels-only", action="store_true",
+                    help="only the standalone kernel measurements (compressor, gather, prefill selector and list "
+                         "builder at BASELINE sizes), one JSON line; for profiler captures of those kernels")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the config-3 prefill and standalone-kernel sub-measurements of the default run")
     ap.add_argument("--cpu-budget-s", type=float, default=15.0)
@@ -385,11 +388,19 @@ def run_b200(args, rank, world, local):
                 rewind(W)
         rewind(caches[0].current_len - ctx)
         ops.check_device_errors(dev)
+        kern_only = None
+        if chain and not args.offload:
+            kern_only = decode_kernels_graph_us(model, caches, args, dev)
+        ops.check_device_errors(dev)
 
     value = world * B * args.steps / (ms / 1000.0)
     e2e = world * B * ke / (e2e_ms / 1000.0)
     hbm, src = read_peaks()
-    avg_launch_s = k_ms / 1000.0 / k_launch
+    in_step_s = k_ms / 1000.0 / k_launch
+    # the kernel's duration: from the graph of the decode kernels alone when
+    # measured (events around every launch inside the step add their own
+    # nodes), else from the per-launch events of the instrumented step
+    avg_launch_s = kern_only / 1e6 if kern_only else in_step_s
     bytes_per_launch = k_bytes / k_launch
     c_avg_s = c_ms / 1000.0 / max(c_launch, 1)
     c_gbs = (c_bytes / max(c_launch, 1)) / c_avg_s / 1e9 if c_launch else None
@@ -419,6 +430,11 @@ def run_b200(args, rank, world, local):
                      "frac": round(achieved / hbm, 4), "peak_source": src,
                      "traffic": read_traffic("decode_layer"),
                      "bytes_per_launch": round(bytes_per_launch), "avg_launch_us": round(avg_launch_s * 1e6, 3),
+                     "duration_source": ("CUDA events around replays of a graph holding the 12 layers' fused "
+                                         "decode kernels alone (the step's caches, chained candidates), / 12"
+                                         if kern_only else "CUDA events around each launch in the step graph"),
+                     "in_step_event_us": round(in_step_s * 1e6, 3),
+                     "in_step_frac": round(bytes_per_launch / in_step_s / 1e9 / hbm, 4),
                      "launches_sampled": k_launch,
                      "selector_kernel": {"kernel": "sd::decode_candidates_kernel<bf16> (side stream)",
                                          "achieved": round(c_gbs, 1) if c_gbs else None, "unit": "GB/s",
@@ -445,6 +461,64 @@ def run_b200(args, rank, world, local):
             "note": "exposed wait = compute-stream time blocked on the layers' prefetch events (instrumented "
                     "graph); prefetch time includes the candidate kernel"}
     return result
+
+
+def decode_kernels_graph_us(model, caches, args, dev, reps: int = 20, warm: int = 3) -> float:
+    """Average duration (us) of one fused decode-layer launch: CUDA events
+    around replays of a graph that holds only the layers' fused decode kernels,
+    chained as in the step (layer L's kernel computes layer L+1's candidates;
+    layer 0 takes the static window), on the step's own caches at the first
+    position of the timed window, with random projection rows.  Every replay
+    rewrites the same new token; the block sums it touches are restored after."""
+    import torch
+    from local_research_small_language_model_b200 import ops
+    B = args.batch
+    n = len(model.layers)
+    a0 = model.layers[0].attention
+    nq = (a0.n_head + 2 * a0.n_kv_head) * a0.head_dim
+    fd = model.config.forecast_heads * model.config.forecast_dim
+    g = torch.Generator(device=dev).manual_seed(77)
+    proj = [torch.randn(B, nq + fd, generator=g, device=dev, dtype=torch.bfloat16) for _ in range(n)]
+    for c in caches:
+        if getattr(c, "cand", None) is None:
+            c.cand = (torch.empty(B, a0.n_kv_head, a0.top_k_blocks, dtype=torch.int32, device=dev),
+                      torch.empty(B, a0.n_kv_head, a0.top_k_blocks, dtype=torch.float32, device=dev))
+    j = caches[0].current_len // a0.block_size
+    snap = [c.proto_sum[:, :, j].clone() for c in caches]
+    cos, sin = model.rotary_emb.cos, model.rotary_emb.sin
+
+    def body():
+        for li, layer in enumerate(model.layers):
+            a, c = layer.attention, caches[li]
+            nxt = (caches[li + 1].proto_sum, proj[li][:, nq:], caches[li + 1].cand) if li + 1 < n else None
+            ops.decode_layer(proj[li][:, :nq], proj[li - 1][:, nq:] if li > 0 else None, cos, sin, c.len_dev,
+                             c.k_store, c.v_store, c.proto_sum, a.n_head, a.n_kv_head, a.block_size, a.top_k_blocks,
+                             a.rule, cand=c.cand if li > 0 else None, next_cand=nxt)
+
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        body()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        body()
+    for _ in range(warm):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1000.0 / (reps * n)
+    for c, r in zip(caches, snap):
+        c.proto_sum[:, :, j].copy_(r)
+    del graph
+    torch.cuda.synchronize()
+    return us
 
 
 def prefill_flops(lists, counts, T, G, causal=True):
@@ -659,6 +733,12 @@ def main():
                "e2e": {"value": round(r["value"], 3), "unit": "tok/s", "h2d_bytes_per_step": 0,
                        "d2h_bytes_per_step": 0}}
         print(json.dumps(out), flush=True)
+        return 0
+
+    if args.kernels_only:
+        import torch
+        torch.cuda.set_device(local)
+        print(json.dumps({"kernels": run_kernels(local)}), flush=True)
         return 0
 
     if world > 1:

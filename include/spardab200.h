@@ -249,6 +249,18 @@ SD_API int sd_prefill_attention(const void *q, int dtype, int64_t B, int64_t T, 
 SD_API int sd_rmsnorm(const void *x, int dtype, int64_t rows, int64_t C, int64_t x_rs, const void *w,
                       float eps, void *out, int64_t o_rs, void *stream);
 
+/* RoPE of a prompt's q [B,T,Hq,D] and k [B,T,Hkv,D] (element strides q_sb,
+ * q_st, q_sh and k_sb, k_st, k_sh) at positions offset .. offset+T-1, written
+ * to contiguous q_out [B,T,Hq,D] and k_out [B,T,Hkv,D].  Replaces
+ * apply_rotary_emb (model/rope.py:34-65) with its rounding sequence: the fp32
+ * tables rope_cos/rope_sin [max_pos, D/2] cast to the activation dtype, then
+ * x*cos, rotate_half(x)*sin and their sum each rounded to it.  D % 16 == 0;
+ * 16-byte aligned rows. */
+SD_API int sd_rope_qk(const void *q, const void *k, int dtype, int64_t B, int64_t T, int64_t Hq, int64_t Hkv,
+                      int64_t D, int64_t q_sb, int64_t q_st, int64_t q_sh, int64_t k_sb, int64_t k_st, int64_t k_sh,
+                      const float *rope_cos, const float *rope_sin, int64_t max_pos, int64_t offset, void *q_out,
+                      void *k_out, void *stream);
+
 /* SwiGLU gate of model/transformer.py:30-31 on a fused [gate | up] projection:
  * gu rows hold 2F values (row stride g_rs); out[r, c] = silu(gate) * up, each
  * op rounded to the activation dtype as the reference's separate ops are. */

@@ -178,12 +178,22 @@ class B200SparseAttention(BaseAttention):
         xq = self.wq(x).view(b, t, self.n_head, self.head_dim)
         xk = self.wk(x).view(b, t, self.n_kv_head, self.head_dim)
         xv = self.wv(x).view(b, t, self.n_kv_head, self.head_dim)
+        out = self.prefill_core(xq, xk, xv, rotary_emb, kv_cache, is_causal, forecast_vector, **kwargs)
+        return self.wo(out.reshape(b, t, self.n_head * self.head_dim).to(x.dtype))
+
+    def prefill_core(self, xq, xk, xv, rotary_emb, kv_cache, is_causal, forecast_vector, **kwargs):
+        """Prefill from the q/k/v projections [B,T,H,D] (any strides with an
+        innermost stride of 1, e.g. views of one packed projection): RoPE,
+        cache write, compressor, selector, block lists and block-sparse
+        attention.  Returns the attention output [B,T,Hq,D] before wo."""
+        b, t = xq.shape[0], xq.shape[1]
         offset = kv_cache.current_len if kv_cache is not None else 0
         if offset:
             # the reference uses seq_len for both queries and keys here
             # (sparse.py:413-430), so a prompt cannot extend a filled cache
             raise NotImplementedError("prefill into a non-empty cache")
-        xq, xk = rotary_emb(xq, xk, offset=0)
+        rotary_emb.ensure(t)
+        xq, xk = ops.rope_qk(xq, xk, rotary_emb.cos, rotary_emb.sin, 0)
         if isinstance(kv_cache, B200OffloadKVCache):
             kv_cache.update(xk, xv)  # host store + block sums + slots; attend over the prompt itself
             kh, vh = xk.transpose(1, 2), xv.transpose(1, 2)
@@ -217,6 +227,5 @@ class B200SparseAttention(BaseAttention):
             else:
                 mode = "masked_static"
             row_topk = topk
-        lists, counts = ops.prefill_lists(mode, b, self.n_kv_head, t, bs, kk, topk, causal, device=x.device)
-        out = ops.prefill_attention(xq, kh, vh, lists, counts, bs, row_topk, causal)
-        return self.wo(out.reshape(b, t, self.n_head * self.head_dim).to(x.dtype))
+        lists, counts = ops.prefill_lists(mode, b, self.n_kv_head, t, bs, kk, topk, causal, device=xq.device)
+        return ops.prefill_attention(xq, kh, vh, lists, counts, bs, row_topk, causal)

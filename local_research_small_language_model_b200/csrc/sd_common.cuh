@@ -73,6 +73,17 @@ template <> __device__ __forceinline__ __half from_f<__half>(float x) { return _
 // Round a float to T's precision and back (identity for float).
 template <typename T> __device__ __forceinline__ float round_to(float x) { return to_f<T>(from_f<T>(x)); }
 
+// One rotated element with the reference's rounding sequence
+// (model/rope.py:58-63): the fp32 tables cast to T, then x*cos and
+// rotate_half(x)*sin and their sum each rounded to T.  rot is the element of
+// rotate_half(x) at this position (-x[d + D/2] in the first half, x[d - D/2]
+// in the second).
+template <typename T> __device__ __forceinline__ float rope_rounded(float x, float rot, float c, float s) {
+  const float a = round_to<T>(__fmul_rn(x, round_to<T>(c)));
+  const float b = round_to<T>(__fmul_rn(rot, round_to<T>(s)));
+  return round_to<T>(__fadd_rn(a, b));
+}
+
 // ---------------------------------------------------------------- PTX wrappers
 // Waits until the kernel ahead of this one on the stream has completed and its
 // writes are visible; returns at once when this kernel was not launched with

@@ -32,6 +32,53 @@ __global__ void compress_blocks_kernel(const T *__restrict__ k, int64_t T_, int 
   }
 }
 
+// Same result through 16-byte loads, for rows whose H*D values sit in 16-byte
+// aligned chunks (kV elements each).  One CTA per (block j, sequence b);
+// thread (g, c) sums chunk column c of rows g, g + kGroups, ... of the block,
+// all of its loads issued before any is used, then the kGroups partial sums
+// of every column are added in shared memory in a fixed order.
+template <typename T, int kGroups>
+__global__ void __launch_bounds__(256) compress_blocks_vec_kernel(const T *__restrict__ k, int64_t T_, int H, int D,
+                                                                  int64_t sb, int64_t st, int64_t sh, int bs,
+                                                                  float *__restrict__ reps, int64_t NB) {
+  constexpr int kV = 16 / static_cast<int>(sizeof(T));
+  constexpr int kRowsPer = 64 / kGroups;  // block_size 64
+  __shared__ float part[kGroups][256 / kGroups * kV];
+  const int64_t j = blockIdx.x, b = blockIdx.y;
+  const int cols = H * D / kV;             // chunk columns of a token row
+  const int c = threadIdx.x % cols, g = threadIdx.x / cols;
+  const int h = c * kV / D, d0 = c * kV - h * D;
+  const int64_t t0 = j * 64;
+  float acc[kV];
+#pragma unroll
+  for (int i = 0; i < kV; ++i) acc[i] = 0.f;
+  if (g < kGroups) {
+    const T *p = k + b * sb + h * sh + d0;
+    uint4 u[kRowsPer];
+#pragma unroll
+    for (int r = 0; r < kRowsPer; ++r) {
+      const int64_t t = t0 + g + r * kGroups;
+      u[r] = t < T_ ? *reinterpret_cast<const uint4 *>(p + t * st) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int r = 0; r < kRowsPer; ++r) {
+      const T *e = reinterpret_cast<const T *>(&u[r]);
+#pragma unroll
+      for (int i = 0; i < kV; ++i) acc[i] += to_f(e[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < kV; ++i) part[g][c * kV + i] = acc[i];
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < H * D; e += blockDim.x) {
+    float s = 0.f;
+#pragma unroll
+    for (int q = 0; q < kGroups; ++q) s += part[q][e];
+    const int hh = e / D, dd = e - hh * D;
+    reps[((b * NB + j) * H + hh) * D + dd] = s * (1.0f / 64.0f);
+  }
+}
+
 // Writes T new tokens of K and V into the head-major cache.
 template <typename T>
 __global__ void kv_copy_kernel(const T *__restrict__ xk, const T *__restrict__ xv, int H, int D, int64_t sb,
@@ -76,6 +123,17 @@ extern "C" int sd_compress_blocks(const void *k, int dtype, int64_t B, int64_t T
   int threads = static_cast<int>(H * D < 1024 ? ((H * D + 31) / 32) * 32 : 1024);
   dim3 grid(static_cast<unsigned>(NB), static_cast<unsigned>(B));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int es = sd::dtype_size(dtype);
+  const int64_t kv = 16 / es;
+  // 16-byte path: block 64, every token row in aligned 16-byte chunks, and
+  // the chunk columns of a row (H*D/kv) times 8 row groups fill 256 threads
+  if (block_size == 64 && sd::aligned16(k) && D % kv == 0 && sb % kv == 0 && st % kv == 0 && sh % kv == 0 &&
+      (H * D / kv) * 8 == 256) {
+    SD_DISPATCH_DTYPE(dtype, E,
+                      sd::compress_blocks_vec_kernel<E, 8><<<grid, 256, 0, s>>>(
+                          static_cast<const E *>(k), T, (int)H, (int)D, sb, st, sh, block_size, reps, NB));
+    return sd::check_launch();
+  }
   SD_DISPATCH_DTYPE(dtype, E,
                     sd::compress_blocks_kernel<E><<<grid, threads, 0, s>>>(
                         static_cast<const E *>(k), T, (int)H, (int)D, sb, st, sh, block_size, reps, NB));

@@ -543,11 +543,7 @@ __global__ void __launch_bounds__(kThreads)
 // x*cos and rotate_half(x)*sin and their sum each rounded to the dtype.
 template <typename T>
 __device__ __forceinline__ float rope_elem(float x, float partner, int d, float c, float s) {
-  const float cc = round_to<T>(c), ss = round_to<T>(s);
-  const float rot = d < kD / 2 ? -partner : partner;
-  const float a = round_to<T>(__fmul_rn(x, cc));
-  const float bq = round_to<T>(__fmul_rn(rot, ss));
-  return round_to<T>(__fadd_rn(a, bq));
+  return rope_rounded<T>(x, d < kD / 2 ? -partner : partner, c, s);
 }
 
 // Tail of the fused kernel's shared memory.

@@ -128,7 +128,78 @@ __global__ void silu_mul_kernel(const T *__restrict__ gu, int64_t g_rs, int F, T
   }
 }
 
+// RoPE of q [B,T,Hq,D] and k [B,T,Hkv,D] (rows addressed through strides)
+// into contiguous outputs, one CTA per token (b, t): thread i takes 8
+// consecutive elements of the first half of one head and the 8 they pair
+// with in the second half, in 16-byte loads.  Requires D % 16 == 0 and
+// 16-byte aligned rows (checked on the host).
+template <typename T>
+__global__ void rope_qk_kernel(const T *__restrict__ q, int64_t q_sb, int64_t q_st, int64_t q_sh,
+                               const T *__restrict__ k, int64_t k_sb, int64_t k_st, int64_t k_sh, int64_t Tn,
+                               int Hq, int Hkv, int D, const float *__restrict__ cos_t,
+                               const float *__restrict__ sin_t, int64_t offset, T *__restrict__ qo,
+                               T *__restrict__ ko) {
+  pdl_wait();
+  constexpr int kV = 8;  // elements per 16-byte chunk (16-bit types; fp32 uses two chunks)
+  const int64_t row = blockIdx.x;
+  const int64_t b = row / Tn, t = row - (row / Tn) * Tn;
+  const int half = D / 2, per_head = half / kV;
+  const float *cr = cos_t + (offset + t) * half;
+  const float *sr = sin_t + (offset + t) * half;
+  for (int task = threadIdx.x; task < (Hq + Hkv) * per_head; task += blockDim.x) {
+    const int hh = task / per_head, d0 = (task - hh * per_head) * kV;
+    const bool isq = hh < Hq;
+    const int h = isq ? hh : hh - Hq;
+    const T *src = isq ? q + b * q_sb + t * q_st + h * q_sh : k + b * k_sb + t * k_st + h * k_sh;
+    T *dst = (isq ? qo + (row * Hq + h) * D : ko + (row * Hkv + h) * D);
+    constexpr int kW = kV * static_cast<int>(sizeof(T)) / 16;  // 16-byte words per 8 elements
+    uint4 ul[kW], uh[kW], ol[kW], oh[kW];
+#pragma unroll
+    for (int w = 0; w < kW; ++w) {
+      ul[w] = reinterpret_cast<const uint4 *>(src + d0)[w];
+      uh[w] = reinterpret_cast<const uint4 *>(src + half + d0)[w];
+    }
+    const T *lo = reinterpret_cast<const T *>(ul), *hi = reinterpret_cast<const T *>(uh);
+    T *olo = reinterpret_cast<T *>(ol), *ohi = reinterpret_cast<T *>(oh);
+#pragma unroll
+    for (int i = 0; i < kV; ++i) {
+      const float c = cr[d0 + i], sn = sr[d0 + i];
+      const float xl = to_f(lo[i]), xh = to_f(hi[i]);
+      olo[i] = from_f<T>(rope_rounded<T>(xl, -xh, c, sn));
+      ohi[i] = from_f<T>(rope_rounded<T>(xh, xl, c, sn));
+    }
+#pragma unroll
+    for (int w = 0; w < kW; ++w) {
+      reinterpret_cast<uint4 *>(dst + d0)[w] = ol[w];
+      reinterpret_cast<uint4 *>(dst + half + d0)[w] = oh[w];
+    }
+  }
+}
+
 }  // namespace sd
+
+extern "C" int sd_rope_qk(const void *q, const void *k, int dtype, int64_t B, int64_t T, int64_t Hq, int64_t Hkv,
+                          int64_t D, int64_t q_sb, int64_t q_st, int64_t q_sh, int64_t k_sb, int64_t k_st,
+                          int64_t k_sh, const float *rope_cos, const float *rope_sin, int64_t max_pos,
+                          int64_t offset, void *q_out, void *k_out, void *stream) {
+  if (!q || !k || !rope_cos || !rope_sin || !q_out || !k_out || B <= 0 || T <= 0 || Hq <= 0 || Hkv <= 0 || D <= 0 ||
+      offset < 0)
+    return SD_ERR_INVALID;
+  if (D % 16 != 0 || offset + T > max_pos) return D % 16 != 0 ? SD_ERR_UNSUPPORTED : SD_ERR_INVALID;
+  const int64_t ev = 16 / sd::dtype_size(dtype);  // elements per 16 bytes
+  if (!sd::aligned16(q) || !sd::aligned16(k) || !sd::aligned16(q_out) || !sd::aligned16(k_out) || q_sb % ev ||
+      q_st % ev || q_sh % ev || k_sb % ev || k_st % ev || k_sh % ev)
+    return SD_ERR_ALIGN;
+  if (B * T > 0x7fffffff || (Hq + Hkv) * D > (1 << 16)) return SD_ERR_UNSUPPORTED;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int threads = static_cast<int>((Hq + Hkv) * (D / 16) < 256 ? (((Hq + Hkv) * (D / 16) + 31) / 32) * 32 : 256);
+  SD_DISPATCH_DTYPE(dtype, E,
+                    return sd::launch(sd::rope_qk_kernel<E>, dim3(static_cast<unsigned>(B * T)), dim3(threads), 0, s,
+                                      sd::pdl_enabled(), static_cast<const E *>(q), q_sb, q_st, q_sh,
+                                      static_cast<const E *>(k), k_sb, k_st, k_sh, T, (int)Hq, (int)Hkv, (int)D,
+                                      rope_cos, rope_sin, offset, static_cast<E *>(q_out), static_cast<E *>(k_out)));
+  return SD_OK;
+}
 
 extern "C" int sd_rmsnorm(const void *x, int dtype, int64_t rows, int64_t C, int64_t x_rs, const void *w,
                           float eps, void *out, int64_t o_rs, void *stream) {

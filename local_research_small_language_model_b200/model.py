@@ -219,6 +219,30 @@ class TransformerBlock(nn.Module):
             gu = F.linear(self.ffn_norm(x2), self.packed_ffn_weight())
             x2 = torch.addmm(x2, ops.silu_mul(gu), self.ffn.w_down.weight.t())
             return x2.view(b, 1, c), current_forecast
+        elif x.is_cuda and mask is None and isinstance(self.attention, B200SparseAttention):
+            # prompt: one GEMM for [wq; wk; wv; wf], the attention core on views
+            # of it, the residual adds folded into addmm, and the SwiGLU gate
+            # on one [w_gate; w_up] GEMM (transformer.py:76-131 in 6 launches
+            # around the attention core instead of 12)
+            a = self.attention
+            x2 = x.reshape(b * t, c)
+            normed = self.attn_norm(x2)
+            proj = F.linear(normed, self.packed_weight())
+            nq, nk = a.n_head * a.head_dim, a.n_kv_head * a.head_dim
+            current_forecast = proj[:, nq + 2 * nk:].view(b, t, self.config.forecast_heads,
+                                                          self.config.forecast_dim)
+            if next_layer_block is not None and next_kv_cache is not None and \
+                    hasattr(next_layer_block.attention, "prefetch"):
+                next_layer_block.attention.prefetch(forecast_vector=current_forecast, offload_cache=next_kv_cache)
+            p3 = proj.view(b, t, -1)
+            out = a.prefill_core(p3[..., :nq].unflatten(-1, (a.n_head, a.head_dim)),
+                                 p3[..., nq:nq + nk].unflatten(-1, (a.n_kv_head, a.head_dim)),
+                                 p3[..., nq + nk:nq + 2 * nk].unflatten(-1, (a.n_kv_head, a.head_dim)),
+                                 rotary_emb, kv_cache, is_causal, prev_layer_forecast)
+            x2 = torch.addmm(x2, out.reshape(b * t, nq).to(x2.dtype), a.wo.weight.t())
+            gu = F.linear(self.ffn_norm(x2), self.packed_ffn_weight())
+            x2 = torch.addmm(x2, ops.silu_mul(gu), self.ffn.w_down.weight.t())
+            return x2.view(b, t, c), current_forecast
         else:
             normed = self.attn_norm(x)
             current_forecast = self.forecast(normed)

@@ -466,3 +466,23 @@ def set_programmatic_launch(enable: bool) -> bool:
     the decode step, where every such kernel follows a library GEMM.  Returns
     the previous setting."""
     return bool(L.load().sd_set_programmatic_launch(int(bool(enable))))
+
+
+def rope_qk(xq: torch.Tensor, xk: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+            offset: int = 0) -> Tuple[torch.Tensor, torch.Tensor]:
+    """apply_rotary_emb (model/rope.py:34-65) on q [B,T,Hq,D] and k [B,T,Hkv,D]
+    in one kernel with the reference's rounding sequence; returns contiguous
+    rotated copies.  cos/sin: the fp32 tables [max_pos, D/2]."""
+    _cuda(xq, xk, cos, sin)
+    b, t, hq, d = xq.shape
+    hkv = xk.shape[2]
+    _rope_tables(cos, sin, d, offset + t)
+    if xk.dtype != xq.dtype:
+        raise TypeError("q and k must share a dtype")
+    xq, xk = _inner1(xq), _inner1(xk)
+    qo = torch.empty(b, t, hq, d, dtype=xq.dtype, device=xq.device)
+    ko = torch.empty(b, t, hkv, d, dtype=xk.dtype, device=xk.device)
+    L.call("sd_rope_qk", xq.data_ptr(), xk.data_ptr(), dtype_code(xq), b, t, hq, hkv, d, xq.stride(0), xq.stride(1),
+           xq.stride(2), xk.stride(0), xk.stride(1), xk.stride(2), cos.data_ptr(), sin.data_ptr(), cos.shape[0],
+           offset, qo.data_ptr(), ko.data_ptr(), _stream(xq))
+    return qo, ko

@@ -80,4 +80,7 @@ class RotaryEmbedding(nn.Module):
         total = offset + xq.shape[1]
         if total > self.max_seq_len:
             self._extend_cache(total, xq.device)
+        if xq.is_cuda and xq.shape[-1] % 16 == 0:
+            from . import ops  # the fused kernel (sd_rope_qk), same rounding sequence
+            return ops.rope_qk(xq, xk, self.cos, self.sin, offset)
         return apply_rotary_emb(xq, xk, self.cos, self.sin, offset=offset)

@@ -396,3 +396,21 @@ def test_decode_layer_selection_and_candidates(dev, dt, rule, start):
         assert np.array_equal(sels[0][1], rc)
         for ix in np.ndindex(b, hkv):
             assert list(sels[0][0][ix][:rc[ix]]) == list(rs[ix][:rc[ix]]), (step, ix)
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("offset,tt", [(0, 700), (16000, 96)])
+def test_rope_qk_bit_exact_vs_reference_formula(dev, dt, offset, tt):
+    """sd_rope_qk on strided q/k views of one packed projection equals the
+    reference's apply_rotary_emb (model/rope.py:34-65) bit for bit, tables
+    cast to the activation dtype as type_as does."""
+    from local_research_small_language_model_b200.rope import apply_rotary_emb
+    b = 2
+    proj = t(normal((b, tt, 1536), seed=21), dev, dt)
+    xq = proj[..., :768].unflatten(-1, (12, 64))
+    xk = proj[..., 768:1024].unflatten(-1, (4, 64))
+    cos, sin = precompute_rope_freqs(64, offset + tt + 64)
+    cos, sin = cos.to(dev), sin.to(dev)
+    q1, k1 = ops.rope_qk(xq, xk, cos, sin, offset)
+    q2, k2 = apply_rotary_emb(xq, xk, cos, sin, offset=offset)
+    assert torch.equal(q1, q2) and torch.equal(k1, k2)
