@@ -33,55 +33,78 @@ __global__ void prefill_lists_kernel(int mode, int causal, int64_t T, int bs, in
   }
   __syncthreads();
   int32_t *dst = lists + ((static_cast<int64_t>(b) * H + h) * nqt + qt) * lcap;
-  if (threadIdx.x == 0) {
+  __shared__ int s_n;
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
     int n = 0;
-    if (mode == kListDense) {
-      for (int j = 0; j <= hi && n < lcap; ++j) dst[n++] = j;
-    } else if (mode == kListMaskedStatic || mode == kListChunkedStatic ||
-               (mode == kListChunkedForecast && bq == 0)) {
-      // masked window: bk <= bq and bq - bk < top_k + 1 (sparse.py:250);
-      // chunked window: bq - top_k + 1 .. bq (sparse.py:325-328); the sink always
-      const int w = mode == kListMaskedStatic ? top_k + 1 : top_k;
-      const int lo = bq - w + 1 > 0 ? bq - w + 1 : 0;
-      if (lo > 0 && n < lcap) dst[n++] = 0;
-      for (int j = lo; j <= bq && n < lcap; ++j) dst[n++] = j;
-    } else if (mode == kListMaskedForecast) {
-      // union of every row's top-k with the sink and the diagonal block
-      votes[0] += 1;
-      if (bq <= hi) votes[bq] += 1;
-      for (int j = 0; j <= hi && n < lcap; ++j)
-        if (votes[j] > 0) dst[n++] = j;
-    } else {  // kListChunkedForecast, bq > 0: union, cut to ms entries
+    if (mode == kListChunkedForecast && bq > 0) {  // union, cut to ms entries (warp-parallel)
       const int ms = nb < top_k + 2 ? nb : top_k + 2;
       int total = 0;
-      for (int j = 0; j <= hi; ++j) total += (votes[j] > 0 || j == 0 || j == bq) ? 1 : 0;
-      if (total <= ms) {
-        for (int j = 0; j <= hi && n < lcap; ++j)
-          if (votes[j] > 0 || j == 0 || j == bq) dst[n++] = j;
-      } else {
+      for (int j0 = 0; j0 <= hi; j0 += 32) {
+        const int j = j0 + lane;
+        total += __popc(__ballot_sync(0xffffffffu, j <= hi && (votes[j] > 0 || j == 0 || j == bq)));
+      }
+      if (total > ms) {
         // keep the sink and the diagonal block, then the most-voted blocks
-        // (ties: lower index first); emit in ascending order
-        int chosen = 2;
-        votes[0] = -1;
-        votes[bq] = -1;
-        while (chosen < ms) {
-          int best = -1, bv = 0;
-          for (int j = 1; j < bq; ++j)
-            if (votes[j] > bv) {
-              bv = votes[j];
-              best = j;
-            }
-          if (best < 0) break;
-          votes[best] = -1;
-          ++chosen;
+        // (ties: lower index first): a warp top-(ms-2) over blocks 1..bq-1
+        __shared__ int s_pick[64];
+        warp_topk([&](int i) { return votes[i + 1] > 0 ? static_cast<float>(votes[i + 1]) : NAN; }, bq - 1, ms - 2,
+                  s_pick, nullptr);
+        __syncwarp();
+        for (int i = lane; i < ms - 2; i += 32)
+          if (s_pick[i] >= 0) s_pick[i] += 1;
+        __syncwarp();
+        // mark the kept blocks, then the rest of the union is dropped
+        for (int j0 = 0; j0 <= hi; j0 += 32) {
+          const int j = j0 + lane;
+          if (j <= hi) {
+            bool keep = j == 0 || j == bq;
+            for (int i = 0; i < ms - 2; ++i) keep = keep || s_pick[i] == j;
+            votes[j] = keep ? 1 : 0;
+          }
         }
+        __syncwarp();
+      } else {
+        for (int j0 = 0; j0 <= hi; j0 += 32) {
+          const int j = j0 + lane;
+          if (j <= hi && (j == 0 || j == bq)) votes[j] = 1;
+        }
+        __syncwarp();
+      }
+      // emit the kept blocks in ascending order
+      for (int j0 = 0; j0 <= hi; j0 += 32) {
+        const int j = j0 + lane;
+        const bool on = j <= hi && votes[j] > 0;
+        const unsigned m = __ballot_sync(0xffffffffu, on);
+        const int slot = n + __popc(m & ((1u << lane) - 1u));
+        if (on && slot < lcap) dst[slot] = j;
+        n += __popc(m);
+      }
+      n = n < lcap ? n : lcap;
+    } else if (lane == 0) {
+      if (mode == kListDense) {
+        for (int j = 0; j <= hi && n < lcap; ++j) dst[n++] = j;
+      } else if (mode == kListMaskedStatic || mode == kListChunkedStatic || mode == kListChunkedForecast) {
+        // masked window: bk <= bq and bq - bk < top_k + 1 (sparse.py:250);
+        // chunked window: bq - top_k + 1 .. bq (sparse.py:325-328, also the
+        // forecast mode's first q-block); the sink always
+        const int w = mode == kListMaskedStatic ? top_k + 1 : top_k;
+        const int lo = bq - w + 1 > 0 ? bq - w + 1 : 0;
+        if (lo > 0 && n < lcap) dst[n++] = 0;
+        for (int j = lo; j <= bq && n < lcap; ++j) dst[n++] = j;
+      } else {  // kListMaskedForecast: every row's top-k with the sink and the diagonal block
+        votes[0] += 1;
+        if (bq <= hi) votes[bq] += 1;
         for (int j = 0; j <= hi && n < lcap; ++j)
-          if (votes[j] == -1) dst[n++] = j;
+          if (votes[j] > 0) dst[n++] = j;
       }
     }
-    counts[(static_cast<int64_t>(b) * H + h) * nqt + qt] = n;
-    for (int i = n; i < lcap; ++i) dst[i] = -1;
+    if (lane == 0) s_n = n;
   }
+  __syncthreads();
+  const int n = s_n;
+  if (threadIdx.x == 0) counts[(static_cast<int64_t>(b) * H + h) * nqt + qt] = n;
+  for (int i = n + threadIdx.x; i < lcap; i += blockDim.x) dst[i] = -1;
 }
 
 // CUDA-core block-sparse prefill attention.  One CTA per (q-tile, h, b) with
@@ -230,6 +253,7 @@ extern "C" int sd_prefill_lists(int mode, int causal, int64_t B, int64_t H, int6
   const bool rows = mode == sd::kListMaskedForecast || mode == sd::kListChunkedForecast;
   if (rows && (!topk || kk <= 0)) return SD_ERR_INVALID;
   if (block_size != sd::kQTile) return SD_ERR_UNSUPPORTED;
+  if (mode == sd::kListChunkedForecast && top_k > 64) return SD_ERR_UNSUPPORTED;  // the cut keeps <= 64 voted blocks
   const int64_t nb = (T + block_size - 1) / block_size;
   if (nb > 65535 || B > 65535 || H > 65535) return SD_ERR_UNSUPPORTED;
   const size_t smem = sizeof(int) * nb;

@@ -187,6 +187,10 @@ __global__ void __launch_bounds__(256)
       }
     }
     // fold the chunk into the running top-8 of each of this warp's 8 rows
+    // (lanes 0..7 hold a row's list, best first).  The first chunk runs the
+    // register tournament; after it a block can only enter a row's list if it
+    // beats the row's 8th entry, which few do, so later chunks filter against
+    // that threshold with a ballot and insert the survivors one at a time.
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
       const int r = warp * 8 + q;
@@ -200,13 +204,44 @@ __global__ void __launch_bounds__(256)
         const bool ok = j < NB && v == v;
         cv[u] = ok ? v : -INFINITY;
         ci[u] = ok ? static_cast<int>(j) : kNoBlock;
-        sort_groups<8>(cv[u], ci[u]);
       }
-      merge_regs<8>(cv[0], ci[0], cv[1], ci[1]);
-      merge_regs<8>(cv[2], ci[2], cv[3], ci[3]);
-      merge_regs<8>(cv[0], ci[0], cv[2], ci[2]);
-      merge_lanes<8>(cv[0], ci[0]);
-      merge_regs<8>(rv[q], ri[q], cv[0], ci[0]);
+      if (j0 == 0) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) sort_groups<8>(cv[u], ci[u]);
+        merge_regs<8>(cv[0], ci[0], cv[1], ci[1]);
+        merge_regs<8>(cv[2], ci[2], cv[3], ci[3]);
+        merge_regs<8>(cv[0], ci[0], cv[2], ci[2]);
+        merge_lanes<8>(cv[0], ci[0]);
+        merge_regs<8>(rv[q], ri[q], cv[0], ci[0]);
+      } else {
+        float tv = __shfl_sync(0xffffffffu, rv[q], 7);
+        int ti = __shfl_sync(0xffffffffu, ri[q], 7);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          unsigned m = __ballot_sync(0xffffffffu, ci[u] != kNoBlock && (ti == kNoBlock || better(cv[u], ci[u], tv, ti)));
+          while (m) {
+            const int src = __ffs(m) - 1;
+            m &= m - 1;
+            const float nv = __shfl_sync(0xffffffffu, cv[u], src);
+            const int ni = __shfl_sync(0xffffffffu, ci[u], src);
+            if (!(ti == kNoBlock || better(nv, ni, tv, ti))) continue;  // an earlier insertion raised the bar
+            // position = entries better than the newcomer; later entries move down one lane
+            const bool above = lane < 8 && ri[q] != kNoBlock && better(rv[q], ri[q], nv, ni);
+            const int pos = __popc(__ballot_sync(0xffffffffu, above));
+            const float upv = __shfl_up_sync(0xffffffffu, rv[q], 1);
+            const int upi = __shfl_up_sync(0xffffffffu, ri[q], 1);
+            if (lane < 8 && lane > pos) {
+              rv[q] = upv;
+              ri[q] = upi;
+            } else if (lane == pos) {
+              rv[q] = nv;
+              ri[q] = ni;
+            }
+            tv = __shfl_sync(0xffffffffu, rv[q], 7);
+            ti = __shfl_sync(0xffffffffu, ri[q], 7);
+          }
+        }
+      }
     }
   }
 #pragma unroll
