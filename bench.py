@@ -59,6 +59,9 @@ def parse():
                          "side stream during layer L, or at the end of layer L's fused kernel")
     ap.add_argument("--pdl", choices=["on", "off"], default="off",
                     help="programmatic dependent launch of the library's decode-step kernels")
+    ap.add_argument("--projections", choices=["cublas", "tc"], default="cublas",
+                    help="decode-step projections: cuBLAS GEMMs with the library's RMSNorm and SwiGLU kernels, or "
+                         "the library's fused tensor-core projections (sd_linear)")
     ap.add_argument("--e2e-steps", type=int, default=1024)
     ap.add_argument("--probe-steps", type=int, default=64)
     ap.add_argument("--cpu-seqs", type=int, default=1, help="sequences per CPU worker thread")
@@ -239,6 +242,8 @@ def run_b200(args, rank, world, local):
     cfg = ModelConfig(block_size=64, top_k_blocks=8, context_length=4096, selector_rule=args.rule,
                       n_layer=args.layers)
     model = SparDAB200Model(cfg).to(dev, torch.bfloat16).eval()
+    for layer in model.layers:
+        layer.use_tc_linear = args.projections == "tc"
     caches = model.allocate_caches(B, ctx + W + 64, selection=args.selection, offload=args.offload)
     gen = torch.Generator(device=dev)
     gen.manual_seed(99 + rank)
@@ -415,6 +420,7 @@ def run_b200(args, rank, world, local):
                    "global_batch": B * world, "per_gpu_batch": B, "seq_len": ctx,
                    "ctx_window": [ctx + 1, ctx + W], "block_size": 64, "top_k": 8,
                    "selector_rule": args.rule, "selection": args.selection, "pdl": args.pdl,
+                   "projections": args.projections,
                    "parallelism": f"batch-shard x{world}, no collective",
                    "l2": "no flush: per-step working set (~0.9 GB of weights, prototypes and selected KV) "
                          "exceeds the 126 MB L2"},

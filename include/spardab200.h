@@ -267,6 +267,32 @@ SD_API int sd_rope_qk(const void *q, const void *k, int dtype, int64_t B, int64_
 SD_API int sd_silu_mul(const void *gu, int dtype, int64_t rows, int64_t F, int64_t g_rs, void *out,
                        int64_t o_rs, void *stream);
 
+/* ---- decode-step projections (sd_linear) ---- */
+#define SD_LINEAR_STORE 0    /* out = X W^T */
+#define SD_LINEAR_RESIDUAL 1 /* out = res + (X W^T rounded to the dtype); out may be res */
+#define SD_LINEAR_SWIGLU 2   /* W holds [gate; up] interleaved in 128-row groups (64 gate rows, then the 64 up
+                                rows of the same output columns); out[m, c] = silu(gate) * up, N/2 columns */
+
+/* One projection of the decode step on the tensor cores (tcgen05, fp32
+ * accumulation), out[M, N(/2)] = epilogue(X W^T) with X [M, K] (row stride
+ * x_rs) and W [N, K] contiguous, 16-bit.  norm_w (nullable, [K]): X is first
+ * RMS-normalised per row with gain norm_w and eps, as model/norm.py:15-21
+ * (normalised value rounded to the dtype, then times the gain).  When the
+ * output tiles alone would leave SMs idle, K is split over a thread-block
+ * cluster whose CTAs add their partial products through distributed shared
+ * memory in a fixed order: no workspace, no allocation, and results depend
+ * only on the shapes.  Replaces the nn.Linear calls around the attention
+ * path: the [wq; wk; wv; wf] projection after attn_norm
+ * (model/transformer.py:104-107, model/forecast.py:23-27), wo and w_down
+ * with the residual add (transformer.py:118-129) and the SwiGLU FFN gate
+ * (transformer.py:18-31), and the tied LM head after final_norm
+ * (model/model.py:141-142).  Output row stride o_rs, residual row stride
+ * r_rs.  K % 64 == 0, N % 128 == 0, K <= 1024 with norm_w; 16-byte aligned
+ * X, W, norm_w, out and x_rs % 8 == 0. */
+SD_API int sd_linear(const void *x, int dtype, int64_t M, int64_t K, int64_t x_rs, const void *w, int64_t N,
+                     const void *norm_w, float eps, int epilogue, const void *res, int64_t r_rs, void *out,
+                     int64_t o_rs, int32_t *err, void *stream);
+
 /* lens[i] += delta for i < n (device int32 array). */
 SD_API int sd_advance_len(int32_t *lens, int n, int delta, void *stream);
 

@@ -31,6 +31,8 @@ _SIGS = {
     "sd_last_cuda_error": [],
     "sd_advance_len": [_c_void_p, _i32, _i32, _c_void_p],
     "sd_set_programmatic_launch": [_i32],
+    "sd_linear": [_c_void_p, _i32, _i64, _i64, _i64, _c_void_p, _i64, _c_void_p, _f32, _i32, _c_void_p, _i64,
+                  _c_void_p, _i64, _c_void_p, _c_void_p],
     "sd_compress_blocks": [_c_void_p, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _c_void_p, _c_void_p],
     "sd_select_blocks": [_c_void_p, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _c_void_p, _i64, _i64, _i64,
                          _i64, _i32, _i32, _i32, _i64, _c_void_p, _c_void_p, _c_void_p],
@@ -67,6 +69,9 @@ _SIGS = {
                                 _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _c_void_p, _c_void_p],
 }
 
+# entry points that return something other than an int status
+_RESTYPES = {}
+
 _lock = threading.Lock()
 _lib = None
 
@@ -95,7 +100,7 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.sd_strerror.argtypes = [_i32]
         for name, args in _SIGS.items():
             fn = getattr(lib, name)
-            fn.restype = ctypes.c_int
+            fn.restype = _RESTYPES.get(name, ctypes.c_int)
             fn.argtypes = args
         _lib = lib
         return lib

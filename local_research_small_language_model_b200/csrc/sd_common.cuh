@@ -59,6 +59,40 @@ int launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStrea
   return check_launch();
 }
 
+// As launch(), with thread-block clusters of `cluster` CTAs (grid dims
+// multiples of it); a 1 x 1 x 1 cluster launches without the attribute.
+template <typename... KArgs, typename... Args>
+int launch_cluster(void (*kern)(KArgs...), dim3 grid, dim3 block, dim3 cluster, size_t smem, cudaStream_t s, bool pdl,
+                   Args &&...args) {
+  if (cluster.x * cluster.y * cluster.z == 1) return launch(kern, grid, block, smem, s, pdl, args...);
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  attr[na].id = cudaLaunchAttributeClusterDimension;
+  attr[na].val.clusterDim.x = cluster.x;
+  attr[na].val.clusterDim.y = cluster.y;
+  attr[na].val.clusterDim.z = cluster.z;
+  ++na;
+  if (pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+  if (e != cudaSuccess) {
+    set_cuda_error(e);
+    cudaGetLastError();
+    return SD_ERR_CUDA;
+  }
+  return check_launch();
+}
+
 // ---------------------------------------------------------------- conversions
 template <typename T> __device__ __forceinline__ float to_f(T x);
 template <> __device__ __forceinline__ float to_f<float>(float x) { return x; }

@@ -14,6 +14,25 @@ namespace sd {
 int encode_rows_map(CUtensorMap *map, const void *base, int dtype, int64_t D, int64_t T, int64_t H, int64_t B,
                     int64_t st, int64_t sh, int64_t sb, int box_rows);
 
+// Encodes a 2-D tiled map over a row-major [rows][cols] matrix of 16-bit
+// elements (row stride `ld` elements), box = box_rows x 64 columns (128
+// bytes, one swizzle atom), 128-byte swizzle; rows past `rows` read as zero.
+int encode_matrix_map(CUtensorMap *map, const void *base, int dtype, int64_t rows, int64_t cols, int64_t ld,
+                      int box_rows);
+
+// As encode_matrix_map, with a box of box_rows x box_cols (box_cols a
+// multiple of 8) and no swizzle: the box lands row-major in shared memory.
+int encode_plain_map(CUtensorMap *map, const void *base, int dtype, int64_t rows, int64_t cols, int64_t ld,
+                     int box_cols, int box_rows);
+
+__device__ __forceinline__ void tma_load_2d(void *smem_dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // ---------------------------------------------------------------- device side
 __device__ __forceinline__ void tma_load_4d(void *smem_dst, const CUtensorMap *map, int x, int y, int z, int w,
                                             uint64_t *bar) {

@@ -112,17 +112,57 @@ class TransformerBlock(nn.Module):
             self._ffn_key = key
         return self._ffn_packed
 
+    def swiglu_weight(self) -> torch.Tensor:
+        """[w_gate; w_up] interleaved in 64-row groups for the fused SwiGLU
+        epilogue, rebuilt when either weight changes."""
+        ws = (self.ffn.w_gate.weight, self.ffn.w_up.weight)
+        key = tuple((w.data_ptr(), w._version, w.dtype) for w in ws)
+        if getattr(self, "_swiglu_w", None) is None or self._swiglu_key != key:
+            with torch.no_grad():
+                self._swiglu_w = ops.swiglu_weight(*ws)
+            self._swiglu_key = key
+        return self._swiglu_w
+
+    def tc_projections(self, x2: torch.Tensor) -> bool:
+        """Whether the decode step's projections run on this library's fused
+        tensor-core kernel (sd_linear): opt-in (`use_tc_linear = True`), for
+        16-bit activations and weights with widths that tile by 64 x 128.  The
+        default is cuBLAS with the library's RMSNorm and SwiGLU kernels, which
+        measured faster for the 64-row decode batch."""
+        cfg = self.config
+        return (getattr(self, "use_tc_linear", False) and x2.is_cuda and x2.dtype in (torch.bfloat16, torch.float16)
+                and self.attn_norm.weight.dtype == x2.dtype and x2.stride(-1) == 1 and cfg.n_embd % 128 == 0
+                and cfg.ffn_dim % 64 == 0 and cfg.n_embd <= 1024)
+
+    def _ffn_decode(self, x2: torch.Tensor, attn_out: torch.Tensor, tc: bool) -> torch.Tensor:
+        """x + wo(attn); then h + w_down(silu(w_gate(n)) * w_up(n)) with n =
+        ffn_norm(h) (transformer.py:118-129)."""
+        a = self.attention
+        if tc:
+            h = ops.linear(attn_out, a.wo.weight, epilogue="residual", res=x2)
+            g = ops.linear(h, self.swiglu_weight(), self.ffn_norm.weight, self.ffn_norm.eps, epilogue="swiglu")
+            return ops.linear(g, self.ffn.w_down.weight, epilogue="residual", res=h, out=h)
+        x2 = torch.addmm(x2, attn_out, a.wo.weight.t())
+        gu = F.linear(self.ffn_norm(x2), self.packed_ffn_weight())
+        return torch.addmm(x2, ops.silu_mul(gu), self.ffn.w_down.weight.t())
+
     def forward(self, x, rotary_emb, kv_cache=None, mask=None, is_causal=True, prev_layer_forecast=None,
                 next_layer_block=None, next_kv_cache=None):
         b, t, c = x.shape
         if isinstance(kv_cache, (B200KVCache, B200OffloadKVCache)) and t == 1:
-            # decode step: 8 launches per layer (norm, [wq;wk;wv;wf] GEMM, fused
-            # attention kernel, wo GEMM with the residual add folded into addmm,
-            # norm, [w_gate;w_up] GEMM, SwiGLU gate kernel, w_down addmm)
+            # decode step: 8 launches per layer by default (norm, [wq;wk;wv;wf]
+            # GEMM, fused attention kernel, wo GEMM with the residual add folded
+            # into addmm, norm, [w_gate;w_up] GEMM, SwiGLU gate kernel, w_down
+            # addmm); with use_tc_linear 5, all of this library (RMSNorm +
+            # [wq;wk;wv;wf], attention, wo + residual, RMSNorm + [w_gate;w_up] +
+            # SwiGLU gate, w_down + residual).
             a = self.attention
             x2 = x.view(b, c)
-            normed = self.attn_norm(x2)
-            proj = F.linear(normed, self.packed_weight())
+            tc = self.tc_projections(x2)
+            if tc:
+                proj = ops.linear(x2, self.packed_weight(), self.attn_norm.weight, self.attn_norm.eps)
+            else:
+                proj = F.linear(self.attn_norm(x2), self.packed_weight())
             nq = (a.n_head + 2 * a.n_kv_head) * a.head_dim
             current_forecast = proj[:, nq:].view(b, 1, self.config.forecast_heads, self.config.forecast_dim)
             if kv_cache.current_len >= kv_cache.tcap:
@@ -194,10 +234,7 @@ class TransformerBlock(nn.Module):
                     probe["end"].record()
                 kv_cache.prefetched = False
                 kv_cache.advance(1, device=not getattr(kv_cache, "shared_len", False))
-                x2 = torch.addmm(x2, out, a.wo.weight.t())
-                gu = F.linear(self.ffn_norm(x2), self.packed_ffn_weight())
-                x2 = torch.addmm(x2, ops.silu_mul(gu), self.ffn.w_down.weight.t())
-                return x2.view(b, 1, c), current_forecast
+                return self._ffn_decode(x2, out, tc).view(b, 1, c), current_forecast
             cand = None
             if getattr(kv_cache, "cand_ready", False):
                 if kv_cache.cand_event is not None:
@@ -215,10 +252,7 @@ class TransformerBlock(nn.Module):
             if probe is not None:
                 probe["end"].record()
             kv_cache.advance(1, device=not getattr(kv_cache, "shared_len", False))
-            x2 = torch.addmm(x2, out, a.wo.weight.t())
-            gu = F.linear(self.ffn_norm(x2), self.packed_ffn_weight())
-            x2 = torch.addmm(x2, ops.silu_mul(gu), self.ffn.w_down.weight.t())
-            return x2.view(b, 1, c), current_forecast
+            return self._ffn_decode(x2, out, tc).view(b, 1, c), current_forecast
         elif x.is_cuda and mask is None and isinstance(self.attention, B200SparseAttention):
             # prompt: one GEMM for [wq; wk; wv; wf], the attention core on views
             # of it, the residual adds folded into addmm, and the SwiGLU gate
@@ -335,7 +369,13 @@ class SparDAB200Model(nn.Module):
         if kv_caches is not None and t == 1 and getattr(kv_caches[0], "shared_len", False) and \
                 kv_caches[0].len_dev.data_ptr() == self._lens.data_ptr():
             ops.advance_len(self._lens, 1)
-        logits = self.embeddings.project(self.final_norm(x))
+        if t == 1 and kv_caches is not None and self.layers[-1].tc_projections(x.view(b, -1)) \
+                and self.config.vocab_size % 128 == 0:
+            # final RMSNorm + tied LM head in one tensor-core launch (model.py:141-142)
+            logits = ops.linear(x.view(b, -1), self.embeddings.weight, self.final_norm.weight,
+                                self.final_norm.eps).view(b, 1, -1)
+        else:
+            logits = self.embeddings.project(self.final_norm(x))
         out = {"logits": logits}
         if return_forecasts:
             out["forecasts"] = forecasts

@@ -486,3 +486,45 @@ def rope_qk(xq: torch.Tensor, xk: torch.Tensor, cos: torch.Tensor, sin: torch.Te
            xq.stride(2), xk.stride(0), xk.stride(1), xk.stride(2), cos.data_ptr(), sin.data_ptr(), cos.shape[0],
            offset, qo.data_ptr(), ko.data_ptr(), _stream(xq))
     return qo, ko
+
+
+LINEAR_EPILOGUES = {"store": 0, "residual": 1, "swiglu": 2}
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, norm_w: Optional[torch.Tensor] = None, eps: float = 1e-6,
+           epilogue: str = "store", res: Optional[torch.Tensor] = None,
+           out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """A decode-step projection on the tensor cores (sd_linear): out = X W^T
+    for x [M, K], w [N, K] (16-bit), with RMSNorm of x in front when norm_w is
+    given (model/norm.py:15-21) and one of the epilogues: "store", "residual"
+    (res + the projection, model/transformer.py:118-129; out may be res) or
+    "swiglu" (w = swiglu_weight(w_gate, w_up); silu(gate) * up, N/2 columns,
+    transformer.py:18-31)."""
+    _cuda(x, w, norm_w, res)
+    if x.dtype != w.dtype or (norm_w is not None and norm_w.dtype != x.dtype):
+        raise TypeError("x, w and the norm gain must share a 16-bit dtype")
+    x = _inner1(x)
+    w = w.contiguous()
+    m, k = x.shape
+    n = w.shape[0]
+    ncols = n // 2 if epilogue == "swiglu" else n
+    if out is None:
+        out = torch.empty(m, ncols, dtype=x.dtype, device=x.device)
+    if epilogue == "residual" and (res is None or res.shape != (m, n) or res.stride(-1) != 1):
+        raise ValueError(f"the residual must be [{m}, {n}] with unit column stride")
+    nw = norm_w.contiguous() if norm_w is not None else None
+    L.call("sd_linear", x.data_ptr(), dtype_code(x), m, k, x.stride(0), w.data_ptr(), n,
+           nw.data_ptr() if nw is not None else None, eps, LINEAR_EPILOGUES[epilogue],
+           res.data_ptr() if res is not None else None, res.stride(0) if res is not None else 0, out.data_ptr(),
+           out.stride(0), error_buffer(x.device).data_ptr(), _stream(x))
+    return out
+
+
+def swiglu_weight(w_gate: torch.Tensor, w_up: torch.Tensor) -> torch.Tensor:
+    """[w_gate; w_up] interleaved in groups of 64 rows (64 gate rows, then the
+    64 up rows of the same output columns), the layout linear(...,
+    epilogue="swiglu") reads."""
+    f, k = w_gate.shape
+    if f % 64:
+        raise ValueError("the FFN width must be a multiple of 64")
+    return torch.stack((w_gate.view(f // 64, 64, k), w_up.view(f // 64, 64, k)), dim=1).reshape(2 * f, k).contiguous()
