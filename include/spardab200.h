@@ -143,6 +143,28 @@ SD_API int sd_decode_attention(const void *q, int dtype, int64_t B, int64_t Hq, 
                         int64_t seq_len_k, int block_size, float scale, void *out,
                         int64_t o_sb, int64_t o_sh, int32_t *err, void *stream);
 
+/* sd_decode_select followed by sd_decode_attention without caller buffers:
+ * the selected-block lists and counts live in a fixed device array of this
+ * library (no device allocation in the call, no workspace argument).  No
+ * counterpart in the reference (its decode allocates the lists as tensors,
+ * model/attention/sparse.py:108-181); for callers that cannot allocate device
+ * memory per call -- a host binding through this C ABI alone, or a serving
+ * runtime that forbids allocation.  Arguments mean what they mean in the two
+ * chained entry points (H of sd_decode_select = Hkv).  Limits of the fixed
+ * scratch: B * Hkv <= 4096 and min(ceil(L / block_size), top_k + 2) <= 64,
+ * else SD_ERR_UNSUPPORTED (the two chained entry points have no such limit).
+ * The first call on a device looks up the scratch address with that device
+ * current (make it before any stream capture); calls whose kernels may
+ * overlap on one device (unordered streams, concurrent host threads) race on
+ * the shared scratch. */
+SD_API int sd_decode_sparse_noalloc(const void *q, int dtype, int64_t q_sb, int64_t q_sh, const void *forecast,
+                                    int f_dtype, int64_t f_sb, int64_t f_sh, const float *reps, int64_t r_sb,
+                                    int64_t r_sn, int64_t r_sh, const void *k_cache, const void *v_cache,
+                                    int64_t c_sb, int64_t c_sh, int64_t c_st, int64_t Tcap, int64_t B, int64_t Hq,
+                                    int64_t Hkv, int64_t D, int64_t seq_len_k, int block_size, int top_k, int rule,
+                                    float scale, void *out, int64_t o_sb, int64_t o_sh, int32_t *err,
+                                    void *stream);
+
 /* KV-cache append with the compressor fused in.  Replaces KVCache.update
  * (model/attention/base.py:19-29) for the block-major cache of this library:
  * k_cache, v_cache [B,H,Tcap,D] contiguous, proto_sum fp32 [B,H,NBcap,D]

@@ -31,6 +31,9 @@ _SIGS = {
     "sd_last_cuda_error": [],
     "sd_advance_len": [_c_void_p, _i32, _i32, _c_void_p],
     "sd_set_programmatic_launch": [_i32],
+    "sd_decode_sparse_noalloc": [_c_void_p, _i32, _i64, _i64, _c_void_p, _i32, _i64, _i64, _c_void_p, _i64, _i64,
+                                 _i64, _c_void_p, _c_void_p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
+                                 _i32, _i32, _i32, _f32, _c_void_p, _i64, _i64, _c_void_p, _c_void_p],
     "sd_linear": [_c_void_p, _i32, _i64, _i64, _i64, _c_void_p, _i64, _c_void_p, _f32, _i32, _c_void_p, _i64,
                   _c_void_p, _i64, _c_void_p, _c_void_p],
     "sd_compress_blocks": [_c_void_p, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _c_void_p, _c_void_p],
