@@ -637,6 +637,33 @@ def _event_time_s(fn, reps=10, warm=3):
     return e0.elapsed_time(e1) / 1000.0 / reps
 
 
+def _graph_time_s(fns):
+    """Average device time per call of the calls fns[i]() captured back to
+    back in one CUDA graph (no host launch gaps between them), from one timed
+    replay after a warm one."""
+    import torch
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for fn in fns:
+            fn()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for fn in fns:
+            fn()
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    del g
+    return e0.elapsed_time(e1) / 1000.0 / len(fns)
+
+
 def fp32_simt_peak_tflops(dev_index: int) -> float:
     """Nominal fp32 CUDA-core rate: SMs x 128 lanes x 2 flops x max SM clock."""
     import torch
@@ -671,13 +698,15 @@ def run_kernels(local: int):
     k_tok = k_store.permute(0, 2, 1, 3)  # the reference's [B, T, H, D] view of the block-major store
     s = _event_time_s(lambda: ops.compress_blocks(k_tok, 64))
     by = k_store.numel() * 2 + B * (T // 64) * H * 64 * 4
-    out["compress_blocks"] = {"kernel": "sd::compress_blocks_kernel (sd_compress_blocks)", "us": round(s * 1e6, 2),
+    out["compress_blocks"] = {"kernel": "sd::compress_blocks_vec_kernel (sd_compress_blocks)", "us": round(s * 1e6, 2),
                               "bytes": by, "gbs": round(by / s / 1e9, 1), "frac": round(by / s / 1e9 / hbm, 4),
                               "shape": "K [64, 16384, 4, 64] bf16 -> prototypes fp32 [64, 256, 4, 64]"}
-    idx = torch.randint(0, T // 64, (B, H, 10), generator=g, device=dev)
-    s = _event_time_s(lambda: ops.gather_kv_blocks(k_store, v_store, idx, 64))
+    # ten index sets, one per call: 10 x 42 MB of rows, beyond the L2, and no
+    # host launch gaps (one graph of the ten calls)
+    idxs = [torch.randint(0, T // 64, (B, H, 10), generator=g, device=dev) for _ in range(10)]
+    s = _graph_time_s([lambda i=i: ops.gather_kv_blocks(k_store, v_store, i, 64) for i in idxs])
     by = 2 * 2 * B * H * 10 * 64 * 64 * 2  # K and V rows read and written
-    out["gather_kv_blocks"] = {"kernel": "sd::gather_kv_kernel (sd_gather_kv_blocks)", "us": round(s * 1e6, 2),
+    out["gather_kv_blocks"] = {"kernel": "sd::gather_kv_vec_kernel (sd_gather_kv_blocks)", "us": round(s * 1e6, 2),
                                "bytes": by, "gbs": round(by / s / 1e9, 1), "frac": round(by / s / 1e9 / hbm, 4),
                                "shape": "10 blocks of 64 rows per (sequence, kv head), 64 x 4, bf16"}
     del k_store, v_store, k_tok
@@ -693,7 +722,7 @@ def run_kernels(local: int):
                                     "frac": round(fl / s / 1e12 / peak32, 4),
                                     "shape": "forecast [1, 32768, 4, 64] bf16 x prototypes [1, 512, 4, 64] fp32"}
     _, topk = ops.select_blocks(f, reps, 8, 64, False, return_scores=False)
-    s = _event_time_s(lambda: ops.prefill_lists("chunked_forecast", 1, H, Tp, 64, 8, topk, True, device=dev))
+    s = _graph_time_s([lambda: ops.prefill_lists("chunked_forecast", 1, H, Tp, 64, 8, topk, True, device=dev)] * 10)
     by = topk.numel() * 8 + H * (Tp // 64) * (10 + 1) * 4
     out["prefill_lists"] = {"kernel": "sd::prefill_lists_kernel (sd_prefill_lists, chunked forecast)",
                             "us": round(s * 1e6, 2), "bytes": by, "gbs": round(by / s / 1e9, 1),

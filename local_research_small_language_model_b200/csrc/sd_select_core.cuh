@@ -184,10 +184,10 @@ template <int K2> __device__ __forceinline__ void merge_lanes(float &v, int &i) 
 // for i = 0..15 (coalesced, 16 loads in flight), then a 4-step reduce-scatter
 // leaves block 32c+2*l16+half's score in that lane; the dot products sum in
 // the same order as score_blocks (per-lane fma chain over 4 dims, then lane
-// pairs 8, 4, 2, 1 apart), so scores are bit-identical.  Up to kChunks chunks
-// are scored at once, their K2-lane groups sorted, and the lists merged in a
-// tournament (registers, then lane groups), which keeps the dependent
-// shuffle chain short; warp 0 merges the warps' lists the same way.  Writes
+// pairs 8, 4, 2, 1 apart), so scores are bit-identical.  Each chunk's K2-lane
+// groups are sorted and merged across lanes, then into the warp's running
+// list; warp 0 merges the warps' lists the same way.  The order of merges
+// does not change the result: entries are ordered by (value desc, index asc).  Writes
 // kk <= K2 (index, value) pairs best-first to out_idx (-1 when fewer than kk
 // entries exist) and out_val (nullable); NaN scores are never chosen.  All
 // threads of warp group g (at most 8 warps) call it; it ends with the group's
@@ -199,66 +199,52 @@ template <int K2, typename Row>
 __device__ __forceinline__ void cta_score_topk_k2(Row row, float4 fv, int n, int n_scored, int excl, float mul,
                                                   int kk, int *out_idx, float *out_val, float *sv, int *si,
                                                   const WarpGroup &g) {
-  constexpr int kChunks = 4;
   const int lane = threadIdx.x & 31, warp = g.warp(), nw = g.nw;
   const int half = lane >> 4, l16 = lane & 15;
   if (n_scored > n) n_scored = n;
   float rv = -INFINITY;  // running best-first list of this warp (K2-lane groups)
   int ri = kNoBlock;
-  for (int base = 32 * warp; base < n; base += 32 * nw * kChunks) {
-    float cv[kChunks];
-    int ci[kChunks];
+  // one 32-block chunk per iteration; the loop stays rolled so its code is
+  // fetched once however many chunks a warp takes (the kernels that inline
+  // this run it once per launch, where instruction fetch, not issue, is what
+  // an unrolled copy would cost)
+#pragma unroll 1
+  for (int c0 = 32 * warp; c0 < n; c0 += 32 * nw) {
+    float p[16];
 #pragma unroll
-    for (int c = 0; c < kChunks; ++c) {
-      const int c0 = base + 32 * nw * c;
-      cv[c] = -INFINITY;
-      ci[c] = kNoBlock;
-      if (c0 >= n) continue;  // warp-uniform: nothing left for this chunk
-      float p[16];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int j = c0 + 2 * i + half;
-        float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (j < n_scored) r = reinterpret_cast<const float4 *>(row(j))[l16];
-        float a = 0.f;
-        a = fmaf(fv.x, r.x, a);
-        a = fmaf(fv.y, r.y, a);
-        a = fmaf(fv.z, r.z, a);
-        a = fmaf(fv.w, r.w, a);
-        p[i] = a;
-      }
-#pragma unroll
-      for (int d = 8; d > 0; d >>= 1) {
-        const bool hi = (lane & d) != 0;
-#pragma unroll
-        for (int j = 0; j < d; ++j) {
-          const float send = hi ? p[j] : p[j + d];
-          const float keep = hi ? p[j + d] : p[j];
-          p[j] = keep + __shfl_xor_sync(0xffffffffu, send, d);
-        }
-      }
-      int b = c0 + 2 * l16 + half;
-      float v = b < n_scored ? p[0] * mul : -INFINITY;
-      const bool ok = b < n && b != excl && v == v;
-      cv[c] = ok ? v : -INFINITY;
-      ci[c] = ok ? b : kNoBlock;
+    for (int i = 0; i < 16; ++i) {
+      const int j = c0 + 2 * i + half;
+      float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (j < n_scored) r = reinterpret_cast<const float4 *>(row(j))[l16];
+      float a = 0.f;
+      a = fmaf(fv.x, r.x, a);
+      a = fmaf(fv.y, r.y, a);
+      a = fmaf(fv.z, r.z, a);
+      a = fmaf(fv.w, r.w, a);
+      p[i] = a;
     }
-    // (chunks past n hold only never-chosen entries: their sorts and merges
-    // are skipped, warp-uniformly)
 #pragma unroll
-    for (int c = 0; c < kChunks; ++c)
-      if (base + 32 * nw * c < n) sort_groups<K2>(cv[c], ci[c]);
+    for (int d = 8; d > 0; d >>= 1) {
+      const bool hi = (lane & d) != 0;
 #pragma unroll
-    for (int w = 1; w < kChunks; w <<= 1)
-#pragma unroll
-      for (int c = 0; c + w < kChunks; c += 2 * w)
-        if (base + 32 * nw * (c + w) < n) merge_regs<K2>(cv[c], ci[c], cv[c + w], ci[c + w]);
-    merge_lanes<K2>(cv[0], ci[0]);
-    if (base == 32 * warp) {  // first round: nothing to merge with yet
-      rv = cv[0];
-      ri = ci[0];
+      for (int j = 0; j < d; ++j) {
+        const float send = hi ? p[j] : p[j + d];
+        const float keep = hi ? p[j + d] : p[j];
+        p[j] = keep + __shfl_xor_sync(0xffffffffu, send, d);
+      }
+    }
+    const int b = c0 + 2 * l16 + half;
+    const float v = b < n_scored ? p[0] * mul : -INFINITY;
+    const bool ok = b < n && b != excl && v == v;
+    float cv = ok ? v : -INFINITY;
+    int ci = ok ? b : kNoBlock;
+    sort_groups<K2>(cv, ci);
+    merge_lanes<K2>(cv, ci);
+    if (c0 == 32 * warp) {  // first chunk: nothing to merge with yet
+      rv = cv;
+      ri = ci;
     } else {
-      merge_regs<K2>(rv, ri, cv[0], ci[0]);  // both lists sit in lanes 0..K2-1
+      merge_regs<K2>(rv, ri, cv, ci);  // both lists sit in lanes 0..K2-1
     }
   }
   if (lane < K2) {

@@ -349,11 +349,15 @@ def test_rmsnorm_matches_reference_formula(dev, dt, rows, c, offset):
     torch.testing.assert_close(got.float(), ref.float(), rtol=tol, atol=tol)
 
 
-@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
-def test_silu_mul_matches_reference_formula(dev, dt):
-    """model/transformer.py:30-31 on a fused [gate | up] projection."""
-    gu = t(normal((64, 4096), seed=3), dev, dt)
-    ref = torch.nn.functional.silu(gu[:, :2048]) * gu[:, 2048:]
+@pytest.mark.parametrize("dt,rows,f", [(torch.float32, 64, 2048), (torch.bfloat16, 64, 2048),
+                                       (torch.float16, 4096, 2048), (torch.bfloat16, 70000, 64),
+                                       (torch.bfloat16, 5, 1001)])
+def test_silu_mul_matches_reference_formula(dev, dt, rows, f):
+    """model/transformer.py:30-31 on a fused [gate | up] projection: the
+    16-byte-chunk kernel (16-bit, F % 8 == 0; also past 65,535 rows) and the
+    scalar kernel (fp32, F = 1001)."""
+    gu = t(normal((rows, 2 * f), seed=3), dev, dt)
+    ref = torch.nn.functional.silu(gu[:, :f]) * gu[:, f:]
     torch.testing.assert_close(ops.silu_mul(gu).float(), ref.float(), rtol=1e-5 if dt == torch.float32 else 8e-3,
                                atol=1e-6 if dt == torch.float32 else 8e-3)
 
