@@ -664,19 +664,6 @@ def _graph_time_s(fns):
     return e0.elapsed_time(e1) / 1000.0 / len(fns)
 
 
-def fp32_simt_peak_tflops(dev_index: int) -> float:
-    """Nominal fp32 CUDA-core rate: SMs x 128 lanes x 2 flops x max SM clock."""
-    import torch
-    props = torch.cuda.get_device_properties(dev_index)
-    mhz = 1965.0
-    try:
-        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as fh:
-            mhz = float(json.load(fh).get("sm_max_mhz", mhz))
-    except Exception:
-        pass
-    return props.multi_processor_count * 128 * 2 * mhz * 1e6 / 1e12
-
-
 def run_kernels(local: int):
     """Standalone device time of the path's other kernels on BASELINE-sized
     inputs, against the HBM roofline (algorithmic bytes per launch / time):
@@ -715,11 +702,14 @@ def run_kernels(local: int):
     reps = torch.randn(1, Tp // 64, H, 64, generator=g, device=dev, dtype=torch.float32)
     s = _event_time_s(lambda: ops.select_blocks(f, reps, 8, 64, False, return_scores=False))
     fl = 2 * Tp * H * (Tp // 64) * 64
-    peak32 = fp32_simt_peak_tflops(local)
-    out["select_blocks_prefill"] = {"kernel": "sd::select_rows_tiled_kernel (sd_select_blocks, no score tensor)",
+    tpeak, tsrc = read_peak_tflops()
+    # the fp32 scores run as 3 bf16 MMAs per product (prototype split in hi /
+    # mid / lo parts): 3 x fl on the tensor cores, against the bf16 peak
+    out["select_blocks_prefill"] = {"kernel": "sd::seltc::select_rows_tc_kernel (sd_select_blocks, no score tensor)",
                                     "us": round(s * 1e6, 2), "flops": fl, "tflops": round(fl / s / 1e12, 2),
-                                    "peak_fp32_simt_tflops": round(peak32, 1),
-                                    "frac": round(fl / s / 1e12 / peak32, 4),
+                                    "mma_flops": 3 * fl, "peak_bf16_tflops": round(tpeak, 1),
+                                    "frac": round(3 * fl / s / 1e12 / tpeak, 4),
+                                    "bound": "issue: the per-row top-8 scan of the scores read from tensor memory",
                                     "shape": "forecast [1, 32768, 4, 64] bf16 x prototypes [1, 512, 4, 64] fp32"}
     _, topk = ops.select_blocks(f, reps, 8, 64, False, return_scores=False)
     s = _graph_time_s([lambda: ops.prefill_lists("chunked_forecast", 1, H, Tp, 64, 8, topk, True, device=dev)] * 10)

@@ -4,6 +4,13 @@
 
 namespace sd {
 
+// sd_select_tc.cu: the tensor-core many-row selector (bf16 forecast, D = 64,
+// k <= 8, no score tensor); SD_ERR_UNSUPPORTED where it does not apply.
+int launch_select_rows_tc(const void *forecast, int f_dtype, int64_t B, int64_t Tq, int64_t H, int64_t D, int64_t f_sb,
+                          int64_t f_st, int64_t f_sh, const float *reps, int64_t NB, int64_t r_sb, int64_t r_sn,
+                          int64_t r_sh, int k, int block_size, int causal, int64_t q_offset, int64_t *topk_idx,
+                          int32_t *err, cudaStream_t s);
+
 constexpr int kSelThreads = 256;
 constexpr int kChunk = 64;  // prototypes staged per step
 
@@ -206,41 +213,9 @@ __global__ void __launch_bounds__(256)
         ci[u] = ok ? static_cast<int>(j) : kNoBlock;
       }
       if (j0 == 0) {
-#pragma unroll
-        for (int u = 0; u < 4; ++u) sort_groups<8>(cv[u], ci[u]);
-        merge_regs<8>(cv[0], ci[0], cv[1], ci[1]);
-        merge_regs<8>(cv[2], ci[2], cv[3], ci[3]);
-        merge_regs<8>(cv[0], ci[0], cv[2], ci[2]);
-        merge_lanes<8>(cv[0], ci[0]);
-        merge_regs<8>(rv[q], ri[q], cv[0], ci[0]);
+        fold_first8<4>(rv[q], ri[q], cv, ci);
       } else {
-        float tv = __shfl_sync(0xffffffffu, rv[q], 7);
-        int ti = __shfl_sync(0xffffffffu, ri[q], 7);
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          unsigned m = __ballot_sync(0xffffffffu, ci[u] != kNoBlock && (ti == kNoBlock || better(cv[u], ci[u], tv, ti)));
-          while (m) {
-            const int src = __ffs(m) - 1;
-            m &= m - 1;
-            const float nv = __shfl_sync(0xffffffffu, cv[u], src);
-            const int ni = __shfl_sync(0xffffffffu, ci[u], src);
-            if (!(ti == kNoBlock || better(nv, ni, tv, ti))) continue;  // an earlier insertion raised the bar
-            // position = entries better than the newcomer; later entries move down one lane
-            const bool above = lane < 8 && ri[q] != kNoBlock && better(rv[q], ri[q], nv, ni);
-            const int pos = __popc(__ballot_sync(0xffffffffu, above));
-            const float upv = __shfl_up_sync(0xffffffffu, rv[q], 1);
-            const int upi = __shfl_up_sync(0xffffffffu, ri[q], 1);
-            if (lane < 8 && lane > pos) {
-              rv[q] = upv;
-              ri[q] = upi;
-            } else if (lane == pos) {
-              rv[q] = nv;
-              ri[q] = ni;
-            }
-            tv = __shfl_sync(0xffffffffu, rv[q], 7);
-            ti = __shfl_sync(0xffffffffu, ri[q], 7);
-          }
-        }
+        fold_insert8<4>(rv[q], ri[q], cv, ci);
       }
     }
   }
@@ -314,6 +289,12 @@ extern "C" int sd_select_blocks(const void *forecast, int f_dtype, int64_t B, in
   if (D < 1 || D > 256) return SD_ERR_UNSUPPORTED;
   const int k = static_cast<int>(top_k < NB ? top_k : NB);
   if (k > 64 || NB > 24576 || B > 65535 || H > 65535) return SD_ERR_UNSUPPORTED;
+  if (!scores) {
+    const int r = sd::launch_select_rows_tc(forecast, f_dtype, B, Tq, H, D, f_sb, f_st, f_sh, reps, NB, r_sb, r_sn,
+                                            r_sh, k, block_size, causal, q_offset, topk_idx, nullptr,
+                                            static_cast<cudaStream_t>(stream));
+    if (r != SD_ERR_UNSUPPORTED) return r;
+  }
   if (D == 64 && k <= 8 && Tq >= sd::kTileRows && (r_sn % 4) == 0 && (r_sb % 4) == 0 && (r_sh % 4) == 0 &&
       sd::aligned16(reps)) {
     // many rows: register-tiled scoring and register top-k

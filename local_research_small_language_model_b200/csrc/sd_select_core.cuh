@@ -269,6 +269,58 @@ __device__ __forceinline__ void cta_score_topk_k2(Row row, float4 fv, int n, int
   g.sync();
 }
 
+// Folding U candidates per lane into a running best-first top-8 list held in
+// lanes 0..7 (rv, ri; the rest of the lanes hold (-inf, kNoBlock) pads), for
+// warps that walk one row's scores chunk by chunk.  The first fold sorts the
+// candidates' 8-lane groups and merges them in a tournament.  Later folds:
+// only a candidate that beats the list's 8th entry can enter, which few do,
+// so a ballot filters against that threshold and the survivors are inserted
+// one at a time.  Both give the best 8 of everything folded so far, by
+// (value desc, index asc).
+template <int U>
+__device__ __forceinline__ void fold_first8(float &rv, int &ri, float (&cv)[U], int (&ci)[U]) {
+#pragma unroll
+  for (int u = 0; u < U; ++u) sort_groups<8>(cv[u], ci[u]);
+#pragma unroll
+  for (int w = 1; w < U; w <<= 1)
+#pragma unroll
+    for (int u = 0; u + w < U; u += 2 * w) merge_regs<8>(cv[u], ci[u], cv[u + w], ci[u + w]);
+  merge_lanes<8>(cv[0], ci[0]);
+  merge_regs<8>(rv, ri, cv[0], ci[0]);
+}
+
+template <int U>
+__device__ __forceinline__ void fold_insert8(float &rv, int &ri, const float (&cv)[U], const int (&ci)[U]) {
+  const int lane = threadIdx.x & 31;
+  float tv = __shfl_sync(0xffffffffu, rv, 7);
+  int ti = __shfl_sync(0xffffffffu, ri, 7);
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    unsigned m = __ballot_sync(0xffffffffu, ci[u] != kNoBlock && (ti == kNoBlock || better(cv[u], ci[u], tv, ti)));
+    while (m) {
+      const int src = __ffs(m) - 1;
+      m &= m - 1;
+      const float nv = __shfl_sync(0xffffffffu, cv[u], src);
+      const int ni = __shfl_sync(0xffffffffu, ci[u], src);
+      if (!(ti == kNoBlock || better(nv, ni, tv, ti))) continue;  // an earlier insertion raised the bar
+      // position = entries better than the newcomer; later entries move down one lane
+      const bool above = lane < 8 && ri != kNoBlock && better(rv, ri, nv, ni);
+      const int pos = __popc(__ballot_sync(0xffffffffu, above));
+      const float upv = __shfl_up_sync(0xffffffffu, rv, 1);
+      const int upi = __shfl_up_sync(0xffffffffu, ri, 1);
+      if (lane < 8 && lane > pos) {
+        rv = upv;
+        ri = upi;
+      } else if (lane == pos) {
+        rv = nv;
+        ri = ni;
+      }
+      tv = __shfl_sync(0xffffffffu, rv, 7);
+      ti = __shfl_sync(0xffffffffu, ri, 7);
+    }
+  }
+}
+
 // Scoring + top-kk (kk <= 32) by warp group g with caller-provided scratch
 // sv, si (g.nw * 32 entries each).
 template <typename Row>
