@@ -7,16 +7,20 @@
 // query heads of the kv head give 64*G query rows, laid out as two 128-row
 // MMA tiles (tile x holds heads 2x and 2x+1; missing heads are zero rows).
 // For every listed key block (64 keys, staged by TMA with 128-byte swizzle in
-// a 3-deep ring shared by the two tiles), each tile's warpgroup runs its own
+// a 2-deep ring shared by the two tiles), each tile's warpgroup runs its own
 // pipeline (ping-pong: one tile's softmax overlaps the other's MMAs):
 //   S_x = Q_x K^T       tcgen05.mma M=128 N=64 K=64 (4 instructions), fp32 in TMEM
 //   softmax             one thread per query row: tcgen05.ld of its 64 scores,
 //                       masks (block membership, causality, length), online
-//                       max/sum in fp32, P row -> 16-bit -> swizzled smem
-//   PV_x = P_x V        tcgen05.mma M=128 N=64 K=64 with V MN-major, into TMEM
-//   O_x = O_x*alpha+PV  in registers after a tcgen05.ld of the row
+//                       max/sum in fp32 with a lazily updated reference maximum
+//                       (raised only when a block exceeds it by 2^8, the
+//                       output rows in TMEM then rescaled), P row -> 16-bit ->
+//                       swizzled smem
+//   O_x += P_x V        tcgen05.mma M=128 N=64 K=64 with V MN-major, accumulated
+//                       in TMEM across the blocks (no per-block read-out)
 // The first thread of each warpgroup issues its tile's MMAs and commits them
-// to that tile's mbarriers; every wait is bounded.  TMEM: 256 columns (S0, S1, PV0, PV1) per CTA, <= 2 CTAs per SM.
+// to that tile's mbarriers; every wait is bounded.  TMEM: 256 columns (S0, S1,
+// O0, O1) per CTA, 2 CTAs per SM.
 #include <type_traits>
 
 #include "sd_prefill.cuh"
@@ -27,7 +31,7 @@ namespace sd {
 namespace tc {
 
 constexpr int kThreads = 256;
-constexpr int kStages = 3;
+constexpr int kStages = 2;
 constexpr int kRowsTile = 128;                  // MMA M
 constexpr int kTileBytes = kRowsTile * 128;     // 128 rows x 64 16-bit values
 constexpr int kKvBytes = 64 * 128;              // 64 keys x 64 16-bit values
@@ -99,10 +103,31 @@ __device__ __forceinline__ float ex2(float x) {
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// 16 consecutive fp32 columns into this thread's TMEM lane.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+      "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+      "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])),
+      "r"(__float_as_uint(v[11])), "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])),
+      "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15]))
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Lazy rescaling: a row keeps its reference maximum m (log2 units) until a
+// block's maximum exceeds it by more than this; the exponentials are then at
+// most 2^8, well inside bf16 and fp32, and the output rows in tensor memory
+// are rescaled only on those rare increases.
+constexpr float kRescaleLog2 = 8.0f;
+
 }  // namespace tc
 
 template <typename T>
-__global__ void __launch_bounds__(tc::kThreads, 1)
+__global__ void __launch_bounds__(tc::kThreads, 2)
     prefill_tc_kernel(const T *__restrict__ q, int64_t q_sb, int64_t q_st, int64_t q_sh,
                       const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv, int64_t T_,
                       int Hkv, int G, const int32_t *__restrict__ lists, const int32_t *__restrict__ counts, int lcap,
@@ -207,10 +232,7 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
   }
   const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
   const uint32_t t_s = tmem + lane_base + 64 * x;          // S_x columns
-  const uint32_t t_pv = tmem + lane_base + 128 + 64 * x;   // PV_x columns
-  float o[64];
-#pragma unroll
-  for (int d = 0; d < 64; ++d) o[d] = 0.f;
+  const uint32_t t_o = tmem + lane_base + 128 + 64 * x;    // O_x columns: the PV MMAs accumulate into them
   float m = -INFINITY, l = 0.f;
   const uint32_t id_s = idesc_f16(fmt, false), id_pv = idesc_f16(fmt, true);
   bool ok = true;
@@ -257,10 +279,10 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
     const int j = block_of(i);
     ok = mbar_wait_bounded(&s_bar[x], i & 1) && ok;
     fence_after_sync();
-    float alpha = 1.f;
+    float sc[64];
+    float mn = m, alpha = 1.f;
     if (warp_active) {
-      // softmax of this row's 64 scores
-      float sc[64];
+      // this row's 64 scores of block i
 #pragma unroll
       for (int c4 = 0; c4 < 4; ++c4) {
         float v[16];
@@ -294,8 +316,39 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
       float mt = sc[0];
 #pragma unroll
       for (int c = 1; c < 64; ++c) mt = fmaxf(mt, sc[c]);
-      const float mn = fmaxf(m, mt * scale_log2);  // scale_log2 > 0: max of the scaled scores
-      alpha = mn == -INFINITY ? 1.f : ex2(m - mn);
+      const float mts = mt * scale_log2;  // scale_log2 > 0: max of the scaled scores
+      if (mts > m + kRescaleLog2 || (m == -INFINITY && mts > -INFINITY)) {
+        mn = mts;
+        alpha = m == -INFINITY ? 0.f : ex2(m - mn);
+      }
+    }
+    // the previous block's PV MMA has finished with the P tile and with O
+    if (i > 0) {
+      ok = mbar_wait_bounded(&o_bar[x], (i - 1) & 1) && ok;
+      fence_after_sync();
+      // both tiles' MMAs that read stage (i - 1) % kStages are complete: the
+      // second tile to get here refills it
+      const int ps = (i - 1) % kStages;
+      if (leader && atomicAdd(&refill[ps], 1) == 1) {
+        refill[ps] = 0;
+        if (i - 1 + kStages < cnt) issue(i - 1 + kStages);
+      }
+    }
+    if (warp_active) {
+      if (i > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+        // a reference maximum rose: rescale the output rows so far (warp-wide
+        // TMEM access; rows that keep their maximum multiply by 1)
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {
+          float v[16];
+          tmem_ld16(t_o + 16 * c4, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int u = 0; u < 16; ++u) v[u] *= alpha;
+          tmem_st16(t_o + 16 * c4, v);
+        }
+        tmem_wait_st();
+      }
       const float nmn = mn == -INFINITY ? 0.f : -mn;  // rows with nothing visible yet keep p = 0
       float ps = 0.f;
       char *prow = sm + Smem::kP + x * kTileBytes;
@@ -320,38 +373,25 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     fence_before_sync();
     wg_sync();
-    // PV_x = P_x V (V tile MN-major: 64 keys of 128-byte rows), then the next
-    // block's S_x right behind it (S_x was read out above)
+    // O_x += P_x V (V tile MN-major: 64 keys of 128-byte rows; the first
+    // block starts O), then the next block's S_x right behind it (S_x was
+    // read out above)
     if (leader) {
       fence_after_sync();
       const uint32_t vaddr = smem_u32(sm + Smem::kV + s * kKvBytes);
 #pragma unroll
       for (int k = 0; k < 4; ++k)
         mma_f16(tmem + 128 + 64 * x, umma_desc_sw128(paddr + 32 * k, 16, 1024),
-                umma_desc_sw128(vaddr + 2048 * k, kKvBytes, 1024), id_pv, k > 0);
+                umma_desc_sw128(vaddr + 2048 * k, kKvBytes, 1024), id_pv, i > 0 || k > 0);
       mma_commit(&o_bar[x]);
       if (i + 1 < cnt) ok = issue_s(i + 1) && ok;
     }
-    ok = mbar_wait_bounded(&o_bar[x], i & 1) && ok;
-    fence_after_sync();
-    if (warp_active) {
-#pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
-        float v[16];
-        tmem_ld16(t_pv + 16 * c4, v);
-#pragma unroll
-        for (int u = 0; u < 16; ++u) o[16 * c4 + u] = fmaf(o[16 * c4 + u], alpha, v[u]);
-      }
-      tmem_wait_ld();
-    }
-    fence_before_sync();
-    // both MMAs of this tile that read stage s are complete: the second tile
-    // to get here refills the stage
-    if (leader && atomicAdd(&refill[s], 1) == 1) {
-      refill[s] = 0;
-      if (i + kStages < cnt) issue(i + kStages);
-    }
+    __syncwarp();
     if (wg_any(!ok)) break;
+  }
+  if (cnt > 0) {  // the last PV MMA
+    ok = mbar_wait_bounded(&o_bar[x], (cnt - 1) & 1) && ok;
+    fence_after_sync();
   }
   const bool failed = __syncthreads_or(!ok);
   if (failed) {  // a bounded wait expired: let copies in flight land, poison the rows
@@ -359,18 +399,33 @@ __global__ void __launch_bounds__(tc::kThreads, 1)
       for (int s = 0; s < kStages; ++s) mbar_wait_bounded(&full[s], 0, 1000000ull);
     l = __int_as_float(0x7fc00000);
   }
-  // ---- epilogue
-  if (row_ok) {
+  // ---- epilogue: O / l, from tensor memory (warp-wide loads)
+  if (warp_active) {
     T *op = out + b * o_sb + t * o_st + static_cast<int64_t>(h * G + g) * o_sh;
     const float inv = l > 0.f ? 1.0f / l : (l == l ? 0.f : l);
 #pragma unroll
-    for (int c8 = 0; c8 < 8; ++c8) {
-      uint4 w;
-      w.x = pack2<T>(o[8 * c8 + 0] * inv, o[8 * c8 + 1] * inv);
-      w.y = pack2<T>(o[8 * c8 + 2] * inv, o[8 * c8 + 3] * inv);
-      w.z = pack2<T>(o[8 * c8 + 4] * inv, o[8 * c8 + 5] * inv);
-      w.w = pack2<T>(o[8 * c8 + 6] * inv, o[8 * c8 + 7] * inv);
-      *reinterpret_cast<uint4 *>(op + 8 * c8) = w;
+    for (int c4 = 0; c4 < 4; ++c4) {
+      float v[16];
+      if (cnt > 0) {
+        tmem_ld16(t_o + 16 * c4, v);
+        tmem_wait_ld();
+      } else {
+#pragma unroll
+        for (int u = 0; u < 16; ++u) v[u] = 0.f;
+      }
+      if (row_ok) {
+        uint4 w0, w1;
+        w0.x = pack2<T>(v[0] * inv, v[1] * inv);
+        w0.y = pack2<T>(v[2] * inv, v[3] * inv);
+        w0.z = pack2<T>(v[4] * inv, v[5] * inv);
+        w0.w = pack2<T>(v[6] * inv, v[7] * inv);
+        w1.x = pack2<T>(v[8] * inv, v[9] * inv);
+        w1.y = pack2<T>(v[10] * inv, v[11] * inv);
+        w1.z = pack2<T>(v[12] * inv, v[13] * inv);
+        w1.w = pack2<T>(v[14] * inv, v[15] * inv);
+        *reinterpret_cast<uint4 *>(op + 16 * c4) = w0;
+        *reinterpret_cast<uint4 *>(op + 16 * c4 + 8) = w1;
+      }
     }
   }
   fence_before_sync();
