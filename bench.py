@@ -54,6 +54,9 @@ def parse():
     ap.add_argument("--offload", action="store_true",
                     help="BASELINE config 5 sample: K/V rows in pinned host memory, forecast-guided prefetch of the "
                          "selected blocks into device slots (use with e.g. --ctx 32768)")
+    ap.add_argument("--cache-blocks", type=int, default=None,
+                    help="with --offload: device slots per (sequence, kv head) for selected blocks (top-k..32; more "
+                         "than top-k make them a block cache with least-recently-used replacement)")
     ap.add_argument("--selection", choices=["kernel", "side-stream", "chain"], default="chain",
                     help="forecast selection inside the fused decode kernel, layer L+1's candidates computed on a "
                          "side stream during layer L, or at the end of layer L's fused kernel")
@@ -244,7 +247,8 @@ def run_b200(args, rank, world, local):
     model = SparDAB200Model(cfg).to(dev, torch.bfloat16).eval()
     for layer in model.layers:
         layer.use_tc_linear = args.projections == "tc"
-    caches = model.allocate_caches(B, ctx + W + 64, selection=args.selection, offload=args.offload)
+    caches = model.allocate_caches(B, ctx + W + 64, selection=args.selection, offload=args.offload,
+                                   cache_blocks=args.cache_blocks if args.offload else None)
     gen = torch.Generator(device=dev)
     gen.manual_seed(99 + rank)
     with torch.no_grad():
@@ -461,6 +465,7 @@ def run_b200(args, rank, world, local):
             "host_store_gb": round(sum(2 * c.host_k.numel() * c.host_k.element_size() for c in caches) / 1e9, 2),
             "h2d_bytes_per_step": round(h2d / args.steps),
             "h2d_gbs": round(h2d / (ms / 1000.0) / 1e9, 2),
+            "device_slots_per_head": caches[0].kslots,
             "prefetch_hit_rate": round(hits / wanted, 4) if wanted else None,
             "exposed_wait_us_per_step": round(w_ms * 1000.0 / max(args.probe_steps, 1), 2),
             "prefetch_us_per_layer": round(c_ms * 1000.0 / max(c_launch, 1), 2),

@@ -1210,7 +1210,7 @@ extern "C" int sd_decode_layer_offload(const void *qkv, int dtype, int64_t qkv_s
   if ((cand_idx == nullptr) != (cand_val == nullptr) || (cand_idx == nullptr) != (cand_slot == nullptr))
     return SD_ERR_INVALID;
   if (forecast != nullptr && cand_idx == nullptr) return SD_ERR_INVALID;
-  if (D != sd::kD || block_size != sd::kRows || kslots != top_k || top_k > 31 || NBcap > 16384 ||
+  if (D != sd::kD || block_size != sd::kRows || kslots < top_k || kslots > 32 || top_k > 31 || NBcap > 16384 ||
       B * Hkv > 0x7fffffff)
     return SD_ERR_UNSUPPORTED;
   if (!sd::aligned16(slot_k) || !sd::aligned16(slot_v) || !sd::aligned16(proto_sum)) return SD_ERR_ALIGN;

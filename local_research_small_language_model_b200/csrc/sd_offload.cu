@@ -13,7 +13,10 @@
 // resident (hits keep their slot; in forecast mode a block can sit in any
 // slot, in static/dense mode block j always uses slot 2 + j % kslots), copies
 // the missing ones host -> device with 16-byte loads spread over the CTA, and
-// records hit/miss/byte counts.  It runs on a side stream during the previous
+// records hit/miss/byte counts.  With more slots than candidates
+// (kslots > top_k) the slots form a block cache: a block stays resident until
+// its slot is needed, and a miss takes the free slot used least recently (the
+// position of its last use is kept per slot).  It runs on a side stream during the previous
 // layer, right after the candidate kernel that chose the blocks.
 #include "sd_common.cuh"
 
@@ -32,7 +35,11 @@ __global__ void __launch_bounds__(kPfThreads)
   __shared__ int miss_block[33], miss_slot[33], nmiss, nwant, nhit;
   const int bh = blockIdx.x;
   const int64_t pos = *cur_len;  // position the next token takes
-  int32_t *sb = slot_block + static_cast<int64_t>(bh) * (kslots + 1);
+  // per (sequence, kv head): block of each slot, the sink flag, then the
+  // position each slot was last used at
+  int32_t *sb = slot_block + static_cast<int64_t>(bh) * (2 * kslots + 1);
+  int32_t *sage = sb + kslots + 1;
+  __shared__ int slot_of_rank[32];
   if (threadIdx.x < 32) {
     const int lane = threadIdx.x;
     int nm = 0, want = 0, hit = 0;
@@ -54,22 +61,33 @@ __global__ void __launch_bounds__(kPfThreads)
           // slot `lane` keeps its block when some valid candidate wants it
           if (i < top_k && wi > 0 && wi < curr && wi == prev) keep = true;
         }
-        const unsigned freem = __ballot_sync(0xffffffffu, lane < kslots && !keep);
-        // m-th miss takes the m-th free slot (there are at least as many free
-        // slots as misses: kslots == top_k and a block occupies one slot)
+        const bool is_free = lane < kslots && !keep;
+        // rank of each free slot by (last use, slot): the m-th miss takes the
+        // free slot of rank m, the least recently used first (there are at
+        // least as many free slots as misses: kslots >= top_k and a block
+        // occupies one slot)
+        const int age = lane < kslots ? sage[lane] : 0;
+        int rank = 0;
+        for (int i = 0; i < kslots; ++i) {
+          const int ai = __shfl_sync(0xffffffffu, age, i);
+          const bool fi = __shfl_sync(0xffffffffu, is_free, i);
+          if (fi && (ai < age || (ai == age && i < lane))) ++rank;
+        }
+        if (is_free) slot_of_rank[rank] = lane;
+        __syncwarp();
         const bool need = valid && hs < 0;
         const int m = __popc(__ballot_sync(0xffffffffu, need) & ((1u << lane) - 1u));
-        unsigned f = freem;
-        for (int q = 0; q < m; ++q) f &= f - 1u;
-        const bool miss = need && f != 0u;
+        const bool miss = need;
         const unsigned missm = __ballot_sync(0xffffffffu, miss);
         int slot = hs;
         if (miss) {
-          slot = __ffs(f) - 1;
+          slot = slot_of_rank[m];
           miss_block[m] = w;
           miss_slot[m] = 2 + slot;
           sb[slot] = w;
         }
+        // every slot used this step (hits and fills) is stamped with the position
+        if (valid && slot >= 0) sage[slot] = static_cast<int>(pos);
         if (lane < top_k) cand_slot[static_cast<int64_t>(bh) * top_k + lane] = valid ? slot : -1;
         nm = __popc(missm);
         want = __popc(__ballot_sync(0xffffffffu, valid));
@@ -161,8 +179,8 @@ extern "C" int sd_offload_prefetch(const void *host_k, const void *host_v, int d
       host_tcap <= 0 || top_k <= 0)
     return SD_ERR_INVALID;
   if (cand_idx != nullptr && cand_slot == nullptr) return SD_ERR_INVALID;
-  if (D != sd::kHd || block_size != sd::kBlockRows || kslots != top_k || top_k > 31 || host_tcap % block_size ||
-      B * Hkv > 0x7fffffff)
+  if (D != sd::kHd || block_size != sd::kBlockRows || kslots < top_k || kslots > 32 || top_k > 31 ||
+      host_tcap % block_size || B * Hkv > 0x7fffffff)
     return SD_ERR_UNSUPPORTED;
   if (!sd::aligned16(host_k) || !sd::aligned16(host_v) || !sd::aligned16(slot_k) || !sd::aligned16(slot_v))
     return SD_ERR_ALIGN;

@@ -310,7 +310,7 @@ class SparDAB200Model(nn.Module):
 
     def allocate_caches(self, batch: int, max_seq_len: int, dtype: Optional[torch.dtype] = None,
                         device=None, overlap_selection: bool = True, offload: bool = False,
-                        selection: Optional[str] = None) -> List:
+                        selection: Optional[str] = None, cache_blocks: Optional[int] = None) -> List:
         """One cache per layer, sharing one device length array so a decode
         step bumps all lengths with a single launch.  With
         ``overlap_selection`` layer L+1's candidates for each decode step are
@@ -321,7 +321,10 @@ class SparDAB200Model(nn.Module):
         ``selection`` overrides ``overlap_selection``: "kernel" (each fused
         kernel scores its own blocks), "side-stream" (layer L+1's candidates on
         a side stream during layer L) or "chain" (layer L's fused kernel ends
-        by computing layer L+1's candidates)."""
+        by computing layer L+1's candidates).  ``cache_blocks`` (offload only):
+        device slots per (sequence, kv head) for selected blocks, top_k..32;
+        more than top_k keep blocks resident across steps with
+        least-recently-used replacement."""
         if selection is None:
             selection = "chain" if overlap_selection else "kernel"
         if selection not in ("kernel", "side-stream", "chain"):
@@ -336,7 +339,7 @@ class SparDAB200Model(nn.Module):
             if offload:
                 c = B200OffloadKVCache(batch, max_seq_len, cfg.n_kv_head, cfg.head_dim, device, dtype,
                                        transfer_stream=side, block_size=cfg.block_size, top_k=cfg.top_k_blocks,
-                                       len_dev=self._lens[i:i + 1])
+                                       len_dev=self._lens[i:i + 1], cache_blocks=cache_blocks)
             else:
                 c = B200KVCache(batch, max_seq_len, cfg.n_kv_head, cfg.head_dim, device, dtype, cfg.block_size,
                                 len_dev=self._lens[i:i + 1])

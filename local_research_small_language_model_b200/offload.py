@@ -10,10 +10,12 @@ the next step needs into device slots.  Block indices never travel to the host
 (the reference calls ``.to("cpu")`` on them, async_offload.py:78).
 
 Device state per layer:
-  slot_k, slot_v  [B, Hkv, (2 + top_k) * 64, D]: slot 0 = sink block 0, slot 1 =
-                  the block being appended to, slots 2.. = staged blocks;
-  slot_block      int32 [B, Hkv, top_k + 1]: which block each slot holds (-1
-                  empty; the last entry is 0 once the sink is loaded);
+  slot_k, slot_v  [B, Hkv, (2 + kslots) * 64, D]: slot 0 = sink block 0, slot 1 =
+                  the block being appended to, slots 2.. = staged blocks
+                  (kslots = top_k, or cache_blocks for an LRU block cache);
+  slot_block      int32 [B, Hkv, 2 * kslots + 1]: which block each slot holds
+                  (-1 empty), then 0 once the sink is loaded, then the
+                  position each slot was last used at;
   cand / cand_slot  the forecast candidates of the next step and their slots;
   proto_sum       fp32 running block sums (selection never reads the host);
   stats           int64 [3]: blocks wanted, hits, bytes copied host -> device.
@@ -43,7 +45,7 @@ class B200OffloadKVCache:
     def __init__(self, max_batch_size: int, max_seq_len: int, n_kv_head: int, head_dim: int,
                  gpu_device: torch.device, dtype: torch.dtype = torch.bfloat16, pin_memory: bool = True,
                  transfer_stream: Optional[torch.cuda.Stream] = None, block_size: int = 64, top_k: int = 8,
-                 len_dev: Optional[torch.Tensor] = None):
+                 len_dev: Optional[torch.Tensor] = None, cache_blocks: Optional[int] = None):
         gpu_device = torch.device(gpu_device)
         if gpu_device.type != "cuda":
             raise ValueError("the B200 offloaded cache needs a CUDA device")
@@ -58,7 +60,13 @@ class B200OffloadKVCache:
         self.gpu_device = gpu_device
         self.dtype = dtype
         self.block_size = block_size
-        self.kslots = top_k
+        # device slots for selected blocks besides the sink and the current
+        # block: top_k of them by default (each step's candidates); more make
+        # the slots a block cache with least-recently-used replacement
+        self.top_k = top_k
+        self.kslots = top_k if cache_blocks is None else int(cache_blocks)
+        if not top_k <= self.kslots <= 32:
+            raise ValueError(f"cache_blocks must be in [top_k, 32], got {self.kslots}")
         self.tcap = ops.num_blocks(max_seq_len, block_size) * block_size
         self.nbcap = self.tcap // block_size
         shape = (max_batch_size, n_kv_head, self.tcap, head_dim)
@@ -66,10 +74,12 @@ class B200OffloadKVCache:
         self.host_v = torch.zeros(shape, dtype=dtype, pin_memory=True)
         for t in (self.host_k, self.host_v):
             _check_device_mapped(t, gpu_device)
-        s = (2 + top_k) * block_size
+        s = (2 + self.kslots) * block_size
         self.slot_k = torch.zeros(max_batch_size, n_kv_head, s, head_dim, device=gpu_device, dtype=dtype)
         self.slot_v = torch.zeros_like(self.slot_k)
-        self.slot_block = torch.full((max_batch_size, n_kv_head, top_k + 1), -1, dtype=torch.int32,
+        # per (sequence, kv head): the block in each slot, the sink flag, the
+        # position each slot was last used at
+        self.slot_block = torch.full((max_batch_size, n_kv_head, 2 * self.kslots + 1), -1, dtype=torch.int32,
                                      device=gpu_device)
         self.cand_slot = torch.full((max_batch_size, n_kv_head, top_k), -1, dtype=torch.int32, device=gpu_device)
         self.cand = (torch.full((max_batch_size, n_kv_head, top_k), -1, dtype=torch.int32, device=gpu_device),

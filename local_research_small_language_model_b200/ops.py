@@ -336,7 +336,7 @@ def offload_prefetch(cache, cand_idx: Optional[torch.Tensor] = None) -> None:
     b, h, _, d = cache.slot_k.shape
     L.call("sd_offload_prefetch", cache.host_k.data_ptr(), cache.host_v.data_ptr(), dtype_code(cache.slot_k), b, h,
            d, cache.tcap, cache.slot_k.data_ptr(), cache.slot_v.data_ptr(), cache.kslots, cache.len_dev.data_ptr(),
-           cache.block_size, cache.kslots, cand_idx.data_ptr() if cand_idx is not None else None,
+           cache.block_size, cache.top_k, cand_idx.data_ptr() if cand_idx is not None else None,
            cache.slot_block.data_ptr(), cache.cand_slot.data_ptr(), cache.stats.data_ptr(),
            torch.cuda.current_stream(cache.slot_k.device).cuda_stream)
 
@@ -368,7 +368,7 @@ def decode_layer_offload(qkv: torch.Tensor, forecast: Optional[torch.Tensor], ro
     L.call("sd_decode_layer_offload", qkv.data_ptr(), dtype_code(qkv), qkv.stride(0), *fargs, rope_cos.data_ptr(),
            rope_sin.data_ptr(), rope_cos.shape[0], cache.len_dev.data_ptr(), cache.host_k.data_ptr(),
            cache.host_v.data_ptr(), cache.tcap, cache.slot_k.data_ptr(), cache.slot_v.data_ptr(), cache.kslots,
-           cache.proto_sum.data_ptr(), b, n_head, hkv, d, cache.nbcap, cache.block_size, cache.kslots,
+           cache.proto_sum.data_ptr(), b, n_head, hkv, d, cache.nbcap, cache.block_size, cache.top_k,
            rule_code(rule, select_before_append),
            sc, out.data_ptr(), out.stride(0),
            cand[0].data_ptr() if cand is not None else None,

@@ -37,16 +37,17 @@ def _prefill(caches, b, pre, dev, seed):
             c.update(k, v)
 
 
-@pytest.mark.parametrize("rule", ["reference", "absolute"])
+@pytest.mark.parametrize("rule,cache_blocks", [("reference", None), ("absolute", None), ("absolute", 24)])
 @torch.no_grad()
-def test_offload_decode_matches_device_cache(dev, rule):
+def test_offload_decode_matches_device_cache(dev, rule, cache_blocks):
     """70 steps from 900 cached tokens (crossing the block boundary at 960):
-    identical logits, identical host store and block sums."""
+    identical logits, identical host store and block sums; with a 24-slot
+    block cache (least-recently-used replacement) as with the default 8."""
     m1, sc = _model(dev, rule)
     m2, _ = _model(dev, rule)
     b, pre = 3, 900
     c1 = m1.allocate_caches(b, 2048)
-    c2 = m2.allocate_caches(b, 2048, offload=True)
+    c2 = m2.allocate_caches(b, 2048, offload=True, cache_blocks=cache_blocks)
     assert all(isinstance(c, B200OffloadKVCache) for c in c2)
     _prefill([c1, c2], b, pre, dev, seed=5)
     ids = torch.randint(0, sc.vocab_size, (b, 1), generator=torch.Generator(device="cpu").manual_seed(3)).to(dev)
@@ -252,3 +253,29 @@ def test_prefetch_reference_rule_vs_golden(dev, golden, case):
         got = set(sn[ix][:cn[ix]].tolist())
         assert {0, curr} <= set(rs[ix][rv[ix]].tolist()) and {0, curr} <= got
         assert got == set(osel[ix][:ocnt[ix]].tolist()), ix
+
+
+@torch.no_grad()
+def test_block_cache_keeps_blocks_resident(dev):
+    """The same decode with 8 and with 24 device slots per (sequence, head):
+    identical logits, and the larger cache hits at least as often (blocks
+    chosen again within its reach are not copied again)."""
+    hits = []
+    logits = []
+    for cb in (None, 24):
+        m, sc = _model(dev, "absolute")
+        c = m.allocate_caches(3, 2048, offload=True, cache_blocks=cb)
+        _prefill([c], 3, 900, dev, seed=5)
+        ids = torch.randint(0, sc.vocab_size, (3, 1), generator=torch.Generator(device="cpu").manual_seed(3)).to(dev)
+        out = []
+        for step in range(40):
+            lg = m(ids, kv_caches=c)["logits"]
+            out.append(lg)
+            ids = lg[:, -1:].argmax(-1)
+        sd.ops.check_device_errors(dev)
+        logits.append(torch.cat(out))
+        st = sum(x.stats.cpu() for x in c[1:]).tolist()
+        assert st[0] > 0
+        hits.append(st[1])
+    assert torch.equal(logits[0], logits[1])
+    assert hits[1] >= hits[0]
