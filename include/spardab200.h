@@ -336,8 +336,10 @@ SD_API int sd_set_programmatic_launch(int enable);
  * [B, Hkv, host_tcap, 64] (block-major, read and written by the GPU through
  * unified addressing).  Per (sequence, kv head) the device keeps a slot buffer
  * slot_k/slot_v [B, Hkv, (2 + kslots) * 64, 64]: slot 0 the sink block, slot 1
- * the block being appended to, slots 2.. the blocks staged for this step.
- * kslots == top_k <= 31, block_size = 64, head_dim = 64. */
+ * the block being appended to, slots 2.. the blocks staged for this step
+ * (and, with kslots > top_k, blocks kept resident from earlier steps: a block
+ * cache with least-recently-used replacement).  top_k <= kslots <= 32,
+ * top_k <= 31, block_size = 64, head_dim = 64. */
 
 /* Forecast-guided prefetch.  Replaces AsyncOffloadedKVCache.async_transfer_
  * selected_blocks (model/attention/async_offload.py:55-112) and the transfer
@@ -346,8 +348,10 @@ SD_API int sd_set_programmatic_launch(int enable);
  * cand_idx [B, Hkv, top_k] (the side-stream top-k, forecast mode) or, with
  * cand_idx NULL or on dense steps, the static window / every block.  Blocks
  * already resident keep their slot; missing ones are copied from the host
- * store.  slot_block int32 [B, Hkv, kslots + 1] is the residency state (init
- * -1; the last entry tracks the sink); cand_slot int32 [B, Hkv, top_k]
+ * store; a miss takes the free slot used least recently.  slot_block int32
+ * [B, Hkv, 2 * kslots + 1] is the residency state (init -1): the block of
+ * each slot, then the sink flag, then the position each slot was last used
+ * at; cand_slot int32 [B, Hkv, top_k]
  * receives each candidate's slot (-1 = not staged).  stats (nullable) u64[3]
  * accumulates wanted blocks, hits and bytes copied. */
 SD_API int sd_offload_prefetch(const void *host_k, const void *host_v, int dtype, int64_t B, int64_t Hkv,
