@@ -18,15 +18,15 @@
 //     planes, written in the same swizzled K-major layout;
 //   * one thread issues 3 planes x 4 K-steps of tcgen05.mma kind::f16 (M=128
 //     rows, N=128 blocks, K=16) into a 128-column fp32 accumulator in TMEM;
-//   * in two passes of 64 blocks, thread t moves 32 scores of its row (TMEM
-//     lane t % 128) into shared memory with the causal mask applied, and
-//     each warp folds the pass into the running top-8 lists of its 16 rows
-//     (warp-cooperative: a tournament for the first pass, then a ballot
-//     against each list's 8th entry and one-at-a-time insertion of the few
-//     that beat it);
-//   * blocks no chunk reached fill the lists with -inf entries in index
-//     order (the reference's topk over -inf scores), and the k best indices
-//     are written.
+//   * thread t reads 64 scores of its row (TMEM lane t % 128, columns
+//     64 * (t / 128) ..) with the causal mask applied, forms ordered 64-bit
+//     keys (order-preserving score bits above the complemented block index)
+//     and keeps a top-8 of its half row in registers; a batch's keys are
+//     staged in shared memory and the warp inserts the candidates that beat
+//     the list's 8th entry in rounds, one per lane per round;
+//   * the two half-row lists are merged, blocks past the row's last visible
+//     one follow as -inf entries in index order (the reference's topk over
+//     -inf scores), and the k best indices are written.
 // The order is (value desc, index asc) everywhere; NaN scores are never
 // chosen.  Every mbarrier wait is bounded.
 #include "sd_select_core.cuh"
