@@ -599,7 +599,13 @@ template <typename T> struct SlotMap {
   int kslots = 0;
 };
 
-template <typename T, typename F, int G>
+// kCands: the launch passes precomputed candidates (chained or side-stream
+// selection).  That instantiation leaves out the in-kernel scoring code, so
+// the code the common path runs is compact: the kernel runs once per layer
+// between library GEMMs, its instructions are fetched cold, and a fetch that
+// has to cross the unused scoring code costs microseconds while the tile
+// loads keep HBM busy.
+template <typename T, typename F, int G, bool kCands>
 __global__ void __launch_bounds__(2 * kThreads)
     decode_layer_kernel(const T *__restrict__ qkv, int64_t qkv_sb, const F *__restrict__ fc, int64_t f_sb,
                         const float *__restrict__ rcos, const float *__restrict__ rsin,
@@ -696,7 +702,7 @@ __global__ void __launch_bounds__(2 * kThreads)
   // selection is known: one bulk copy per K/V half of that region, issued
   // before anything else so the scoring reads shared memory.
   const int stage_cap = ProtoStage<T>::kRowsPerHalf * 2;
-  const bool stage_protos = use_f && one_tile && cand_idx == nullptr && kk <= 32 && rule != SD_RULE_REFERENCE;
+  const bool stage_protos = !kCands && use_f && one_tile && kk <= 32 && rule != SD_RULE_REFERENCE;
   const int nstage = stage_protos ? (curr < stage_cap ? curr : stage_cap) : 0;
   // warp 0 keeps the precomputed candidates of its lanes (rank = lane) for
   // the merge in phase 2
@@ -863,7 +869,7 @@ __global__ void __launch_bounds__(2 * kThreads)
   // -- 2. selection over this layer's prototypes (sum / bs)
   if (use_f) {
     const int n_scored = rule == SD_RULE_REFERENCE ? 1 : nb;
-    if (cand_idx != nullptr) {
+    if constexpr (kCands) {
       // precomputed top-k (rank order) over every block but the current one,
       // whose sum changed above.  The current block is attended anyway, so
       // scoring it can only push the k-th candidate out of the top-k: one
@@ -902,7 +908,7 @@ __global__ void __launch_bounds__(2 * kThreads)
         if (__any_sync(0xffffffffu, displaced) && lane == 0 && disp_t >= 0) S.tile_n[disp_t] = 0;
       }
       attn_sync();
-    } else if (kk <= 32) {
+    } else if (kk <= 32) {  // in-kernel selection (no candidates passed)
       __shared__ float asv[kWarps * 32];
       __shared__ int asi[kWarps * 32];
       const float4 fq = reinterpret_cast<const float4 *>(X.f)[threadIdx.x & 15];
@@ -1080,7 +1086,7 @@ int launch_decode_layer(const void *qkv, int64_t qkv_sb, const void *fc, int64_t
   CUtensorMap mk, mv;
   const int r = make_maps<T>(&mk, &mv, kc, vc, B, Hkv, Tcap, kD, Tcap * kD, Hkv * Tcap * kD);
   if (r != SD_OK) return r;
-  auto kern = decode_layer_kernel<T, F, G>;
+  auto kern = cand_idx != nullptr ? decode_layer_kernel<T, F, G, true> : decode_layer_kernel<T, F, G, false>;
   if (set_max_smem(kern, smem) != SD_OK) return SD_ERR_CUDA;
   // the next layer's candidates come from a second group of kThreads threads
   const unsigned threads = nx.proto != nullptr ? 2 * kThreads : kThreads;
