@@ -625,6 +625,21 @@ __global__ void __launch_bounds__(2 * kThreads)
   rule &= ~SD_SELECT_BEFORE_APPEND;
   const int b = blockIdx.x / Hkv, h = blockIdx.x - (blockIdx.x / Hkv) * Hkv;
   const int Hq = Hkv * G;
+  const int64_t bh = static_cast<int64_t>(b) * Hkv + h;
+  // warp 0 requests the precomputed candidates (rank = lane) together with
+  // the length, so both loads are in flight at once; phase 0 keeps the ones
+  // the step uses.  The tile maps' descriptors are fetched meanwhile.
+  int cj = -1, cslot = 0;
+  float cv = -INFINITY;
+  if (kCands && threadIdx.x < 32 && static_cast<int>(threadIdx.x) < top_k) {
+    cj = cand_idx[bh * top_k + threadIdx.x];
+    cv = cand_val[bh * top_k + threadIdx.x];
+    if (slots) cslot = sm.cand_slot[bh * top_k + threadIdx.x];
+  }
+  if (threadIdx.x == 32 && is16<T>()) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmk)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmv)) : "memory");
+  }
   const int64_t pos = *cur_len;
   if (pos < 0 || pos >= (slots ? sm.host_tcap : Tcap)) {  // cache full (or corrupt length): write nothing
     report(err, SD_KERR_BOUNDS);
@@ -635,7 +650,6 @@ __global__ void __launch_bounds__(2 * kThreads)
   const int nb = curr + 1;
   const int ms = nb < top_k + 2 ? nb : top_k + 2;
   const int kk = top_k < nb ? top_k : nb;
-  const int64_t bh = static_cast<int64_t>(b) * Hkv + h;
 
   // -- next-layer scoring warps (present only when nx.proto != nullptr): the
   //    next layer's candidates for its coming step, top-k over its blocks
@@ -706,8 +720,6 @@ __global__ void __launch_bounds__(2 * kThreads)
   const int nstage = stage_protos ? (curr < stage_cap ? curr : stage_cap) : 0;
   // warp 0 keeps the precomputed candidates of its lanes (rank = lane) for
   // the merge in phase 2
-  int cj = -1;
-  float cv = -INFINITY;
   if (threadIdx.x < 32) {
     const int lane = threadIdx.x;
     if (lane < kStages) mbar_init(&S.full[lane], 1);
@@ -757,11 +769,11 @@ __global__ void __launch_bounds__(2 * kThreads)
       if (early_cands) {
         // candidates are distinct blocks other than the current one; the sink
         // is already staged, so it is skipped when it is a candidate
-        if (lane < kk) {
-          cj = cand_idx[bh * top_k + lane];
-          cv = cand_val[bh * top_k + lane];
+        if (lane >= kk) {  // loaded at entry for every rank < top_k
+          cj = -1;
+          cv = -INFINITY;
         }
-        const int cs = slots && lane < kk ? sm.cand_slot[bh * top_k + lane] : 0;
+        const int cs = slots && lane < kk ? cslot : 0;
         const bool keep = cj > 0 && cj < nb && cj != curr && cs >= 0 && (!slots || cs < sm.kslots);
         const unsigned bal = __ballot_sync(0xffffffffu, keep);
         const int slot = nt + __popc(bal & ((1u << lane) - 1u));
