@@ -283,6 +283,13 @@ SD_API int sd_rope_qk(const void *q, const void *k, int dtype, int64_t B, int64_
                       const float *rope_cos, const float *rope_sin, int64_t max_pos, int64_t offset, void *q_out,
                       void *k_out, void *stream);
 
+/* Greedy next token: out[r * o_stride] = the index of the largest of the n
+ * values of row r (row stride ld), the first on ties, NaN above every number
+ * -- torch.argmax(logits[:, -1, :], dim=-1) of the reference's greedy decode
+ * (model/model.py:185, evaluation/latency.py:156).  int64 indices. */
+SD_API int sd_argmax_rows(const void *x, int dtype, int64_t rows, int64_t n, int64_t ld, int64_t *out,
+                          int64_t o_stride, void *stream);
+
 /* SwiGLU gate of model/transformer.py:30-31 on a fused [gate | up] projection:
  * gu rows hold 2F values (row stride g_rs); out[r, c] = silu(gate) * up, each
  * op rounded to the activation dtype as the reference's separate ops are. */

@@ -62,6 +62,7 @@ _SIGS = {
                              _c_void_p, _i64, _i64, _i64, _c_void_p],
     "sd_rmsnorm": [_c_void_p, _i32, _i64, _i64, _i64, _c_void_p, _f32, _c_void_p, _i64, _c_void_p],
     "sd_silu_mul": [_c_void_p, _i32, _i64, _i64, _i64, _c_void_p, _i64, _c_void_p],
+    "sd_argmax_rows": [_c_void_p, _i32, _i64, _i64, _i64, _c_void_p, _i64, _c_void_p],
     "sd_rope_qk": [_c_void_p, _c_void_p, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                    _c_void_p, _c_void_p, _i64, _i64, _c_void_p, _c_void_p, _c_void_p],
     "sd_offload_prefetch": [_c_void_p, _c_void_p, _i32, _i64, _i64, _i64, _i64, _c_void_p, _c_void_p, _i32,

@@ -154,6 +154,81 @@ __global__ void silu_mul_vec_kernel(const T *__restrict__ gu, int64_t g_rs, int 
   }
 }
 
+// Greedy next token: per row, the index of the largest value, the first one
+// on ties, NaN above every number (torch.argmax's order).  One CTA of 512
+// threads per row: 16-byte loads where the row allows them, a warp shuffle
+// reduction, then one across the warps.
+__device__ __forceinline__ bool argmax_better(float a, int ia, float b, int ib) {
+  const bool na = a != a, nb = b != b;
+  if (na != nb) return na;
+  if (na) return ia < ib;
+  return a > b || (a == b && ia < ib);
+}
+
+template <typename T, bool kVec>
+__global__ void __launch_bounds__(512) argmax_rows_kernel(const T *__restrict__ x, int64_t n, int64_t ld,
+                                                          int64_t *__restrict__ out, int64_t o_stride) {
+  pdl_wait();
+  const T *row = x + static_cast<int64_t>(blockIdx.x) * ld;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  if (kVec) {
+    for (int64_t c = 8 * static_cast<int64_t>(threadIdx.x); c < n; c += 8 * blockDim.x) {
+      const uint4 u = *reinterpret_cast<const uint4 *>(row + c);
+      const T *e = reinterpret_cast<const T *>(&u);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float v = to_f(e[i]);
+        const int j = static_cast<int>(c) + i;
+        if (argmax_better(v, j, bv, bi)) {
+          bv = v;
+          bi = j;
+        }
+      }
+    }
+  } else {
+    for (int64_t c = threadIdx.x; c < n; c += blockDim.x) {
+      const float v = to_f(row[c]);
+      if (argmax_better(v, static_cast<int>(c), bv, bi)) {
+        bv = v;
+        bi = static_cast<int>(c);
+      }
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+    if (argmax_better(ov, oi, bv, bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  __shared__ float wv[16];
+  __shared__ int wi[16];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    wv[warp] = bv;
+    wi[warp] = bi;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = static_cast<int>(blockDim.x >> 5);
+    bv = lane < nw ? wv[lane] : -INFINITY;
+    bi = lane < nw ? wi[lane] : 0x7fffffff;
+#pragma unroll
+    for (int off = 8; off > 0; off >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+      if (argmax_better(ov, oi, bv, bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if (lane == 0) out[static_cast<int64_t>(blockIdx.x) * o_stride] = bi;
+  }
+}
+
 // RoPE of q [B,T,Hq,D] and k [B,T,Hkv,D] (rows addressed through strides)
 // into contiguous outputs, one CTA per token (b, t): thread i takes 8
 // consecutive elements of the first half of one head and the 8 they pair
@@ -277,5 +352,22 @@ extern "C" int sd_silu_mul(const void *gu, int dtype, int64_t rows, int64_t F, i
                     return sd::launch(sd::silu_mul_kernel<E>, dim3(gx, static_cast<unsigned>(rows)), dim3(256), 0, s,
                                       sd::pdl_enabled(), static_cast<const E *>(gu), g_rs, (int)F,
                                       static_cast<E *>(out), o_rs));
+  return SD_OK;
+}
+
+extern "C" int sd_argmax_rows(const void *x, int dtype, int64_t rows, int64_t n, int64_t ld, int64_t *out,
+                              int64_t o_stride, void *stream) {
+  if (!x || !out || rows <= 0 || n <= 0 || ld < n) return SD_ERR_INVALID;
+  if (rows > 0x7fffffff || n > 0x7fffffff) return SD_ERR_UNSUPPORTED;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool vec = dtype != SD_DTYPE_F32 && n % 8 == 0 && ld % 8 == 0 && sd::aligned16(x);
+  const dim3 grid(static_cast<unsigned>(rows));
+  SD_DISPATCH_DTYPE(dtype, E, {
+    if (vec)
+      return sd::launch(sd::argmax_rows_kernel<E, true>, grid, dim3(512), 0, s, sd::pdl_enabled(),
+                        static_cast<const E *>(x), n, ld, out, o_stride);
+    return sd::launch(sd::argmax_rows_kernel<E, false>, grid, dim3(512), 0, s, sd::pdl_enabled(),
+                      static_cast<const E *>(x), n, ld, out, o_stride);
+  });
   return SD_OK;
 }

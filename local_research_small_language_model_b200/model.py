@@ -405,7 +405,7 @@ class DecodeEngine:
 
     def _body(self):
         out = self.model(self.ids, kv_caches=self.caches)
-        self.next_ids.copy_(out["logits"][:, -1:, :].argmax(dim=-1))
+        ops.argmax_rows(out["logits"][:, -1, :], out=self.next_ids)
         self.ids.copy_(self.next_ids)
 
     def _snapshot(self):

@@ -454,6 +454,23 @@ def silu_mul(gu: torch.Tensor) -> torch.Tensor:
     return out
 
 
+def argmax_rows(x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """torch.argmax(x, dim=-1) for 2-D x (rows with unit column stride): the
+    first index of each row's maximum, NaN above every number.  Writes int64
+    indices into ``out`` (any shape with one element per row) or a new [rows]
+    tensor."""
+    _cuda(x)
+    x = _inner1(x)
+    rows, n = x.shape
+    if out is None:
+        out = torch.empty(rows, dtype=torch.int64, device=x.device)
+    if out.dtype != torch.int64 or out.numel() != rows:
+        raise ValueError("out must hold one int64 per row")
+    o_stride = out.stride(0) if out.dim() >= 1 else 1
+    L.call("sd_argmax_rows", x.data_ptr(), dtype_code(x), rows, n, x.stride(0), out.data_ptr(), o_stride, _stream(x))
+    return out
+
+
 def advance_len(lens: torch.Tensor, delta: int = 1) -> None:
     _cuda(lens)
     L.call("sd_advance_len", lens.data_ptr(), lens.numel(), delta, _stream(lens))

@@ -418,3 +418,23 @@ def test_rope_qk_bit_exact_vs_reference_formula(dev, dt, offset, tt):
     q1, k1 = ops.rope_qk(xq, xk, cos, sin, offset)
     q2, k2 = apply_rotary_emb(xq, xk, cos, sin, offset=offset)
     assert torch.equal(q1, q2) and torch.equal(k1, k2)
+
+
+@pytest.mark.parametrize("dt,rows,n", [(torch.bfloat16, 64, 32000), (torch.float16, 3, 1000), (torch.float32, 5, 777),
+                                       (torch.bfloat16, 7, 1001)])
+def test_argmax_rows_matches_torch(dev, dt, rows, n):
+    """Greedy next token (model/model.py:185): the first index of each row's
+    maximum, NaN above every number, as torch.argmax; ties planted on purpose
+    (16-byte path for 16-bit rows with n % 8 == 0, the scalar path otherwise)."""
+    g = torch.Generator(device=dev).manual_seed(rows + n)
+    x = torch.randn(rows, n, generator=g, device=dev).to(dt)
+    x[0, n // 3] = x[0, n - 1] = x[0].max() + 1  # tie: the first wins
+    if rows > 2:
+        x[2, 5] = float("nan")
+        x[2, n - 2] = float("nan")
+    got = ops.argmax_rows(x)
+    ref = torch.argmax(x, dim=-1)
+    assert torch.equal(got, ref)
+    out = torch.full((rows, 1), -7, dtype=torch.int64, device=dev)
+    ops.argmax_rows(x, out=out)
+    assert torch.equal(out[:, 0], ref)
