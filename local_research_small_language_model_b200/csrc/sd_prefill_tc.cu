@@ -279,6 +279,17 @@ __global__ void __launch_bounds__(tc::kThreads, 2)
     const int j = block_of(i);
     ok = mbar_wait_bounded(&s_bar[x], i & 1) && ok;
     fence_after_sync();
+    // S(i) complete implies this tile's PV(i - 1) complete (its leader issued
+    // PV(i - 1) before S(i), and a commit tracks every earlier MMA of the
+    // thread): both tiles done with stage (i - 1) % kStages, the second to
+    // get here refills it, a softmax earlier than waiting for PV(i - 1)
+    if (i > 0) {
+      const int ps = (i - 1) % kStages;
+      if (leader && atomicAdd(&refill[ps], 1) == 1) {
+        refill[ps] = 0;
+        if (i - 1 + kStages < cnt) issue(i - 1 + kStages);
+      }
+    }
     float sc[64];
     float mn = m, alpha = 1.f;
     if (warp_active) {
@@ -313,9 +324,14 @@ __global__ void __launch_bounds__(tc::kThreads, 2)
 #pragma unroll
         for (int c = 0; c < 64; ++c) sc[c] = c < nv ? sc[c] : -INFINITY;
       }
-      float mt = sc[0];
+      // maximum over 8 interleaved partial maxima (a short dependency chain)
+      float m8[8];
 #pragma unroll
-      for (int c = 1; c < 64; ++c) mt = fmaxf(mt, sc[c]);
+      for (int e = 0; e < 8; ++e) m8[e] = sc[e];
+#pragma unroll
+      for (int c = 8; c < 64; ++c) m8[c & 7] = fmaxf(m8[c & 7], sc[c]);
+      const float mt = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                             fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
       const float mts = mt * scale_log2;  // scale_log2 > 0: max of the scaled scores
       if (mts > m + kRescaleLog2 || (m == -INFINITY && mts > -INFINITY)) {
         mn = mts;
@@ -326,13 +342,6 @@ __global__ void __launch_bounds__(tc::kThreads, 2)
     if (i > 0) {
       ok = mbar_wait_bounded(&o_bar[x], (i - 1) & 1) && ok;
       fence_after_sync();
-      // both tiles' MMAs that read stage (i - 1) % kStages are complete: the
-      // second tile to get here refills it
-      const int ps = (i - 1) % kStages;
-      if (leader && atomicAdd(&refill[ps], 1) == 1) {
-        refill[ps] = 0;
-        if (i - 1 + kStages < cnt) issue(i - 1 + kStages);
-      }
     }
     if (warp_active) {
       if (i > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
@@ -350,7 +359,7 @@ __global__ void __launch_bounds__(tc::kThreads, 2)
         tmem_wait_st();
       }
       const float nmn = mn == -INFINITY ? 0.f : -mn;  // rows with nothing visible yet keep p = 0
-      float ps = 0.f;
+      float ps8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // 8 partial row sums
       char *prow = sm + Smem::kP + x * kTileBytes;
 #pragma unroll
       for (int c8 = 0; c8 < 8; ++c8) {
@@ -358,7 +367,7 @@ __global__ void __launch_bounds__(tc::kThreads, 2)
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
           p[u] = ex2(fmaf(sc[8 * c8 + u], scale_log2, nmn));
-          ps += p[u];
+          ps8[u] += p[u];
         }
         uint4 w;
         w.x = pack2<T>(p[0], p[1]);
@@ -367,6 +376,7 @@ __global__ void __launch_bounds__(tc::kThreads, 2)
         w.w = pack2<T>(p[6], p[7]);
         *reinterpret_cast<uint4 *>(prow + sw128(r, c8)) = w;
       }
+      const float ps = ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) + ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
       l = l * alpha + ps;
       m = mn;
     }
