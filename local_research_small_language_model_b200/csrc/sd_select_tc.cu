@@ -11,22 +11,24 @@
 // product of two bf16 values is exact in fp32, so the result differs from an
 // fp32 CUDA-core dot product only by accumulation rounding.
 //
-// One CTA per (128 query rows, kv head, sequence), 256 threads:
-//   * the forecast tile [128 rows x 64] arrives by TMA (128-byte swizzle);
+// One CTA per (256 query rows, kv head, sequence), 256 threads:
+//   * the forecast tile [256 rows x 64] arrives by TMA (128-byte swizzle);
 //   * per chunk of 128 prototypes (blocks the tile's last row cannot see are
 //     never loaded): the threads split the fp32 prototypes into the three bf16
 //     planes, written in the same swizzled K-major layout;
-//   * one thread issues 3 planes x 4 K-steps of tcgen05.mma kind::f16 (M=128
-//     rows, N=128 blocks, K=16) into a 128-column fp32 accumulator in TMEM;
-//   * thread t reads 64 scores of its row (TMEM lane t % 128, columns
-//     64 * (t / 128) ..) with the causal mask applied, forms ordered 64-bit
+//   * one thread issues, for each of the two 128-row halves, 3 planes x 4
+//     K-steps of tcgen05.mma kind::f16 (M=128 rows, N=128 blocks, K=16) into
+//     two 128-column fp32 accumulators in TMEM (the split planes serve 256
+//     rows);
+//   * thread t reads the 128 scores of row t (TMEM lane t % 128, columns
+//     128 * (t / 128) ..) with the causal mask applied, forms ordered 64-bit
 //     keys (order-preserving score bits above the complemented block index)
-//     and keeps a top-8 of its half row in registers; a batch's keys are
-//     staged in shared memory and the warp inserts the candidates that beat
-//     the list's 8th entry in rounds, one per lane per round;
-//   * the two half-row lists are merged, blocks past the row's last visible
-//     one follow as -inf entries in index order (the reference's topk over
-//     -inf scores), and the k best indices are written.
+//     and keeps the row's top-8 in registers; a batch's keys are staged in
+//     shared memory and the warp inserts the candidates that beat the list's
+//     8th entry in rounds, one per lane per round;
+//   * blocks past the row's last visible one follow as -inf entries in index
+//     order (the reference's topk over -inf scores), and the k best indices
+//     are written.
 // The order is (value desc, index asc) everywhere; NaN scores are never
 // chosen.  Every mbarrier wait is bounded.
 #include "sd_select_core.cuh"
@@ -36,13 +38,13 @@ namespace sd {
 namespace seltc {
 
 constexpr int kThreads = 256;
-constexpr int kRows = 128;    // forecast rows per CTA (MMA M)
+constexpr int kRows = 256;    // forecast rows per CTA (two MMA M tiles of 128)
 constexpr int kBlk = 128;     // prototypes per chunk (MMA N)
 constexpr int kABytes = kRows * 128;
 constexpr int kPlaneBytes = kBlk * 128;
-constexpr int kTmemCols = 128;
+constexpr int kTmemCols = 256;
 
-// Shared memory: A [128][64] bf16 | hi | mid | lo planes [128][64] bf16 (once
+// Shared memory: A [256][64] bf16 | hi | mid | lo planes [128][64] bf16 (once
 // a chunk's MMAs are done, the planes hold the threads' staged keys) |
 // barriers.  1024-aligned tiles.
 constexpr int kPlaneOff = kABytes;
@@ -158,12 +160,12 @@ __global__ void __launch_bounds__(kThreads, 2)
     jmax = t < 0 ? 0 : (t / bs + 1 < NB ? t / bs + 1 : NB);
   }
   // this thread's row and its last visible block (inclusive; -1: none)
-  const int lr = tid & (kRows - 1), half = tid >> 7;
+  const int lr = tid, half = tid >> 7;  // row; its 128-row MMA tile
   const int64_t t_abs = row0 + lr + q_offset;
   int64_t jvis = NB - 1;
   if (causal) jvis = t_abs < 0 ? -1 : (t_abs / bs < NB - 1 ? t_abs / bs : NB - 1);
 
-  // this thread's running top-8 of its half row, as ordered keys (0: empty)
+  // this thread's running top-8 of its row, as ordered keys (0: empty)
   uint64_t key[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) key[i] = 0;
@@ -217,14 +219,17 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (warp == 0) {
       if (c == 0) ok = mbar_wait_bounded(abar, 0) && ok;
       if (tid == 0) {
-        const uint32_t a = smem_u32(sm);
-        int step = 0;
 #pragma unroll
-        for (int p = 0; p < 3; ++p) {
-          const uint32_t bp = smem_u32(sm + kPlaneOff + p * kPlaneBytes);
+        for (int m = 0; m < 2; ++m) {
+          const uint32_t a = smem_u32(sm + m * (kABytes / 2));
+          int step = 0;
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk, ++step)
-            mma(tmem, desc_sw128(a + 32 * kk), desc_sw128(bp + 32 * kk), step > 0);
+          for (int p = 0; p < 3; ++p) {
+            const uint32_t bp = smem_u32(sm + kPlaneOff + p * kPlaneBytes);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk, ++step)
+              mma(tmem + 128 * m, desc_sw128(a + 32 * kk), desc_sw128(bp + 32 * kk), step > 0);
+          }
         }
         commit(dbar);
       }
@@ -232,17 +237,17 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     ok = mbar_wait_bounded(dbar, c & 1) && ok;
     fence_after();
-    // ---- this thread's 64 scores of its row (TMEM lane t % 128, columns
-    // 64 * (t / 128) ..) in batches of 16: the batch's keys go to shared
+    // ---- this thread's 128 scores of its row (TMEM lane t % 128, columns
+    // 128 * (t / 128) ..) in batches of 16: the batch's keys go to shared
     // memory, the ones above the list's 8th entry are candidates, and the
     // warp loops until every lane has inserted its candidates (one per lane
     // per round, branch-free), so a rare insertion costs one round, not one
     // per value
-    const int64_t jc = j0 + 64 * half;  // first block of the half
+    const int64_t jc = j0;  // first block of the chunk
     if (__any_sync(0xffffffffu, jc <= jvis)) {  // warp-uniform: tcgen05.ld is a warp-wide instruction
-      const uint32_t taddr = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16) + 64 * half;
+      const uint32_t taddr = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16) + 128 * half;
 #pragma unroll 1
-      for (int g = 0; g < 64; g += 16) {
+      for (int g = 0; g < 128; g += 16) {
         float v[16];
         tmem_ld16(taddr + g, v);
         const uint64_t thr = key[7];
@@ -273,27 +278,15 @@ __global__ void __launch_bounds__(kThreads, 2)
   if (warp == 0 && c == 0) ok = mbar_wait_bounded(abar, 0) && ok;
   if (!ok && err && tid == 0) atomicExch(err, SD_KERR_TIMEOUT);
 
-  // ---- merge the half-row lists (the upper half hands its keys over), let
-  // blocks past the row's last visible one follow as -inf entries, lowest
-  // index first, wherever the list has room, and write the k best indices
-  uint64_t *kx = reinterpret_cast<uint64_t *>(sm + kPlaneOff);  // [8][128]
-  if (half == 1) {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) kx[i * kRows + lr] = key[i];
-  }
-  __syncthreads();
-  if (half == 0) {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) insert_key(key, kx[i * kRows + lr]);
+  // ---- blocks past the row's last visible one follow as -inf entries,
+  // lowest index first, wherever the list has room; the k best are written
 #pragma unroll 1
-    for (int64_t jf = jvis + 1; jf < jvis + 9 && jf < NB; ++jf)
-      insert_key(key, order_key(-INFINITY, static_cast<int>(jf)));
-    if (row0 + lr < Tq) {
-      int64_t *dst = idx_out + ((static_cast<int64_t>(b) * H + h) * Tq + row0 + lr) * k;
+  for (int64_t jf = jvis + 1; jf < jvis + 9 && jf < NB; ++jf) insert_key(key, order_key(-INFINITY, static_cast<int>(jf)));
+  if (row0 + lr < Tq) {
+    int64_t *dst = idx_out + ((static_cast<int64_t>(b) * H + h) * Tq + row0 + lr) * k;
 #pragma unroll
-      for (int i = 0; i < 8; ++i)  // constant indices keep the list in registers
-        if (i < k) dst[i] = key[i] == 0 ? -1 : static_cast<int64_t>(0xffffffffu - static_cast<uint32_t>(key[i]));
-    }
+    for (int i = 0; i < 8; ++i)  // constant indices keep the list in registers
+      if (i < k) dst[i] = key[i] == 0 ? -1 : static_cast<int64_t>(0xffffffffu - static_cast<uint32_t>(key[i]));
   }
   fence_before();
   __syncthreads();

@@ -37,13 +37,13 @@ def _check_vs_oracle(f, r, k, causal, q_offset, idx):
 
 
 @pytest.mark.parametrize("tq,nb,k,causal,q_offset", [
-    (128, 2, 8, True, 0),        # fewer visible blocks than k: -inf fills
+    (256, 2, 8, True, 0),        # fewer visible blocks than k: -inf fills
     (300, 5, 5, True, 0),        # ragged last tile
     (4096, 64, 8, True, 0),
     (4096, 64, 8, False, 0),
     (1000, 80, 3, True, 4096),   # chunked prefill: rows start past the cache
     (2048, 200, 8, False, 0),    # several 128-block chunks
-    (130, 300, 1, True, 16000),
+    (260, 300, 1, True, 16000),
 ])
 @torch.no_grad()
 def test_tensor_core_selector_vs_oracle(dev, tq, nb, k, causal, q_offset):
