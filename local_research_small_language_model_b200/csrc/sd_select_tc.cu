@@ -21,11 +21,13 @@
 //     two 128-column fp32 accumulators in TMEM (the split planes serve 256
 //     rows);
 //   * thread t reads the 128 scores of row t (TMEM lane t % 128, columns
-//     128 * (t / 128) ..) with the causal mask applied, forms ordered 64-bit
-//     keys (order-preserving score bits above the complemented block index)
-//     and keeps the row's top-8 in registers; a batch's keys are staged in
-//     shared memory and the warp inserts the candidates that beat the list's
-//     8th entry in rounds, one per lane per round;
+//     128 * (t / 128) ..) up to the warp's last visible block, with the causal
+//     mask applied, maps them to ordered 32-bit keys (order-preserving score
+//     bits) and keeps the row's top-8 (key, block) pairs in registers; a
+//     batch's keys are staged in shared memory and the warp inserts the
+//     candidates that beat the list's 8th key in rounds, one per lane per
+//     round, in ascending block order, so a strict comparison leaves equal
+//     scores in ascending index order;
 //   * blocks past the row's last visible one follow as -inf entries in index
 //     order (the reference's topk over -inf scores), and the k best indices
 //     are written.
@@ -50,7 +52,7 @@ constexpr int kTmemCols = 256;
 constexpr int kPlaneOff = kABytes;
 constexpr int kBarOff = kPlaneOff + 3 * kPlaneBytes;
 constexpr int kSmemBytes = kBarOff + 64;
-static_assert(16 * kThreads * 8 <= 3 * kPlaneBytes, "the staged keys fit over the planes");
+static_assert(16 * kThreads * 4 <= 3 * kPlaneBytes, "the staged keys fit over the planes");
 
 __device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) {
   // K-major, 128-byte swizzle: LBO 16 bytes, SBO 1024 bytes (8 rows of 128 B),
@@ -93,25 +95,28 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// Ordered 64-bit key of (score, block): larger key = better under (value
-// desc, index asc): the score's bits mapped to an order-preserving unsigned
-// integer above, the complement of the block index below.  0 is below every
-// key (an empty slot).  NaN is never keyed.
-__device__ __forceinline__ uint64_t order_key(float v, int j) {
+// Ordered 32-bit key of a score: larger key = larger score (the float's bits
+// mapped to an order-preserving unsigned integer).  0 is below every non-NaN
+// score's key (an empty slot); NaN is never keyed.
+__device__ __forceinline__ uint32_t order_key(float v) {
   const uint32_t u = __float_as_uint(v);
-  const uint32_t o = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-  return (static_cast<uint64_t>(o) << 32) | (0xffffffffu - static_cast<uint32_t>(j));
+  return u ^ (static_cast<uint32_t>(static_cast<int32_t>(u) >> 31) | 0x80000000u);
 }
+constexpr uint32_t kKeyNegInf = 0x007fffffu;  // order_key(-inf)
 
-// Sorted insertion into an 8-entry list of keys, best first; x = 0 (or any
-// key not above key[7]) leaves the list unchanged.  Branch-free.
-__device__ __forceinline__ void insert_key(uint64_t (&key)[8], uint64_t x) {
+// Sorted insertion of (x, xi) into an 8-entry list, best first; x = 0 (or
+// any key not above kv[7]) leaves the list unchanged.  A key equal to an
+// entry goes after it.  Branch-free.
+__device__ __forceinline__ void insert_key(uint32_t (&kv)[8], int (&ki)[8], uint32_t x, int xi) {
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    const bool b = x > key[i];
-    const uint64_t t = b ? key[i] : x;
-    key[i] = b ? x : key[i];
-    x = t;
+    const bool b = x > kv[i];
+    const uint32_t tv = b ? kv[i] : x;
+    const int ti = b ? ki[i] : xi;
+    kv[i] = b ? x : kv[i];
+    ki[i] = b ? xi : ki[i];
+    x = tv;
+    xi = ti;
   }
 }
 
@@ -165,13 +170,20 @@ __global__ void __launch_bounds__(kThreads, 2)
   int64_t jvis = NB - 1;
   if (causal) jvis = t_abs < 0 ? -1 : (t_abs / bs < NB - 1 ? t_abs / bs : NB - 1);
 
-  // this thread's running top-8 of its row, as ordered keys (0: empty)
-  uint64_t key[8];
+  // the warp's last visible block: its scan stops there
+  const int wjvis = __reduce_max_sync(0xffffffffu, static_cast<int>(jvis));
+
+  // this thread's running top-8 of its row: ordered keys (0: empty), blocks
+  uint32_t kv[8];
+  int ki[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) key[i] = 0;
+  for (int i = 0; i < 8; ++i) {
+    kv[i] = 0;
+    ki[i] = -1;
+  }
   // per-thread staging of a batch's 16 keys, [16][256] over the planes
   // (free while the scores are read)
-  uint64_t *kst = reinterpret_cast<uint64_t *>(sm + kPlaneOff);
+  uint32_t *kst = reinterpret_cast<uint32_t *>(sm + kPlaneOff);
   const float *rbase = reps + b * r_sb + h * r_sh;
   bool ok = true;
   int c = 0;
@@ -237,37 +249,40 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     ok = mbar_wait_bounded(dbar, c & 1) && ok;
     fence_after();
-    // ---- this thread's 128 scores of its row (TMEM lane t % 128, columns
-    // 128 * (t / 128) ..) in batches of 16: the batch's keys go to shared
-    // memory, the ones above the list's 8th entry are candidates, and the
-    // warp loops until every lane has inserted its candidates (one per lane
-    // per round, branch-free), so a rare insertion costs one round, not one
-    // per value
-    const int64_t jc = j0;  // first block of the chunk
-    if (__any_sync(0xffffffffu, jc <= jvis)) {  // warp-uniform: tcgen05.ld is a warp-wide instruction
+    // ---- this thread's scores of its row (TMEM lane t % 128, columns
+    // 128 * (t / 128) ..) in batches of 16, up to the warp's last visible
+    // block: the batch's keys go to shared memory, the ones above the list's
+    // 8th key are candidates, and the warp loops until every lane has
+    // inserted its candidates (one per lane per round, lowest block first,
+    // branch-free), so a rare insertion costs one round, not one per value
+    const int jc = static_cast<int>(j0);  // first block of the chunk
+    if (jc <= wjvis) {  // warp-uniform: tcgen05.ld is a warp-wide instruction
       const uint32_t taddr = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16) + 128 * half;
+      const int lim0 = static_cast<int>(jvis) - jc;  // scores i <= lim0 - g of a batch are visible
 #pragma unroll 1
-      for (int g = 0; g < 128; g += 16) {
+      for (int g = 0; g < 128 && jc + g <= wjvis; g += 16) {
         float v[16];
         tmem_ld16(taddr + g, v);
-        const uint64_t thr = key[7];
+        const int lim = lim0 - g;
+        const uint32_t thr = kv[7];
         uint32_t cand = 0;
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const int64_t j = jc + g + i;
           const float sv = __fadd_rn(v[i] * scale, 0.0f);  // -0 -> +0: equal scores share one key
-          const uint64_t kk = (j <= jvis && sv == sv) ? order_key(sv, static_cast<int>(j)) : 0ull;
+          const uint32_t kk = (i <= lim && sv == sv) ? order_key(sv) : 0u;
           kst[i * kThreads + tid] = kk;
           cand |= static_cast<uint32_t>(kk > thr) << i;
         }
         while (__any_sync(0xffffffffu, cand != 0)) {
-          uint64_t x = 0;
+          uint32_t x = 0;
+          int xi = 0;
           if (cand) {
             const int i = __ffs(cand) - 1;
             cand &= cand - 1;
             x = kst[i * kThreads + tid];
+            xi = jc + g + i;
           }
-          insert_key(key, x);
+          insert_key(kv, ki, x, xi);
         }
       }
     }
@@ -281,12 +296,12 @@ __global__ void __launch_bounds__(kThreads, 2)
   // ---- blocks past the row's last visible one follow as -inf entries,
   // lowest index first, wherever the list has room; the k best are written
 #pragma unroll 1
-  for (int64_t jf = jvis + 1; jf < jvis + 9 && jf < NB; ++jf) insert_key(key, order_key(-INFINITY, static_cast<int>(jf)));
+  for (int64_t jf = jvis + 1; jf < jvis + 9 && jf < NB; ++jf) insert_key(kv, ki, kKeyNegInf, static_cast<int>(jf));
   if (row0 + lr < Tq) {
     int64_t *dst = idx_out + ((static_cast<int64_t>(b) * H + h) * Tq + row0 + lr) * k;
 #pragma unroll
     for (int i = 0; i < 8; ++i)  // constant indices keep the list in registers
-      if (i < k) dst[i] = key[i] == 0 ? -1 : static_cast<int64_t>(0xffffffffu - static_cast<uint32_t>(key[i]));
+      if (i < k) dst[i] = kv[i] == 0 ? -1 : static_cast<int64_t>(ki[i]);
   }
   fence_before();
   __syncthreads();
