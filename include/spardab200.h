@@ -265,6 +265,24 @@ SD_API int sd_prefill_attention(const void *q, int dtype, int64_t B, int64_t T, 
                                 int kk, int block_size, int causal, float scale, void *out, int64_t o_sb,
                                 int64_t o_st, int64_t o_sh, void *stream);
 
+/* Gradients of sd_prefill_attention: the backward that autograd takes through
+ * the reference's masked / chunked SDPA prefill paths
+ * (model/attention/sparse.py:185-364) when the sparse backend is trained
+ * (tests/test_sparse_attention.py:63-77, training/trainer.py).  q, k, v and the
+ * block lists / per-row top-k are the forward's (same layouts and strides);
+ * dout [B,T,Hq,D] (element strides g_sb, g_st, g_sh) is the gradient of the
+ * output, all four in `dtype`.  Writes fp32 dq [B,T,Hq,D] and dk, dv
+ * [B,Hkv,T,D], all contiguous; dk and dv are zeroed on the stream first.  The
+ * softmax is recomputed exactly in fp32 (no forward statistics needed).
+ * D == 64, block_size == 64. */
+SD_API int sd_prefill_attention_backward(const void *q, const void *k, const void *v, const void *dout,
+                                         int dtype, int64_t B, int64_t T, int64_t Hq, int64_t Hkv, int64_t D,
+                                         int64_t q_sb, int64_t q_st, int64_t q_sh, int64_t c_sb, int64_t c_sh,
+                                         int64_t c_st, int64_t g_sb, int64_t g_st, int64_t g_sh,
+                                         const int32_t *lists, const int32_t *counts, int lcap,
+                                         const int64_t *topk, int kk, int block_size, int causal, float scale,
+                                         float *dq, float *dk, float *dv, void *stream);
+
 /* RMSNorm of `rows` rows of C values (row strides x_rs, o_rs), computed as
  * model/norm.py:15-21 does: normalised in fp32, cast to the activation dtype,
  * then multiplied by the gain w [C] in that dtype. */

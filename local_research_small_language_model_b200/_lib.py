@@ -60,6 +60,10 @@ _SIGS = {
     "sd_prefill_attention": [_c_void_p, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _c_void_p, _c_void_p,
                              _i64, _i64, _i64, _c_void_p, _c_void_p, _i32, _c_void_p, _i32, _i32, _i32, _f32,
                              _c_void_p, _i64, _i64, _i64, _c_void_p],
+    "sd_prefill_attention_backward": [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i64, _i64, _i64, _i64,
+                                      _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _c_void_p,
+                                      _c_void_p, _i32, _c_void_p, _i32, _i32, _i32, _f32, _c_void_p, _c_void_p,
+                                      _c_void_p, _c_void_p],
     "sd_rmsnorm": [_c_void_p, _i32, _i64, _i64, _i64, _c_void_p, _f32, _c_void_p, _i64, _c_void_p],
     "sd_silu_mul": [_c_void_p, _i32, _i64, _i64, _i64, _c_void_p, _i64, _c_void_p],
     "sd_argmax_rows": [_c_void_p, _i32, _i64, _i64, _i64, _c_void_p, _i64, _c_void_p],

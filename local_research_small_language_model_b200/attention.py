@@ -16,6 +16,49 @@ from .forecast import ForecastBlockSelector, KVBlockCompressor
 from .rope import apply_rotary_emb
 
 
+class _RopeQK(torch.autograd.Function):
+    """RoPE of q and k (ops.rope_qk, model/rope.py:34-65) with its backward for
+    training: the rotation's transpose is the rotation by the negated angle,
+    i.e. the same kernel with -sin (sin is the same for both halves of a head,
+    so rotate_half commutes with it)."""
+
+    @staticmethod
+    def forward(ctx, xq, xk, cos, sin):
+        ctx.save_for_backward(cos, sin)
+        ctx.shapes = (xq.shape, xk.shape)
+        return ops.rope_qk(xq, xk, cos, sin, 0)
+
+    @staticmethod
+    def backward(ctx, gq, gk):
+        cos, sin = ctx.saved_tensors
+        if gq is None:
+            gq = torch.zeros(ctx.shapes[0], dtype=gk.dtype, device=gk.device)
+        if gk is None:
+            gk = torch.zeros(ctx.shapes[1], dtype=gq.dtype, device=gq.device)
+        dq, dk = ops.rope_qk(gq, gk, cos, -sin, 0)
+        return dq, dk, None, None
+
+
+class _SparseAttentionCore(torch.autograd.Function):
+    """Block-sparse prefill attention (ops.prefill_attention) with its backward
+    (ops.prefill_attention_backward, fp32) for training: the gradients autograd
+    takes through the reference's masked / chunked SDPA (sparse.py:185-364).
+    The block lists and per-row top-k are indices and carry no gradient, as in
+    the reference, where only topk's indices build the mask."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, lists, counts, topk, block_size, causal):
+        ctx.save_for_backward(q, k, v, lists, counts, topk)
+        ctx.block_size, ctx.causal = block_size, causal
+        return ops.prefill_attention(q, k, v, lists, counts, block_size, topk, causal)
+
+    @staticmethod
+    def backward(ctx, gout):
+        q, k, v, lists, counts, topk = ctx.saved_tensors
+        dq, dk, dv = ops.prefill_attention_backward(q, k, v, gout, lists, counts, ctx.block_size, topk, ctx.causal)
+        return dq.to(q.dtype), dk.to(k.dtype), dv.to(v.dtype), None, None, None, None, None
+
+
 class BaseAttention(nn.Module):
     """model/attention/base.py:35-52: owns wq, wk, wv, wo (same state-dict keys)."""
 
@@ -181,35 +224,17 @@ class B200SparseAttention(BaseAttention):
         out = self.prefill_core(xq, xk, xv, rotary_emb, kv_cache, is_causal, forecast_vector, **kwargs)
         return self.wo(out.reshape(b, t, self.n_head * self.head_dim).to(x.dtype))
 
-    def prefill_core(self, xq, xk, xv, rotary_emb, kv_cache, is_causal, forecast_vector, **kwargs):
-        """Prefill from the q/k/v projections [B,T,H,D] (any strides with an
-        innermost stride of 1, e.g. views of one packed projection): RoPE,
-        cache write, compressor, selector, block lists and block-sparse
-        attention.  Returns the attention output [B,T,Hq,D] before wo."""
-        b, t = xq.shape[0], xq.shape[1]
-        offset = kv_cache.current_len if kv_cache is not None else 0
-        if offset:
-            # the reference uses seq_len for both queries and keys here
-            # (sparse.py:413-430), so a prompt cannot extend a filled cache
-            raise NotImplementedError("prefill into a non-empty cache")
-        rotary_emb.ensure(t)
-        xq, xk = ops.rope_qk(xq, xk, rotary_emb.cos, rotary_emb.sin, 0)
-        if isinstance(kv_cache, B200OffloadKVCache):
-            kv_cache.update(xk, xv)  # host store + block sums + slots; attend over the prompt itself
-            kh, vh = xk.transpose(1, 2), xv.transpose(1, 2)
-        elif kv_cache is not None:
-            k_all, v_all = kv_cache.update(xk, xv)
-            if isinstance(kv_cache, B200KVCache):
-                kh, vh = kv_cache.k_store[:, :, :t], kv_cache.v_store[:, :, :t]
-            else:
-                kh, vh = k_all.transpose(1, 2), v_all.transpose(1, 2)
-        else:
-            kh, vh = xk.transpose(1, 2), xv.transpose(1, 2)
+    def block_lists(self, xk: torch.Tensor, f: Optional[torch.Tensor], is_causal: bool, chunked: bool):
+        """The prefill's key-block lists (sparse.py:185-364): compressor +
+        selector on the RoPE'd keys xk [B,T,Hkv,D] and forecast f (or None),
+        then the per-q-block lists of the masked path (dense, forecast or
+        static window) or of the chunked path.  Returns (lists, counts,
+        per-row top-k or None, causal) for ops.prefill_attention."""
+        b, t = xk.shape[0], xk.shape[1]
         bs, kk = self.block_size, self.top_k_blocks
         nb = ops.num_blocks(t, bs)
-        f = forecast_vector if (self.mode == "forecast" and forecast_vector is not None) else None
         topk = None
-        if kwargs.get("use_chunked_gather", t > 8192):
+        if chunked:
             causal = True  # the chunked path always clears future blocks (sparse.py:330-346)
             if f is not None:
                 _, topk = ops.select_blocks(f, self.compressor(xk), kk, bs, False, return_scores=False)
@@ -227,5 +252,47 @@ class B200SparseAttention(BaseAttention):
             else:
                 mode = "masked_static"
             row_topk = topk
-        lists, counts = ops.prefill_lists(mode, b, self.n_kv_head, t, bs, kk, topk, causal, device=xq.device)
-        return ops.prefill_attention(xq, kh, vh, lists, counts, bs, row_topk, causal)
+        lists, counts = ops.prefill_lists(mode, b, self.n_kv_head, t, bs, kk, topk, causal, device=xk.device)
+        return lists, counts, row_topk, causal
+
+    def prefill_core(self, xq, xk, xv, rotary_emb, kv_cache, is_causal, forecast_vector, **kwargs):
+        """Prefill from the q/k/v projections [B,T,H,D] (any strides with an
+        innermost stride of 1, e.g. views of one packed projection): RoPE,
+        cache write, compressor, selector, block lists and block-sparse
+        attention.  Returns the attention output [B,T,Hq,D] before wo.
+
+        While autograd records and q, k or v needs a gradient, RoPE and the
+        attention core run as autograd functions with CUDA backward kernels
+        (training without a cache, as the reference's trainer does)."""
+        b, t = xq.shape[0], xq.shape[1]
+        grad = torch.is_grad_enabled() and (xq.requires_grad or xk.requires_grad or xv.requires_grad)
+        if grad and kv_cache is not None:
+            raise NotImplementedError("gradients through a KV cache are not supported: train without a cache")
+        offset = kv_cache.current_len if kv_cache is not None else 0
+        if offset:
+            # the reference uses seq_len for both queries and keys here
+            # (sparse.py:413-430), so a prompt cannot extend a filled cache
+            raise NotImplementedError("prefill into a non-empty cache")
+        rotary_emb.ensure(t)
+        if grad:
+            xq, xk = _RopeQK.apply(xq, xk, rotary_emb.cos, rotary_emb.sin)
+        else:
+            xq, xk = ops.rope_qk(xq, xk, rotary_emb.cos, rotary_emb.sin, 0)
+        if isinstance(kv_cache, B200OffloadKVCache):
+            kv_cache.update(xk, xv)  # host store + block sums + slots; attend over the prompt itself
+            kh, vh = xk.transpose(1, 2), xv.transpose(1, 2)
+        elif kv_cache is not None:
+            k_all, v_all = kv_cache.update(xk, xv)
+            if isinstance(kv_cache, B200KVCache):
+                kh, vh = kv_cache.k_store[:, :, :t], kv_cache.v_store[:, :, :t]
+            else:
+                kh, vh = k_all.transpose(1, 2), v_all.transpose(1, 2)
+        else:
+            kh, vh = xk.transpose(1, 2), xv.transpose(1, 2)
+        f = forecast_vector if (self.mode == "forecast" and forecast_vector is not None) else None
+        lists, counts, row_topk, causal = self.block_lists(
+            xk.detach(), f.detach() if f is not None else None, is_causal,
+            kwargs.get("use_chunked_gather", t > 8192))
+        if grad:
+            return _SparseAttentionCore.apply(xq, kh, vh, lists, counts, row_topk, self.block_size, causal)
+        return ops.prefill_attention(xq, kh, vh, lists, counts, self.block_size, row_topk, causal)

@@ -1,0 +1,303 @@
+// Backward pass of the block-sparse GQA prefill attention: the gradients that
+// autograd takes through the reference's masked and chunked SDPA paths
+// (model/attention/sparse.py:185-364) when a model is trained with the sparse
+// backend (tests/test_sparse_attention.py:63-77, training/trainer.py).
+//
+// Inputs are the forward's q, k, v, the upstream gradient dO and the same
+// block lists (and per-row top-k for the masked forecast mode) as
+// sd_prefill_attention, so the allowed (query, key) pairs are exactly the
+// forward's.  With P the softmax of scale * q k^T over the allowed keys:
+//   dV = P^T dO      dP = dO V^T      Delta = rowsum(P * dP)
+//   dS = P * (dP - Delta)      dQ = scale * dS K      dK = scale * dS^T Q
+// all in fp32.  One CTA per (64-token query block, query head, sequence),
+// 256 threads.  Pass 1 walks the block list for each row's softmax statistics
+// (running maximum, sum of exponentials and sum of exp * dP, so Delta needs no
+// forward output); pass 2 walks it again for the gradients.  Every product is
+// a 64 x 64 x 64 fp32 product over shared-memory tiles with rows padded to 65
+// floats (column walks hit distinct banks); thread (ti, tj) owns rows ti + 16a
+// and columns tj + 16b of each 64 x 64 result.  dQ rows belong to one CTA and
+// are stored; dK and dV of a key block collect contributions from every query
+// block and head that lists it and are added with fp32 atomics into buffers
+// the entry point zeroes first.
+#include "sd_prefill.cuh"
+
+namespace sd {
+namespace bwd {
+
+constexpr int kThreads = 256;
+constexpr int kLd = kHeadDim + 1;  // padded row stride of the shared tiles, floats
+constexpr int kTile = kQTile * kLd;
+constexpr size_t kSmemBytes = 6 * kTile * sizeof(float) + kQTile * sizeof(int);
+
+// acc[a][b] += sum_x A[row a][x] * B[row b][x]   (A B^T)
+__device__ __forceinline__ void mm_abt(const float *A, const float *B, int ti, int tj, float (&acc)[4][4]) {
+#pragma unroll 4
+  for (int x = 0; x < kHeadDim; ++x) {
+    float av[4], bv[4];
+#pragma unroll
+    for (int a = 0; a < 4; ++a) av[a] = A[(ti + 16 * a) * kLd + x];
+#pragma unroll
+    for (int b = 0; b < 4; ++b) bv[b] = B[(tj + 16 * b) * kLd + x];
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+      for (int b = 0; b < 4; ++b) acc[a][b] = fmaf(av[a], bv[b], acc[a][b]);
+  }
+}
+
+// acc[a][b] += sum_x A[row a][x] * B[x][col b]   (A B)
+__device__ __forceinline__ void mm_ab(const float *A, const float *B, int ti, int tj, float (&acc)[4][4]) {
+#pragma unroll 4
+  for (int x = 0; x < kQTile; ++x) {
+    float av[4], bv[4];
+#pragma unroll
+    for (int a = 0; a < 4; ++a) av[a] = A[(ti + 16 * a) * kLd + x];
+#pragma unroll
+    for (int b = 0; b < 4; ++b) bv[b] = B[x * kLd + tj + 16 * b];
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+      for (int b = 0; b < 4; ++b) acc[a][b] = fmaf(av[a], bv[b], acc[a][b]);
+  }
+}
+
+// acc[a][b] += sum_x A[x][col a] * B[x][col b]   (A^T B)
+__device__ __forceinline__ void mm_atb(const float *A, const float *B, int ti, int tj, float (&acc)[4][4]) {
+#pragma unroll 4
+  for (int x = 0; x < kQTile; ++x) {
+    float av[4], bv[4];
+#pragma unroll
+    for (int a = 0; a < 4; ++a) av[a] = A[x * kLd + ti + 16 * a];
+#pragma unroll
+    for (int b = 0; b < 4; ++b) bv[b] = B[x * kLd + tj + 16 * b];
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+      for (int b = 0; b < 4; ++b) acc[a][b] = fmaf(av[a], bv[b], acc[a][b]);
+  }
+}
+
+// Sum / maximum over the 16 lanes that share a row (lanes 0-15 or 16-31).
+__device__ __forceinline__ float half_sum(float x) {
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+  return x;
+}
+__device__ __forceinline__ float half_max(float x) {
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, o));
+  return x;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads)
+    prefill_bwd_kernel(const T *__restrict__ q, int64_t q_sb, int64_t q_st, int64_t q_sh, const T *__restrict__ k,
+                       const T *__restrict__ v, int64_t c_sb, int64_t c_sh, int64_t c_st,
+                       const T *__restrict__ dout, int64_t g_sb, int64_t g_st, int64_t g_sh, int64_t T_, int Hq,
+                       int Hkv, const int32_t *__restrict__ lists, const int32_t *__restrict__ counts, int lcap,
+                       const int64_t *__restrict__ topk, int kk, int causal, float scale, float *__restrict__ dq,
+                       float *__restrict__ dk, float *__restrict__ dv) {
+  extern __shared__ float smf[];
+  float *Qs = smf;          // q rows of the query block
+  float *Gs = Qs + kTile;   // dO rows
+  float *Ks = Gs + kTile;   // key block
+  float *Vs = Ks + kTile;   // value block
+  float *Ps = Vs + kTile;   // P of the block
+  float *Ds = Ps + kTile;   // dS of the block
+  int *s_ok = reinterpret_cast<int *>(Ds + kTile);  // row may see the block (valid row, member)
+
+  const int qt = blockIdx.x, hq = blockIdx.y, b = blockIdx.z;
+  const int G = Hq / Hkv, h = hq / G;
+  const int tid = threadIdx.x, ti = tid >> 4, tj = tid & 15;
+  const int64_t t0 = static_cast<int64_t>(qt) * kQTile;
+  const int nqt = gridDim.x;
+  const int64_t nbk = (T_ + kQTile - 1) / kQTile;
+
+  for (int e = tid; e < kQTile * kHeadDim; e += kThreads) {
+    const int r = e / kHeadDim, d = e % kHeadDim;
+    const int64_t t = t0 + r;
+    const bool ok = t < T_;
+    Qs[r * kLd + d] = ok ? to_f(q[b * q_sb + t * q_st + hq * q_sh + d]) : 0.f;
+    Gs[r * kLd + d] = ok ? to_f(dout[b * g_sb + t * g_st + hq * g_sh + d]) : 0.f;
+  }
+  const int64_t lrow = (static_cast<int64_t>(b) * Hkv + h) * nqt + qt;
+  const int32_t *list = lists + lrow * lcap;
+  int cnt = counts[lrow];
+  cnt = cnt < 0 ? 0 : (cnt > lcap ? lcap : cnt);
+  const T *kb = k + b * c_sb + h * c_sh;
+  const T *vb = v + b * c_sb + h * c_sh;
+
+  // stages key block j into Ks / Vs and each row's permission into s_ok
+  auto stage = [&](int j) {
+    const int64_t k0 = static_cast<int64_t>(j) * kQTile;
+    for (int e = tid; e < kQTile * kHeadDim; e += kThreads) {
+      const int rr = e / kHeadDim, d = e % kHeadDim;
+      const int64_t kt = k0 + rr;
+      const bool ok = kt < T_;
+      Ks[rr * kLd + d] = ok ? to_f(kb[kt * c_st + d]) : 0.f;
+      Vs[rr * kLd + d] = ok ? to_f(vb[kt * c_st + d]) : 0.f;
+    }
+    if (tid < kQTile) {
+      const int64_t t = t0 + tid;
+      bool ok = t < T_;
+      if (ok && topk) {  // masked forecast mode: per-row membership (sparse.py:243-247)
+        const int bq = static_cast<int>(t / kQTile);
+        const int64_t *rowk = topk + ((static_cast<int64_t>(b) * Hkv + h) * T_ + t) * kk;
+        bool in = (j == 0) || (j == bq);
+        for (int e = 0; e < kk && !in; ++e) {
+          int64_t jj = rowk[e];
+          jj = jj < 0 ? 0 : (jj > nbk - 1 ? nbk - 1 : jj);
+          in = jj == j;
+        }
+        ok = in;
+      }
+      s_ok[tid] = ok ? 1 : 0;
+    }
+  };
+  // whether (row ti + 16a, key tj + 16b of block j) is an allowed pair
+  auto allowed = [&](int a, int bb, int64_t k0) {
+    const int r = ti + 16 * a;
+    const int64_t kt = k0 + tj + 16 * bb;
+    return s_ok[r] != 0 && kt < T_ && (!causal || kt <= t0 + r);
+  };
+
+  // ---- pass 1: per-row maximum m, sum of exponentials l, sum of exp * dP
+  float m[4], l[4], pd[4];
+#pragma unroll
+  for (int a = 0; a < 4; ++a) {
+    m[a] = -INFINITY;
+    l[a] = 0.f;
+    pd[a] = 0.f;
+  }
+  for (int i = 0; i < cnt; ++i) {
+    const int j = list[i];
+    if (j < 0 || j >= nbk) continue;  // uniform across the CTA
+    __syncthreads();
+    stage(j);
+    __syncthreads();
+    const int64_t k0 = static_cast<int64_t>(j) * kQTile;
+    float s[4][4] = {}, dp[4][4] = {};
+    mm_abt(Qs, Ks, ti, tj, s);
+    mm_abt(Gs, Vs, ti, tj, dp);
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+      float x[4], mx = -INFINITY;
+#pragma unroll
+      for (int bb = 0; bb < 4; ++bb) {
+        x[bb] = allowed(a, bb, k0) ? s[a][bb] * scale : -INFINITY;
+        mx = fmaxf(mx, x[bb]);
+      }
+      const float mn = fmaxf(m[a], half_max(mx));
+      const float alpha = m[a] == -INFINITY ? 0.f : expf(m[a] - mn);
+      float ls = 0.f, lp = 0.f;
+#pragma unroll
+      for (int bb = 0; bb < 4; ++bb) {
+        const float e = x[bb] == -INFINITY ? 0.f : expf(x[bb] - mn);
+        ls += e;
+        lp = fmaf(e, dp[a][bb], lp);
+      }
+      ls = half_sum(ls);
+      lp = half_sum(lp);
+      l[a] = fmaf(l[a], alpha, ls);
+      pd[a] = fmaf(pd[a], alpha, lp);
+      m[a] = mn;
+    }
+  }
+  // log-sum-exp and Delta of each owned row (rows that see nothing: P = 0)
+  float lse[4], delta[4];
+#pragma unroll
+  for (int a = 0; a < 4; ++a) {
+    lse[a] = l[a] > 0.f ? m[a] + logf(l[a]) : INFINITY;
+    delta[a] = l[a] > 0.f ? pd[a] / l[a] : 0.f;
+  }
+
+  // ---- pass 2: P, dS per block; dQ in registers, dK / dV atomically
+  float gq[4][4] = {};
+  for (int i = 0; i < cnt; ++i) {
+    const int j = list[i];
+    if (j < 0 || j >= nbk) continue;
+    __syncthreads();
+    stage(j);
+    __syncthreads();
+    const int64_t k0 = static_cast<int64_t>(j) * kQTile;
+    float s[4][4] = {}, dp[4][4] = {};
+    mm_abt(Qs, Ks, ti, tj, s);
+    mm_abt(Gs, Vs, ti, tj, dp);
+    bool any = false;
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+      for (int bb = 0; bb < 4; ++bb) {
+        float p = 0.f, ds = 0.f;
+        if (allowed(a, bb, k0)) {
+          p = expf(s[a][bb] * scale - lse[a]);
+          ds = p * (dp[a][bb] - delta[a]);
+          any = true;
+        }
+        Ps[(ti + 16 * a) * kLd + tj + 16 * bb] = p;
+        Ds[(ti + 16 * a) * kLd + tj + 16 * bb] = ds;
+      }
+    if (!__syncthreads_or(any)) continue;  // no allowed pair in this block: nothing to add
+    mm_ab(Ds, Ks, ti, tj, gq);
+    float gk[4][4] = {}, gv[4][4] = {};
+    mm_atb(Ds, Qs, ti, tj, gk);
+    mm_atb(Ps, Gs, ti, tj, gv);
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+      const int64_t kt = k0 + ti + 16 * a;
+      if (kt >= T_) continue;
+      const int64_t base = ((static_cast<int64_t>(b) * Hkv + h) * T_ + kt) * kHeadDim;
+#pragma unroll
+      for (int bb = 0; bb < 4; ++bb) {
+        atomicAdd(dk + base + tj + 16 * bb, scale * gk[a][bb]);
+        atomicAdd(dv + base + tj + 16 * bb, gv[a][bb]);
+      }
+    }
+  }
+#pragma unroll
+  for (int a = 0; a < 4; ++a) {
+    const int64_t t = t0 + ti + 16 * a;
+    if (t >= T_) continue;
+    float *dst = dq + ((static_cast<int64_t>(b) * T_ + t) * Hq + hq) * kHeadDim;
+#pragma unroll
+    for (int bb = 0; bb < 4; ++bb) dst[tj + 16 * bb] = scale * gq[a][bb];
+  }
+}
+
+}  // namespace bwd
+}  // namespace sd
+
+extern "C" int sd_prefill_attention_backward(const void *q, const void *k, const void *v, const void *dout,
+                                             int dtype, int64_t B, int64_t T, int64_t Hq, int64_t Hkv, int64_t D,
+                                             int64_t q_sb, int64_t q_st, int64_t q_sh, int64_t c_sb, int64_t c_sh,
+                                             int64_t c_st, int64_t g_sb, int64_t g_st, int64_t g_sh,
+                                             const int32_t *lists, const int32_t *counts, int lcap,
+                                             const int64_t *topk, int kk, int block_size, int causal, float scale,
+                                             float *dq, float *dk, float *dv, void *stream) {
+  if (!q || !k || !v || !dout || !lists || !counts || !dq || !dk || !dv || B <= 0 || T <= 0 || Hq <= 0 ||
+      Hkv <= 0 || Hq % Hkv || lcap <= 0)
+    return SD_ERR_INVALID;
+  if (D != sd::kHeadDim || block_size != sd::kQTile) return SD_ERR_UNSUPPORTED;
+  if (topk && kk <= 0) return SD_ERR_INVALID;
+  const int64_t nqt = (T + sd::kQTile - 1) / sd::kQTile;
+  if (nqt > 0x7fffffff || Hq > 65535 || B > 65535) return SD_ERR_UNSUPPORTED;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const size_t kv_bytes = static_cast<size_t>(B * Hkv * T * D) * sizeof(float);
+  cudaError_t e = cudaMemsetAsync(dk, 0, kv_bytes, s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(dv, 0, kv_bytes, s);
+  if (e != cudaSuccess) {
+    sd::set_cuda_error(e);
+    return SD_ERR_CUDA;
+  }
+  const dim3 grid(static_cast<unsigned>(nqt), static_cast<unsigned>(Hq), static_cast<unsigned>(B));
+  SD_DISPATCH_DTYPE(dtype, E, {
+    auto kern = sd::bwd::prefill_bwd_kernel<E>;
+    if (sd::set_max_smem(kern, sd::bwd::kSmemBytes) != SD_OK) return SD_ERR_CUDA;
+    kern<<<grid, sd::bwd::kThreads, sd::bwd::kSmemBytes, s>>>(
+        static_cast<const E *>(q), q_sb, q_st, q_sh, static_cast<const E *>(k), static_cast<const E *>(v), c_sb,
+        c_sh, c_st, static_cast<const E *>(dout), g_sb, g_st, g_sh, T, static_cast<int>(Hq), static_cast<int>(Hkv),
+        lists, counts, lcap, topk, kk, causal, scale, dq, dk, dv);
+    return sd::check_launch();
+  });
+  return SD_OK;
+}

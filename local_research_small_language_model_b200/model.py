@@ -25,6 +25,14 @@ from .forecast import ForecastProjection
 from .rope import RotaryEmbedding
 
 
+def _records_grad(x: torch.Tensor, module: nn.Module) -> bool:
+    """Whether autograd is recording a graph that needs the gradient of x or of
+    one of the module's parameters.  The packed projections and the RMSNorm /
+    SwiGLU kernels have no backward, so such calls take the layer-by-layer
+    path, whose attention core has CUDA backward kernels."""
+    return torch.is_grad_enabled() and (x.requires_grad or any(p.requires_grad for p in module.parameters()))
+
+
 class RMSNorm(nn.Module):
     """model/norm.py:7-21."""
 
@@ -34,7 +42,9 @@ class RMSNorm(nn.Module):
         self.weight = nn.Parameter(torch.ones(dim))
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        if x.is_cuda and x.dtype == self.weight.dtype:
+        # the library's kernel has no backward: while autograd records a graph
+        # that needs x's or the gain's gradient, the differentiable formula runs
+        if x.is_cuda and x.dtype == self.weight.dtype and not _records_grad(x, self):
             c = x.shape[-1]
             return ops.rmsnorm(x.reshape(-1, c), self.weight, self.eps).view(x.shape)
         xf = x.float()
@@ -253,7 +263,8 @@ class TransformerBlock(nn.Module):
                 probe["end"].record()
             kv_cache.advance(1, device=not getattr(kv_cache, "shared_len", False))
             return self._ffn_decode(x2, out, tc).view(b, 1, c), current_forecast
-        elif x.is_cuda and mask is None and isinstance(self.attention, B200SparseAttention):
+        elif x.is_cuda and mask is None and isinstance(self.attention, B200SparseAttention) \
+                and not _records_grad(x, self):
             # prompt: one GEMM for [wq; wk; wv; wf], the attention core on views
             # of it, the residual adds folded into addmm, and the SwiGLU gate
             # on one [w_gate; w_up] GEMM (transformer.py:76-131 in 6 launches

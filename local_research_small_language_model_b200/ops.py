@@ -432,6 +432,37 @@ def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, lists: 
     return out
 
 
+def prefill_attention_backward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, dout: torch.Tensor,
+                               lists: torch.Tensor, counts: torch.Tensor, block_size: int,
+                               topk: Optional[torch.Tensor] = None, causal: bool = True,
+                               scale: Optional[float] = None) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Gradients of prefill_attention for the output gradient dout [B,T,Hq,D]
+    (the backward of the reference's masked / chunked SDPA, sparse.py:185-364):
+    same q, k, v, lists and topk as the forward.  Returns fp32 (dq [B,T,Hq,D],
+    dk [B,Hkv,T,D], dv [B,Hkv,T,D])."""
+    _cuda(q, k, v, dout, lists, counts, topk)
+    b, t, hq, d = q.shape
+    hkv = k.shape[1]
+    q, k, v, dout = _inner1(q), _inner1(k), _inner1(v), _inner1(dout)
+    if k.stride() != v.stride():
+        k, v = k.contiguous(), v.contiguous()
+    if q.dtype != k.dtype:
+        q = q.to(k.dtype)
+    if dout.dtype != k.dtype:
+        dout = dout.to(k.dtype)
+    dq = torch.empty(b, t, hq, d, dtype=torch.float32, device=q.device)
+    dk = torch.empty(b, hkv, t, d, dtype=torch.float32, device=q.device)
+    dv = torch.empty_like(dk)
+    tk = topk.to(torch.int64).contiguous() if topk is not None else None
+    sc = 1.0 / math.sqrt(d) if scale is None else scale
+    L.call("sd_prefill_attention_backward", q.data_ptr(), k.data_ptr(), v.data_ptr(), dout.data_ptr(),
+           dtype_code(k), b, t, hq, hkv, d, q.stride(0), q.stride(1), q.stride(2), k.stride(0), k.stride(1),
+           k.stride(2), dout.stride(0), dout.stride(1), dout.stride(2), lists.data_ptr(), counts.data_ptr(),
+           lists.shape[-1], tk.data_ptr() if tk is not None else None, tk.shape[-1] if tk is not None else 0,
+           block_size, int(bool(causal)), sc, dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), _stream(q))
+    return dq, dk, dv
+
+
 def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
     """RMSNorm (model/norm.py:15-21) over the last dim of a 2-D [rows, C] tensor."""
     _cuda(x, weight)

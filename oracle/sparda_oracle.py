@@ -383,6 +383,94 @@ def chunked_prefill(q, k, v, forecast, block_size: int, top_k: int, mode: str = 
     return chunked_attention(q, k, v, sel, cnt, block_size, scale, dtype), sel, cnt
 
 
+def masked_allowed_from_topk(topk: Optional[np.ndarray], seq_len: int, block_size: int,
+                             is_causal: bool = True) -> np.ndarray:
+    """The ``allowed`` mask of _forward_masked_sdpa (sparse.py:226-253) for
+    given per-row top-k block indices [B, H, T, k] (clamped to [0, N_b - 1]
+    like the reference's scatter): same block, the sink block or a top-k block
+    of the query row, and causal.  ``topk=None``: the dense causal mask
+    (sparse.py:201-224).  Returns [B, H|1, T, T] bool."""
+    t = np.arange(seq_len)
+    causal = t[None, :] <= t[:, None]
+    if topk is None:
+        allowed = causal if is_causal else np.ones_like(causal)
+        return allowed[None, None]
+    nb = num_blocks(seq_len, block_size)
+    b, h = topk.shape[0], topk.shape[1]
+    sel = np.zeros((b, h, seq_len, nb), dtype=bool)
+    np.put_along_axis(sel, np.clip(topk, 0, nb - 1), True, axis=-1)
+    bq = (t // block_size)[:, None]
+    bk = (t // block_size)[None, :]
+    allowed = sel[..., t // block_size] | ((bk == bq) | (bk == 0))[None, None]
+    if is_causal:
+        allowed = allowed & causal[None, None]
+    return allowed
+
+
+def chunked_allowed(sel: np.ndarray, cnt: np.ndarray, seq_len: int, block_size: int) -> np.ndarray:
+    """The key set of _forward_chunked_gather (sparse.py:334-360) as a mask:
+    query t sees key s when s's block is listed for t's q-block and s <= t.
+    sel [B, H, N_b, MS], cnt [B, H, N_b].  Returns [B, H, T, T] bool."""
+    b, h, nb, _ = sel.shape
+    t = np.arange(seq_len)
+    listed = np.zeros((b, h, nb, nb), dtype=bool)
+    for bb in range(b):
+        for hh in range(h):
+            for q in range(nb):
+                ids = sel[bb, hh, q, :cnt[bb, hh, q]]
+                listed[bb, hh, q, ids[(ids >= 0) & (ids < nb)]] = True
+    allowed = listed[:, :, (t // block_size)[:, None], (t // block_size)[None, :]]
+    return allowed & (t[None, :] <= t[:, None])[None, None]
+
+
+def attention_backward(q, k, v, dout, allowed, scale: Optional[float] = None, dtype=np.float64):
+    """Gradients of out = softmax(scale * q k^T over ``allowed``) v, the
+    backward autograd takes through the reference's SDPA calls
+    (sparse.py:255-282, :334-360) with GQA by repeat_interleave: a kv head's
+    dk / dv sum over its query heads.  q, dout [B, Hq, T, D]; k, v
+    [B, Hkv, T, D]; allowed [B, Hkv|1, T, T].  A row with no allowed key has a
+    zero output and zero gradients.  Returns (dq, dk, dv)."""
+    q, k, v, dout = (np.asarray(a, dtype=dtype) for a in (q, k, v, dout))
+    b, hq, t, d = q.shape
+    hkv = k.shape[1]
+    g = hq // hkv
+    scale = 1.0 / math.sqrt(d) if scale is None else scale
+    dq, dk, dv = np.zeros_like(q), np.zeros_like(k), np.zeros_like(v)
+    for h in range(hq):
+        kh = h // g
+        a = allowed[:, kh if allowed.shape[1] > 1 else 0]
+        sc = np.where(a, np.einsum("btd,bsd->bts", q[:, h], k[:, kh]) * scale, NEG_INF)
+        mx = sc.max(axis=-1, keepdims=True)
+        e = np.where(a, np.exp(sc - np.where(np.isfinite(mx), mx, 0.0)), 0.0)
+        den = e.sum(axis=-1, keepdims=True)
+        p = e / np.where(den > 0, den, 1.0)
+        dv[:, kh] += np.einsum("bts,btd->bsd", p, dout[:, h])
+        dp = np.einsum("btd,bsd->bts", dout[:, h], v[:, kh])
+        ds = p * (dp - (p * dp).sum(axis=-1, keepdims=True))
+        dq[:, h] = np.einsum("bts,bsd->btd", ds, k[:, kh]) * scale
+        dk[:, kh] += np.einsum("bts,btd->bsd", ds, q[:, h]) * scale
+    return dq, dk, dv
+
+
+def attention_forward(q, k, v, allowed, scale: Optional[float] = None, dtype=np.float64):
+    """softmax(scale * q k^T over ``allowed``) v, with zero rows where nothing
+    is allowed (the function attention_backward differentiates)."""
+    q, k, v = (np.asarray(a, dtype=dtype) for a in (q, k, v))
+    b, hq, t, d = q.shape
+    g = hq // k.shape[1]
+    scale = 1.0 / math.sqrt(d) if scale is None else scale
+    out = np.zeros_like(q)
+    for h in range(hq):
+        kh = h // g
+        a = allowed[:, kh if allowed.shape[1] > 1 else 0]
+        sc = np.where(a, np.einsum("btd,bsd->bts", q[:, h], k[:, kh]) * scale, NEG_INF)
+        mx = sc.max(axis=-1, keepdims=True)
+        e = np.where(a, np.exp(sc - np.where(np.isfinite(mx), mx, 0.0)), 0.0)
+        den = e.sum(axis=-1, keepdims=True)
+        out[:, h] = np.einsum("bts,bsd->btd", e / np.where(den > 0, den, 1.0), v[:, kh])
+    return out
+
+
 def gather_kv_blocks(k, v, block_indices, block_size: int):
     """gather_kv_blocks (sparse.py:19-62): k, v [B, H, T, D], indices [B, H, S]
     -> [B, H, S*block_size, D], zero beyond T."""

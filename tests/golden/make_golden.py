@@ -509,6 +509,43 @@ PREFETCH_ABS_CASES = [
 ]
 
 
+BACKWARD_CASES = [
+    # name, B, T, layer_idx, mode, with_forecast, chunked, seed
+    ("T256", 1, 256, 1, "forecast", True, False, 800),
+    ("T300_static", 1, 300, 1, "static", False, False, 801),
+    ("T200_layer0", 1, 200, 0, "forecast", True, False, 802),
+    ("T640_chunked", 1, 640, 1, "forecast", True, True, 803),
+]
+
+
+def backward_cases(torch, out):
+    """Gradients autograd takes through the reference's masked and chunked
+    attention cores (sparse.py:185-364) for loss = sum(out * w): q, k, v
+    gradients, row-subsampled, plus their full per-row sums.  The chunked case
+    has N_b = 10 = MS, so its unions are never truncated."""
+    res = {}
+    for name, b, t, li, mode, with_f, chunked, seed in BACKWARD_CASES:
+        a = _attn(torch, layer_idx=li, mode=mode)
+        q = torch.from_numpy(normal((b, 12, t, 64), seed=seed)).requires_grad_(True)
+        k = torch.from_numpy(normal((b, 4, t, 64), seed=seed + 1)).requires_grad_(True)
+        v = torch.from_numpy(normal((b, 4, t, 64), seed=seed + 2)).requires_grad_(True)
+        f = torch.from_numpy(normal((b, t, 4, 64), seed=seed + 3)) if with_f else None
+        w = torch.from_numpy(normal((b, t, 768), seed=seed + 4))
+        if chunked:
+            o = a._forward_chunked_gather(q, k, v, t, forecast_vector=f)
+        else:
+            o = a._forward_masked_sdpa(q, k, v, t, forecast_vector=f)
+        (o.reshape(b, t, 768) * w).sum().backward()
+        gq, gk, gv = (x.grad.double().numpy() for x in (q, k, v))
+        res[name + "_dq_rows"] = gq[:, :, ::29].astype(np.float32)
+        res[name + "_dk_rows"] = gk[:, :, ::13].astype(np.float32)
+        res[name + "_dv_rows"] = gv[:, :, ::13].astype(np.float32)
+        res[name + "_dq_sum"] = gq.sum(-1).astype(np.float32)
+        res[name + "_dk_sum"] = gk.sum(-1).astype(np.float32)
+        res[name + "_dv_sum"] = gv.sum(-1).astype(np.float32)
+    np.savez(os.path.join(out, "backward.npz"), **res)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True)
@@ -518,7 +555,7 @@ def main():
     torch = _setup(args.reference)
     jobs = [config1, compressor_cases, selector_cases, decode_cases, masked_cases, chunked_cases,
             prefetch_cases, model_cases, decode_big_cases, model_sparse_cases, chunked_big_cases,
-            prefetch_abs_cases, async_decode_cases]
+            prefetch_abs_cases, async_decode_cases, backward_cases]
     for job in jobs:
         if args.only and job.__name__ not in args.only.split(","):
             continue

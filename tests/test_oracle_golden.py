@@ -389,3 +389,71 @@ def test_async_decode_vs_reference(golden, case):
         for ix in np.ndindex(*cnt.shape):
             assert set(sel[ix][:cnt[ix]].tolist()) == set(rsel[ix][:rcnt[ix]].tolist()), (s, ix)
         np.testing.assert_allclose(outs[s], g[f"{case}_s{s}_out"], rtol=0, atol=2e-6)
+
+
+def backward_inputs(b, t, with_f, seed):
+    """Regenerates a backward case's inputs (make_golden.backward_cases):
+    q [B,12,T,64], k, v [B,4,T,64], forecast [B,T,4,64] or None, and the
+    output gradient [B,12,T,64] of loss = sum(out * w)."""
+    q = normal((b, 12, t, 64), seed=seed)
+    k = normal((b, 4, t, 64), seed=seed + 1)
+    v = normal((b, 4, t, 64), seed=seed + 2)
+    f = normal((b, t, 4, 64), seed=seed + 3) if with_f else None
+    dout = normal((b, t, 768), seed=seed + 4).reshape(b, t, 12, 64).transpose(0, 2, 1, 3)
+    return q, k, v, f, dout
+
+
+def oracle_backward_allowed(k, f, t, layer_idx, mode, chunked):
+    """The oracle's allowed mask of a backward case (masked or chunked path)."""
+    if chunked:
+        reps = O.compress_blocks(k.transpose(0, 2, 1, 3), 64)
+        sel, cnt, union = O.chunked_select(f, reps, t, 64, 8, k.shape[0], k.shape[1], mode)
+        assert union.sum(-1).max() <= 10  # N_b = MS: no truncation, the reference's lists
+        return O.chunked_allowed(sel, cnt, t, 64)
+    allowed, _, _ = O.masked_allowed(f, k, t, 64, 8, layer_idx, mode, True)
+    return allowed
+
+
+def _bwd_ids():
+    from tests.golden.make_golden import BACKWARD_CASES
+    return BACKWARD_CASES
+
+
+@pytest.mark.parametrize("case", _bwd_ids(), ids=[c[0] for c in _bwd_ids()])
+def test_attention_backward_vs_reference(golden, case):
+    """The oracle's gradients of the masked / chunked attention cores equal the
+    ones autograd took through the reference (fp32) for loss = sum(out * w)."""
+    name, b, t, li, mode, with_f, chunked, seed = case
+    g = golden("backward")
+    q, k, v, f, dout = backward_inputs(b, t, with_f, seed)
+    allowed = oracle_backward_allowed(k, f, t, li, mode, chunked)
+    dq, dk, dv = O.attention_backward(q, k, v, dout, allowed)
+    for got, key, every in ((dq, "dq", 29), (dk, "dk", 13), (dv, "dv", 13)):
+        np.testing.assert_allclose(got[:, :, ::every], g[f"{name}_{key}_rows"], rtol=1e-4, atol=2e-5)
+        np.testing.assert_allclose(got.sum(-1), g[f"{name}_{key}_sum"], rtol=1e-4, atol=2e-4)
+
+
+def test_attention_backward_finite_differences():
+    """attention_backward is the gradient of attention_forward: central
+    differences in float64 on a small GQA case with a row that sees nothing."""
+    rng = np.random.default_rng(7)
+    b, hq, hkv, t, d = 1, 4, 2, 9, 8
+    q, dout = rng.standard_normal((b, hq, t, d)), rng.standard_normal((b, hq, t, d))
+    k, v = rng.standard_normal((b, hkv, t, d)), rng.standard_normal((b, hkv, t, d))
+    allowed = rng.random((b, hkv, t, t)) < 0.6
+    allowed[:, 1, 3] = False  # an empty row: zero output, zero gradients
+    dq, dk, dv = O.attention_backward(q, k, v, dout, allowed)
+
+    def loss(qq, kk, vv):
+        return float((O.attention_forward(qq, kk, vv, allowed) * dout).sum())
+
+    eps = 1e-6
+    for x, gx, which in ((q, dq, 0), (k, dk, 1), (v, dv, 2)):
+        for ix in [tuple(rng.integers(0, n) for n in x.shape) for _ in range(12)]:
+            args = [q.copy(), k.copy(), v.copy()]
+            args[which][ix] += eps
+            up = loss(*args)
+            args[which][ix] -= 2 * eps
+            fd = (up - loss(*args)) / (2 * eps)
+            assert abs(fd - gx[ix]) <= 1e-6 * max(1.0, abs(fd)), (which, ix, fd, gx[ix])
+    assert np.all(dq[:, 2:4, 3] == 0)  # query heads 2, 3 use kv head 1's empty row
