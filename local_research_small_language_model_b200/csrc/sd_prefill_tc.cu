@@ -14,10 +14,14 @@
 //                       masks (block membership, causality, length), online
 //                       max/sum in fp32 with a lazily updated reference maximum
 //                       (raised only when a block exceeds it by 2^8, the
-//                       output rows in TMEM then rescaled), P row -> 16-bit ->
-//                       swizzled smem
-//   O_x += P_x V        tcgen05.mma M=128 N=64 K=64 with V MN-major, accumulated
-//                       in TMEM across the blocks (no per-block read-out)
+//                       output rows in TMEM then rescaled), P row -> 16-bit
+//                       pairs -> tcgen05.st over the first 32 columns of S_x
+//   O_x += P_x V        tcgen05.mma M=128 N=64 K=64 with A (= P) read from
+//                       tensor memory and V MN-major from shared memory,
+//                       accumulated in TMEM across the blocks (no per-block
+//                       read-out); the next S_x MMA, issued after it by the
+//                       same thread, overwrites P only after it (tcgen05.mma
+//                       operations of a thread execute in issue order)
 // The first thread of each warpgroup issues its tile's MMAs and commits them
 // to that tile's mbarriers; every wait is bounded.  TMEM: 256 columns (S0, S1,
 // O0, O1) per CTA, 2 CTAs per SM.
@@ -41,8 +45,7 @@ constexpr int kMaxKK = 16;                      // per-row top-k kept in registe
 struct Smem {
   // all tile buffers 1024-byte aligned (128-byte swizzle atoms)
   static constexpr int kQ = 0;                          // 2 tiles
-  static constexpr int kP = kQ + 2 * kTileBytes;        // 2 tiles
-  static constexpr int kK = kP + 2 * kTileBytes;        // kStages tiles
+  static constexpr int kK = kQ + 2 * kTileBytes;        // kStages tiles
   static constexpr int kV = kK + kStages * kKvBytes;    // kStages tiles
   static constexpr int kBar = kV + kStages * kKvBytes;  // mbarriers
   static constexpr int kBytes = kBar + 256;
@@ -67,6 +70,16 @@ __device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t a, uint64_t b,
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
       "l"(a), "l"(b), "r"(idesc), "r"(acc ? 1u : 0u)
+      : "memory");
+}
+
+// The same MMA with A (M x K, K-major 16-bit pairs per 32-bit column) read
+// from tensor memory at column address tmem_a.
+__device__ __forceinline__ void mma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t b, uint32_t idesc, bool acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(b), "r"(idesc), "r"(acc ? 1u : 0u)
       : "memory");
 }
 
@@ -259,7 +272,6 @@ __global__ void __launch_bounds__(tc::kThreads, 2)
     return res != 0;
   };
   const uint32_t qaddr = smem_u32(sm + Smem::kQ + x * kTileBytes);
-  const uint32_t paddr = smem_u32(sm + Smem::kP + x * kTileBytes);
   auto issue_s = [&](int i) {  // leader: S_x = Q_x K^T for list entry i
     const int s = i % kStages;
     const bool got = mbar_wait_bounded(&full[s], (i / kStages) & 1);
@@ -360,27 +372,26 @@ __global__ void __launch_bounds__(tc::kThreads, 2)
       }
       const float nmn = mn == -INFINITY ? 0.f : -mn;  // rows with nothing visible yet keep p = 0
       float ps8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // 8 partial row sums
-      char *prow = sm + Smem::kP + x * kTileBytes;
+      // P row as 16-bit pairs (key 2c in the low half of column c) over the
+      // first 32 columns of S_x, already read out above
 #pragma unroll
-      for (int c8 = 0; c8 < 8; ++c8) {
-        float p[8];
+      for (int h2 = 0; h2 < 2; ++h2) {
+        float pw[16];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          p[u] = ex2(fmaf(sc[8 * c8 + u], scale_log2, nmn));
-          ps8[u] += p[u];
+        for (int c = 0; c < 16; ++c) {
+          const int kc = 32 * h2 + 2 * c;
+          const float p0 = ex2(fmaf(sc[kc], scale_log2, nmn)), p1 = ex2(fmaf(sc[kc + 1], scale_log2, nmn));
+          ps8[(2 * c) & 7] += p0;
+          ps8[(2 * c + 1) & 7] += p1;
+          pw[c] = __uint_as_float(pack2<T>(p0, p1));
         }
-        uint4 w;
-        w.x = pack2<T>(p[0], p[1]);
-        w.y = pack2<T>(p[2], p[3]);
-        w.z = pack2<T>(p[4], p[5]);
-        w.w = pack2<T>(p[6], p[7]);
-        *reinterpret_cast<uint4 *>(prow + sw128(r, c8)) = w;
+        tmem_st16(t_s + 16 * h2, pw);
       }
+      tmem_wait_st();
       const float ps = ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) + ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
       l = l * alpha + ps;
       m = mn;
     }
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     fence_before_sync();
     wg_sync();
     // O_x += P_x V (V tile MN-major: 64 keys of 128-byte rows; the first
@@ -391,8 +402,8 @@ __global__ void __launch_bounds__(tc::kThreads, 2)
       const uint32_t vaddr = smem_u32(sm + Smem::kV + s * kKvBytes);
 #pragma unroll
       for (int k = 0; k < 4; ++k)
-        mma_f16(tmem + 128 + 64 * x, umma_desc_sw128(paddr + 32 * k, 16, 1024),
-                umma_desc_sw128(vaddr + 2048 * k, kKvBytes, 1024), id_pv, i > 0 || k > 0);
+        mma_f16_ts(tmem + 128 + 64 * x, tmem + 64 * x + 8 * k, umma_desc_sw128(vaddr + 2048 * k, kKvBytes, 1024),
+                   id_pv, i > 0 || k > 0);
       mma_commit(&o_bar[x]);
       if (i + 1 < cnt) ok = issue_s(i + 1) && ok;
     }
