@@ -169,12 +169,13 @@ SD_API int sd_decode_sparse_noalloc(const void *q, int dtype, int64_t q_sb, int6
  * (model/attention/base.py:19-29) for the block-major cache of this library:
  * k_cache, v_cache [B,H,Tcap,D] contiguous, proto_sum fp32 [B,H,NBcap,D]
  * contiguous (running block sums; prototype = sum / block_size).
- * xk, xv: [B,T,H,D] with strides (sb, st, sh); written at positions
- * start .. start+T-1, then the sums of every touched block are recomputed. */
+ * xk, xv: [B,T,H,D] with element strides (sb, st, sh) and (vsb, vst, vsh);
+ * written at positions start .. start+T-1, then the sums of every touched
+ * block are recomputed in fp32. */
 SD_API int sd_kv_append(const void *xk, const void *xv, int dtype, int64_t B, int64_t T, int64_t H,
-                 int64_t D, int64_t sb, int64_t st, int64_t sh, void *k_cache, void *v_cache,
-                 float *proto_sum, int64_t Tcap, int64_t NBcap, int64_t start, int block_size,
-                 void *stream);
+                 int64_t D, int64_t sb, int64_t st, int64_t sh, int64_t vsb, int64_t vst, int64_t vsh,
+                 void *k_cache, void *v_cache, float *proto_sum, int64_t Tcap, int64_t NBcap, int64_t start,
+                 int block_size, void *stream);
 
 /* Fused decode layer: RoPE + KV append + compressor update + selection +
  * block-sparse attention, one CTA per (sequence, kv head).  Replaces

@@ -47,8 +47,8 @@ _SIGS = {
     "sd_decode_attention": [_c_void_p, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _c_void_p, _c_void_p, _i64, _i64,
                             _i64, _i64, _c_void_p, _c_void_p, _i32, _i64, _i32, _f32, _c_void_p, _i64, _i64,
                             _c_void_p, _c_void_p],
-    "sd_kv_append": [_c_void_p, _c_void_p, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _c_void_p, _c_void_p,
-                     _c_void_p, _i64, _i64, _i64, _i32, _c_void_p],
+    "sd_kv_append": [_c_void_p, _c_void_p, _i32, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
+                     _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _i32, _c_void_p],
     "sd_decode_layer": [_c_void_p, _i32, _i64, _c_void_p, _i32, _i64, _c_void_p, _c_void_p, _i64, _c_void_p,
                         _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _i64, _i64, _i64, _i32, _i32, _i32, _f32,
                         _c_void_p, _i64, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _c_void_p,

@@ -210,15 +210,12 @@ def kv_append(xk: torch.Tensor, xv: torch.Tensor, k_store: torch.Tensor, v_store
     """Writes xk, xv [B,T,H,D] into the head-major stores [B,H,Tcap,D] at
     positions start.. and refreshes the block sums [B,H,NBcap,D] they touch."""
     _cuda(xk, xv, k_store, v_store, proto_sum)
-    if xk.stride() != xv.stride():
-        xk, xv = xk.contiguous(), xv.contiguous()
     xk, xv = _inner1(xk.to(k_store.dtype)), _inner1(xv.to(v_store.dtype))
-    if xk.stride() != xv.stride():
-        xk, xv = xk.contiguous(), xv.contiguous()
     b, t, h, d = xk.shape
     L.call("sd_kv_append", xk.data_ptr(), xv.data_ptr(), dtype_code(k_store), b, t, h, d, xk.stride(0),
-           xk.stride(1), xk.stride(2), k_store.data_ptr(), v_store.data_ptr(), proto_sum.data_ptr(),
-           k_store.shape[2], proto_sum.shape[2], start, block_size, _stream(xk))
+           xk.stride(1), xk.stride(2), xv.stride(0), xv.stride(1), xv.stride(2), k_store.data_ptr(),
+           v_store.data_ptr(), proto_sum.data_ptr(), k_store.shape[2], proto_sum.shape[2], start, block_size,
+           _stream(xk))
 
 
 def _rope_tables(cos: torch.Tensor, sin: torch.Tensor, head_dim: int, need: int) -> None:
