@@ -71,6 +71,10 @@ def parse():
     ap.add_argument("--kernels-only", action="store_true",
                     help="only the standalone kernel measurements (compressor, gather, prefill selector and list "
                          "builder at BASELINE sizes), one JSON line; for profiler captures of those kernels")
+    ap.add_argument("--backward", action="store_true",
+                    help="only the block-sparse attention backward (sd_prefill_attention_backward) and its forward "
+                         "on one --ctx-token sequence (12 query / 4 kv heads, bf16, the masked forecast lists up to "
+                         "8192 tokens, chunked above), one JSON line; for training-path timing and profiler captures")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the config-3 prefill and standalone-kernel sub-measurements of the default run")
     ap.add_argument("--cpu-budget-s", type=float, default=15.0)
@@ -669,6 +673,39 @@ def _graph_time_s(fns):
     return e0.elapsed_time(e1) / 1000.0 / len(fns)
 
 
+def run_backward(args, local: int):
+    """Event-timed attention backward and forward of one prefill layer's
+    shapes; the products the backward executes (7 fp32 64x64x64 products per
+    listed key block, query block and head) against the fp32 CUDA-core rate."""
+    import torch
+    from local_research_small_language_model_b200 import ops
+    dev = torch.device("cuda", local)
+    g = torch.Generator(device=dev).manual_seed(0)
+    T, hq, hkv = args.ctx, 12, 4
+    q = torch.randn(1, T, hq, 64, generator=g, device=dev, dtype=torch.bfloat16)
+    k = torch.randn(1, hkv, T, 64, generator=g, device=dev, dtype=torch.bfloat16)
+    v = torch.randn(1, hkv, T, 64, generator=g, device=dev, dtype=torch.bfloat16)
+    go = torch.randn(1, T, hq, 64, generator=g, device=dev, dtype=torch.bfloat16)
+    f = torch.randn(1, T, hkv, 64, generator=g, device=dev, dtype=torch.bfloat16)
+    chunked = T > 8192
+    reps = ops.compress_blocks(k.transpose(1, 2).contiguous(), 64)
+    _, topk = ops.select_blocks(f, reps, 8, 64, not chunked, return_scores=False)
+    mode = "chunked_forecast" if chunked else "masked_forecast"
+    lists, counts = ops.prefill_lists(mode, 1, hkv, T, 64, 8, topk, True, device=dev)
+    row_topk = None if chunked else topk
+    bwd_s = _event_time_s(lambda: ops.prefill_attention_backward(q, k, v, go, lists, counts, 64, row_topk, True))
+    fwd_s = _event_time_s(lambda: ops.prefill_attention(q, k, v, lists, counts, 64, row_topk, True))
+    ops.check_device_errors(dev)
+    blocks = int(counts.clamp_min(0).sum().item()) * (hq // hkv)
+    flops = blocks * 7 * 2 * 64 ** 3
+    fp32_peak = 148 * 128 * 2 * 1.965e9 / 1e12
+    return {"kernel": "sd::bwd::prefill_bwd_kernel<bf16> (sd_prefill_attention_backward)",
+            "mode": mode, "seq_len": T, "us": round(bwd_s * 1e6, 2), "forward_us": round(fwd_s * 1e6, 2),
+            "flops": flops, "tflops": round(flops / bwd_s / 1e12, 2),
+            "fp32_simt_peak_tflops": round(fp32_peak, 1), "frac_of_fp32_simt": round(flops / bwd_s / 1e12 / fp32_peak, 3),
+            "bound": "fp32 CUDA-core products: shared-memory operand loads and, at small T, too few CTAs"}
+
+
 def run_kernels(local: int):
     """Standalone device time of the path's other kernels on BASELINE-sized
     inputs, against the HBM roofline (algorithmic bytes per launch / time):
@@ -769,6 +806,12 @@ def main():
         import torch
         torch.cuda.set_device(local)
         print(json.dumps({"kernels": run_kernels(local)}), flush=True)
+        return 0
+
+    if args.backward:
+        import torch
+        torch.cuda.set_device(local)
+        print(json.dumps({"backward": run_backward(args, local)}), flush=True)
         return 0
 
     if world > 1:
