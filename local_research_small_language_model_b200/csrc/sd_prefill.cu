@@ -259,7 +259,9 @@ extern "C" int sd_prefill_lists(int mode, int causal, int64_t B, int64_t H, int6
   const size_t smem = sizeof(int) * nb;
   if (sd::set_max_smem(sd::prefill_lists_kernel, smem) != SD_OK) return SD_ERR_CUDA;
   dim3 grid(static_cast<unsigned>(nb), static_cast<unsigned>(H), static_cast<unsigned>(B));
-  sd::prefill_lists_kernel<<<grid, 256, smem, static_cast<cudaStream_t>(stream)>>>(
+  // 64 threads per list: most of a list's time is one warp's union / cut, so
+  // small CTAs let up to 32 lists per SM overlap those serial phases
+  sd::prefill_lists_kernel<<<grid, 64, smem, static_cast<cudaStream_t>(stream)>>>(
       mode, causal, T, block_size, top_k, (int)H, topk, kk, lcap, lists, counts);
   return sd::check_launch();
 }
