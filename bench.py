@@ -675,8 +675,10 @@ def _graph_time_s(fns):
 
 def run_backward(args, local: int):
     """Event-timed attention backward and forward of one prefill layer's
-    shapes; the products the backward executes (7 fp32 64x64x64 products per
-    listed key block, query block and head) against the fp32 CUDA-core rate."""
+    shapes.  Per listed key block, query block and head the backward runs
+    seven 64x64x64 products: S and dP (twice: both passes) on the tensor
+    cores, dQ, dK and dV as fp32 CUDA-core products (the part reported against
+    the fp32 CUDA-core rate)."""
     import torch
     from local_research_small_language_model_b200 import ops
     dev = torch.device("cuda", local)
@@ -697,13 +699,15 @@ def run_backward(args, local: int):
     fwd_s = _event_time_s(lambda: ops.prefill_attention(q, k, v, lists, counts, 64, row_topk, True))
     ops.check_device_errors(dev)
     blocks = int(counts.clamp_min(0).sum().item()) * (hq // hkv)
-    flops = blocks * 7 * 2 * 64 ** 3
+    per_product = 2 * 64 ** 3
     fp32_peak = 148 * 128 * 2 * 1.965e9 / 1e12
-    return {"kernel": "sd::bwd::prefill_bwd_kernel<bf16> (sd_prefill_attention_backward)",
+    simt = blocks * 3 * per_product  # dQ, dK, dV from the fp32 P and dS
+    return {"kernel": "sd::bwd::prefill_bwd_tc_kernel<bf16> (sd_prefill_attention_backward)",
             "mode": mode, "seq_len": T, "us": round(bwd_s * 1e6, 2), "forward_us": round(fwd_s * 1e6, 2),
-            "flops": flops, "tflops": round(flops / bwd_s / 1e12, 2),
-            "fp32_simt_peak_tflops": round(fp32_peak, 1), "frac_of_fp32_simt": round(flops / bwd_s / 1e12 / fp32_peak, 3),
-            "bound": "fp32 CUDA-core products: shared-memory operand loads and, at small T, too few CTAs"}
+            "flops": blocks * 7 * per_product, "tensor_flops": blocks * 4 * per_product, "simt_flops": simt,
+            "simt_tflops": round(simt / bwd_s / 1e12, 2), "fp32_simt_peak_tflops": round(fp32_peak, 1),
+            "simt_frac": round(simt / bwd_s / 1e12 / fp32_peak, 3),
+            "bound": "the three fp32 CUDA-core products (S and dP run on the tensor cores); at small T, too few CTAs"}
 
 
 def run_kernels(local: int):

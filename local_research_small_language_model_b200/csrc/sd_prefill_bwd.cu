@@ -20,6 +20,7 @@
 // block and head that lists it and are added with fp32 atomics into buffers
 // the entry point zeroes first.
 #include "sd_prefill.cuh"
+#include "sd_tma.cuh"
 
 namespace sd {
 namespace bwd {
@@ -264,6 +265,293 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
+// ---------------------------------------------------------------------------
+// 16-bit inputs: S = Q K^T and dP = dO V^T on the tensor cores (mma.sync
+// m16n8k16, fp32 accumulators).  A product of two 16-bit values is exact in
+// fp32, so these match the fp32 products above up to accumulation order.  The
+// three products that consume the fp32 P and dS stay fp32 CUDA-core products,
+// reading K, Q and dO from the same 16-bit tiles.  Warp w computes S / dP for
+// rows 16 (w % 4) .. +15 and keys 32 (w / 4) .. +31 of each block; pass 1 keeps
+// separate running statistics per key half, merged once at its end.
+// ---------------------------------------------------------------------------
+constexpr int kLdb = 72;  // 16-bit tile row stride in elements (144 bytes: ldmatrix rows on distinct banks)
+constexpr int kTileB = kQTile * kLdb;
+constexpr size_t kSmemTcBytes =
+    4 * kTileB * 2 + 2 * kTile * sizeof(float) + kQTile * sizeof(int) + 2 * kQTile * 3 * sizeof(float);
+
+// acc[a][b] += sum_x A[row a][x] * B[x][col b], B a 16-bit tile
+template <typename T>
+__device__ __forceinline__ void mm_ab16(const float *A, const T *B, int ti, int tj, float (&acc)[4][4]) {
+#pragma unroll 4
+  for (int x = 0; x < kQTile; ++x) {
+    float av[4], bv[4];
+#pragma unroll
+    for (int a = 0; a < 4; ++a) av[a] = A[(ti + 16 * a) * kLd + x];
+#pragma unroll
+    for (int b = 0; b < 4; ++b) bv[b] = to_f(B[x * kLdb + tj + 16 * b]);
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+      for (int b = 0; b < 4; ++b) acc[a][b] = fmaf(av[a], bv[b], acc[a][b]);
+  }
+}
+
+// acc[a][b] += sum_x A[x][col a] * B[x][col b], B a 16-bit tile
+template <typename T>
+__device__ __forceinline__ void mm_atb16(const float *A, const T *B, int ti, int tj, float (&acc)[4][4]) {
+#pragma unroll 4
+  for (int x = 0; x < kQTile; ++x) {
+    float av[4], bv[4];
+#pragma unroll
+    for (int a = 0; a < 4; ++a) av[a] = A[x * kLd + ti + 16 * a];
+#pragma unroll
+    for (int b = 0; b < 4; ++b) bv[b] = to_f(B[x * kLdb + tj + 16 * b]);
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+      for (int b = 0; b < 4; ++b) acc[a][b] = fmaf(av[a], bv[b], acc[a][b]);
+  }
+}
+
+// Sum / maximum over the 4 lanes that share a row of an mma.sync C fragment.
+__device__ __forceinline__ float quad_sum(float x) {
+  x += __shfl_xor_sync(0xffffffffu, x, 1);
+  return x + __shfl_xor_sync(0xffffffffu, x, 2);
+}
+__device__ __forceinline__ float quad_max(float x) {
+  x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 1));
+  return fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 2));
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 2)
+    prefill_bwd_tc_kernel(const T *__restrict__ q, int64_t q_sb, int64_t q_st, int64_t q_sh, const T *__restrict__ k,
+                          const T *__restrict__ v, int64_t c_sb, int64_t c_sh, int64_t c_st,
+                          const T *__restrict__ dout, int64_t g_sb, int64_t g_st, int64_t g_sh, int64_t T_, int Hq,
+                          int Hkv, const int32_t *__restrict__ lists, const int32_t *__restrict__ counts, int lcap,
+                          const int64_t *__restrict__ topk, int kk, int causal, float scale, float *__restrict__ dq,
+                          float *__restrict__ dk, float *__restrict__ dv) {
+  extern __shared__ __align__(16) char smraw[];
+  T *Qb = reinterpret_cast<T *>(smraw);  // q  [row][d]
+  T *Gb = Qb + kTileB;                   // dO [row][d]
+  T *Kb = Gb + kTileB;                   // k of the block [key][d]
+  T *Vb = Kb + kTileB;                   // v of the block [key][d]
+  float *Ps = reinterpret_cast<float *>(Vb + kTileB);  // P  [row][key]
+  float *Ds = Ps + kTile;                              // dS [row][key]
+  int *s_ok = reinterpret_cast<int *>(Ds + kTile);
+  float *s_stat = reinterpret_cast<float *>(s_ok + kQTile);  // [key half][row][m, l, pd]
+
+  const int qt = blockIdx.x, hq = blockIdx.y, b = blockIdx.z;
+  const int G = Hq / Hkv, h = hq / G;
+  const int tid = threadIdx.x, ti = tid >> 4, tj = tid & 15;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int rg = warp & 3, kh = warp >> 2;  // MMA rows 16 rg .., keys 32 kh ..
+  const int r0 = 16 * rg + (lane >> 2);     // this thread's fragment rows r0 and r0 + 8
+  const int kc = 32 * kh + 2 * (lane & 3);  // its fragment keys kc + 8 nt + {0, 1}
+  const int64_t t0 = static_cast<int64_t>(qt) * kQTile;
+  const int nqt = gridDim.x;
+  const int64_t nbk = (T_ + kQTile - 1) / kQTile;
+  constexpr int kCh = kHeadDim / 8;  // 16-byte chunks of a row
+
+  for (int e = tid; e < kQTile * kCh; e += kThreads) {
+    const int r = e / kCh, c8 = (e - r * kCh) * 8;
+    const int64_t t = t0 + r;
+    uint4 xq = make_uint4(0u, 0u, 0u, 0u), xg = xq;
+    if (t < T_) {
+      xq = *reinterpret_cast<const uint4 *>(q + b * q_sb + t * q_st + hq * q_sh + c8);
+      xg = *reinterpret_cast<const uint4 *>(dout + b * g_sb + t * g_st + hq * g_sh + c8);
+    }
+    *reinterpret_cast<uint4 *>(Qb + r * kLdb + c8) = xq;
+    *reinterpret_cast<uint4 *>(Gb + r * kLdb + c8) = xg;
+  }
+  const int64_t lrow = (static_cast<int64_t>(b) * Hkv + h) * nqt + qt;
+  const int32_t *list = lists + lrow * lcap;
+  int cnt = counts[lrow];
+  cnt = cnt < 0 ? 0 : (cnt > lcap ? lcap : cnt);
+  const T *kbase = k + b * c_sb + h * c_sh;
+  const T *vbase = v + b * c_sb + h * c_sh;
+
+  auto stage = [&](int j) {
+    const int64_t k0 = static_cast<int64_t>(j) * kQTile;
+    for (int e = tid; e < kQTile * kCh; e += kThreads) {
+      const int c = e / kCh, c8 = (e - c * kCh) * 8;
+      const int64_t kt = k0 + c;
+      uint4 xk = make_uint4(0u, 0u, 0u, 0u), xv = xk;
+      if (kt < T_) {
+        xk = *reinterpret_cast<const uint4 *>(kbase + kt * c_st + c8);
+        xv = *reinterpret_cast<const uint4 *>(vbase + kt * c_st + c8);
+      }
+      *reinterpret_cast<uint4 *>(Kb + c * kLdb + c8) = xk;
+      *reinterpret_cast<uint4 *>(Vb + c * kLdb + c8) = xv;
+    }
+    if (tid < kQTile) {
+      const int64_t t = t0 + tid;
+      bool ok = t < T_;
+      if (ok && topk) {  // masked forecast mode: per-row membership (sparse.py:243-247)
+        const int bq = static_cast<int>(t / kQTile);
+        const int64_t *rowk = topk + ((static_cast<int64_t>(b) * Hkv + h) * T_ + t) * kk;
+        bool in = (j == 0) || (j == bq);
+        for (int e = 0; e < kk && !in; ++e) {
+          int64_t jj = rowk[e];
+          jj = jj < 0 ? 0 : (jj > nbk - 1 ? nbk - 1 : jj);
+          in = jj == j;
+        }
+        ok = in;
+      }
+      s_ok[tid] = ok ? 1 : 0;
+    }
+  };
+  auto allowed = [&](int r, int key, int64_t k0) {
+    const int64_t kt = k0 + key;
+    return s_ok[r] != 0 && kt < T_ && (!causal || kt <= t0 + r);
+  };
+  // S (s) and dP (p) of this warp's 16 x 32 block: n-tiles nt = keys 32 kh + 8 nt ..
+  auto products = [&](float (&sacc)[4][4], float (&pacc)[4][4]) {
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        sacc[nt][i] = 0.f;
+        pacc[nt][i] = 0.f;
+      }
+#pragma unroll
+    for (int ks = 0; ks < kHeadDim / 16; ++ks) {
+      uint32_t aq[4], ag[4];
+      const int arow = 16 * rg + (lane & 15), acol = 16 * ks + (lane >> 4) * 8;
+      ldsm_x4(smem_u32(Qb + arow * kLdb + acol), aq[0], aq[1], aq[2], aq[3]);
+      ldsm_x4(smem_u32(Gb + arow * kLdb + acol), ag[0], ag[1], ag[2], ag[3]);
+#pragma unroll
+      for (int np = 0; np < 2; ++np) {
+        const int brow = 32 * kh + 16 * np + (lane & 7) + ((lane >> 4) << 3);
+        const int bcol = 16 * ks + ((lane >> 3) & 1) * 8;
+        uint32_t bk[4], bv[4];
+        ldsm_x4(smem_u32(Kb + brow * kLdb + bcol), bk[0], bk[1], bk[2], bk[3]);
+        ldsm_x4(smem_u32(Vb + brow * kLdb + bcol), bv[0], bv[1], bv[2], bv[3]);
+        mma16816<T>(sacc[2 * np], aq, bk[0], bk[1]);
+        mma16816<T>(sacc[2 * np + 1], aq, bk[2], bk[3]);
+        mma16816<T>(pacc[2 * np], ag, bv[0], bv[1]);
+        mma16816<T>(pacc[2 * np + 1], ag, bv[2], bv[3]);
+      }
+    }
+  };
+
+  // ---- pass 1: per (row, key half) running maximum, sum of exponentials and
+  // sum of exp * dP
+  float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f}, pd[2] = {0.f, 0.f};
+  for (int i = 0; i < cnt; ++i) {
+    const int j = list[i];
+    if (j < 0 || j >= nbk) continue;  // uniform across the CTA
+    __syncthreads();
+    stage(j);
+    __syncthreads();
+    const int64_t k0 = static_cast<int64_t>(j) * kQTile;
+    float sa[4][4], pa[4][4];
+    products(sa, pa);
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+      const int r = r0 + 8 * hr;
+      float x[8], mx = -INFINITY;
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          x[2 * nt + e] = allowed(r, kc + 8 * nt + e, k0) ? sa[nt][2 * hr + e] * scale : -INFINITY;
+          mx = fmaxf(mx, x[2 * nt + e]);
+        }
+      const float mn = fmaxf(m[hr], quad_max(mx));
+      const float alpha = m[hr] == -INFINITY ? 0.f : expf(m[hr] - mn);
+      float ls = 0.f, lp = 0.f;
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float ex = x[2 * nt + e] == -INFINITY ? 0.f : expf(x[2 * nt + e] - mn);
+          ls += ex;
+          lp = fmaf(ex, pa[nt][2 * hr + e], lp);
+        }
+      l[hr] = fmaf(l[hr], alpha, quad_sum(ls));
+      pd[hr] = fmaf(pd[hr], alpha, quad_sum(lp));
+      m[hr] = mn;
+    }
+  }
+  // merge the two key halves of every row
+  if ((lane & 3) == 0)
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+      float *st = s_stat + (kh * kQTile + r0 + 8 * hr) * 3;
+      st[0] = m[hr];
+      st[1] = l[hr];
+      st[2] = pd[hr];
+    }
+  __syncthreads();
+  float lse[2], delta[2];
+#pragma unroll
+  for (int hr = 0; hr < 2; ++hr) {
+    const float *s0 = s_stat + (r0 + 8 * hr) * 3, *s1 = s_stat + (kQTile + r0 + 8 * hr) * 3;
+    const float mm = fmaxf(s0[0], s1[0]);
+    const float e0 = s0[0] == -INFINITY ? 0.f : expf(s0[0] - mm), e1 = s1[0] == -INFINITY ? 0.f : expf(s1[0] - mm);
+    const float ll = s0[1] * e0 + s1[1] * e1, pp = s0[2] * e0 + s1[2] * e1;
+    lse[hr] = ll > 0.f ? mm + logf(ll) : INFINITY;
+    delta[hr] = ll > 0.f ? pp / ll : 0.f;
+  }
+
+  // ---- pass 2: P, dS per block; dQ in registers, dK / dV atomically
+  float gq[4][4] = {};
+  for (int i = 0; i < cnt; ++i) {
+    const int j = list[i];
+    if (j < 0 || j >= nbk) continue;
+    __syncthreads();
+    stage(j);
+    __syncthreads();
+    const int64_t k0 = static_cast<int64_t>(j) * kQTile;
+    float sa[4][4], pa[4][4];
+    products(sa, pa);
+    bool any = false;
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+      const int r = r0 + 8 * hr;
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int key = kc + 8 * nt + e;
+          float p = 0.f, ds = 0.f;
+          if (allowed(r, key, k0)) {
+            p = expf(sa[nt][2 * hr + e] * scale - lse[hr]);
+            ds = p * (pa[nt][2 * hr + e] - delta[hr]);
+            any = true;
+          }
+          Ps[r * kLd + key] = p;
+          Ds[r * kLd + key] = ds;
+        }
+    }
+    if (!__syncthreads_or(any)) continue;  // no allowed pair in this block: nothing to add
+    mm_ab16(Ds, Kb, ti, tj, gq);  // dQ += dS K
+    float gk[4][4] = {}, gv[4][4] = {};
+    mm_atb16(Ds, Qb, ti, tj, gk);  // dK = dS^T Q
+    mm_atb16(Ps, Gb, ti, tj, gv);  // dV = P^T dO
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+      const int64_t kt = k0 + ti + 16 * a;
+      if (kt >= T_) continue;
+      const int64_t base = ((static_cast<int64_t>(b) * Hkv + h) * T_ + kt) * kHeadDim;
+#pragma unroll
+      for (int bb = 0; bb < 4; ++bb) {
+        atomicAdd(dk + base + tj + 16 * bb, scale * gk[a][bb]);
+        atomicAdd(dv + base + tj + 16 * bb, gv[a][bb]);
+      }
+    }
+  }
+#pragma unroll
+  for (int a = 0; a < 4; ++a) {
+    const int64_t t = t0 + ti + 16 * a;
+    if (t >= T_) continue;
+    float *dst = dq + ((static_cast<int64_t>(b) * T_ + t) * Hq + hq) * kHeadDim;
+#pragma unroll
+    for (int bb = 0; bb < 4; ++bb) dst[tj + 16 * bb] = scale * gq[a][bb];
+  }
+}
+
 }  // namespace bwd
 }  // namespace sd
 
@@ -290,6 +578,23 @@ extern "C" int sd_prefill_attention_backward(const void *q, const void *k, const
     return SD_ERR_CUDA;
   }
   const dim3 grid(static_cast<unsigned>(nqt), static_cast<unsigned>(Hq), static_cast<unsigned>(B));
+  // 16-bit inputs with 16-byte aligned rows: S and dP on the tensor cores
+  const bool rows16 = sd::aligned16(q) && sd::aligned16(k) && sd::aligned16(v) && sd::aligned16(dout) &&
+                      q_sb % 8 == 0 && q_st % 8 == 0 && q_sh % 8 == 0 && c_sb % 8 == 0 && c_sh % 8 == 0 &&
+                      c_st % 8 == 0 && g_sb % 8 == 0 && g_st % 8 == 0 && g_sh % 8 == 0;
+  if (dtype != SD_DTYPE_F32 && rows16) {
+    auto run = [&](auto kern, auto tag) {
+      using E = decltype(tag);
+      if (sd::set_max_smem(kern, sd::bwd::kSmemTcBytes) != SD_OK) return SD_ERR_CUDA;
+      kern<<<grid, sd::bwd::kThreads, sd::bwd::kSmemTcBytes, s>>>(
+          static_cast<const E *>(q), q_sb, q_st, q_sh, static_cast<const E *>(k), static_cast<const E *>(v), c_sb,
+          c_sh, c_st, static_cast<const E *>(dout), g_sb, g_st, g_sh, T, static_cast<int>(Hq), static_cast<int>(Hkv),
+          lists, counts, lcap, topk, kk, causal, scale, dq, dk, dv);
+      return sd::check_launch();
+    };
+    if (dtype == SD_DTYPE_BF16) return run(sd::bwd::prefill_bwd_tc_kernel<__nv_bfloat16>, __nv_bfloat16());
+    if (dtype == SD_DTYPE_F16) return run(sd::bwd::prefill_bwd_tc_kernel<__half>, __half());
+  }
   SD_DISPATCH_DTYPE(dtype, E, {
     auto kern = sd::bwd::prefill_bwd_kernel<E>;
     if (sd::set_max_smem(kern, sd::bwd::kSmemBytes) != SD_OK) return SD_ERR_CUDA;

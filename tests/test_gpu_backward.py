@@ -91,18 +91,20 @@ def test_backward_vs_oracle(dev, case, dtype):
         np.testing.assert_allclose(a, r, **TOL)
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16], ids=["f32", "bf16", "f16"])
 @torch.no_grad()
-def test_backward_ragged_batch_and_gqa_groups(dev):
+def test_backward_ragged_batch_and_gqa_groups(dev, dtype):
     """B = 3 sequences of T = 130 (a 2-row last q-block), G = 1, 2 and 4
-    query heads per kv head, chunked and masked lists: against the oracle."""
+    query heads per kv head, chunked and masked lists: against the oracle.
+    16-bit inputs run S and dP on the tensor cores, fp32 inputs on CUDA cores."""
     g = torch.Generator(device=dev).manual_seed(5)
     for hq, hkv in ((4, 4), (8, 4), (8, 2)):
         b, t = 3, 130
-        q = torch.randn(b, t, hq, 64, generator=g, device=dev)
-        k = torch.randn(b, hkv, t, 64, generator=g, device=dev)
-        v = torch.randn(b, hkv, t, 64, generator=g, device=dev)
-        go = torch.randn(b, t, hq, 64, generator=g, device=dev)
-        f = torch.randn(b, t, hkv, 64, generator=g, device=dev)
+        q = torch.randn(b, t, hq, 64, generator=g, device=dev).to(dtype)
+        k = torch.randn(b, hkv, t, 64, generator=g, device=dev).to(dtype)
+        v = torch.randn(b, hkv, t, 64, generator=g, device=dev).to(dtype)
+        go = torch.randn(b, t, hq, 64, generator=g, device=dev).to(dtype)
+        f = torch.randn(b, t, hkv, 64, generator=g, device=dev).to(dtype)
         for chunked in (False, True):
             reps = ops.compress_blocks(k.transpose(1, 2).contiguous(), 64)
             _, topk = ops.select_blocks(f, reps, 2, 64, not chunked, return_scores=False)
