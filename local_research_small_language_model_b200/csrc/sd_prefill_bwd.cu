@@ -18,7 +18,9 @@
 // and columns tj + 16b of each 64 x 64 result.  dQ rows belong to one CTA and
 // are stored; dK and dV of a key block collect contributions from every query
 // block and head that lists it and are added with fp32 atomics into buffers
-// the entry point zeroes first.
+// the entry point zeroes first.  16-bit inputs with 16-byte aligned rows take
+// prefill_bwd_tc_kernel below instead, which computes S and dP on the tensor
+// cores; this kernel serves fp32 inputs and other strides.
 #include "sd_prefill.cuh"
 #include "sd_tma.cuh"
 
