@@ -676,9 +676,8 @@ def _graph_time_s(fns):
 def run_backward(args, local: int):
     """Event-timed attention backward and forward of one prefill layer's
     shapes.  Per listed key block, query block and head the backward runs
-    seven 64x64x64 products: S and dP (twice: both passes) on the tensor
-    cores, dQ, dK and dV as fp32 CUDA-core products (the part reported against
-    the fp32 CUDA-core rate)."""
+    seven 64x64x64 products on the tensor cores (mma.sync): S and dP in both
+    passes, and dQ, dK, dV twice each (bf16 high and low parts of P and dS)."""
     import torch
     from local_research_small_language_model_b200 import ops
     dev = torch.device("cuda", local)
@@ -700,14 +699,16 @@ def run_backward(args, local: int):
     ops.check_device_errors(dev)
     blocks = int(counts.clamp_min(0).sum().item()) * (hq // hkv)
     per_product = 2 * 64 ** 3
-    fp32_peak = 148 * 128 * 2 * 1.965e9 / 1e12
-    simt = blocks * 3 * per_product  # dQ, dK, dV from the fp32 P and dS
-    return {"kernel": "sd::bwd::prefill_bwd_tc_kernel<bf16> (sd_prefill_attention_backward)",
+    flops = blocks * 7 * per_product  # S and dP in both passes, dQ, dK, dV
+    mma = blocks * (4 + 2 * 3) * per_product  # dQ, dK, dV run twice (bf16 high and low parts of P / dS)
+    peak = read_peak_tflops()
+    return {"kernel": "sd::bwd::prefill_bwd_tc_kernel<bf16, true> (sd_prefill_attention_backward)",
             "mode": mode, "seq_len": T, "us": round(bwd_s * 1e6, 2), "forward_us": round(fwd_s * 1e6, 2),
-            "flops": blocks * 7 * per_product, "tensor_flops": blocks * 4 * per_product, "simt_flops": simt,
-            "simt_tflops": round(simt / bwd_s / 1e12, 2), "fp32_simt_peak_tflops": round(fp32_peak, 1),
-            "simt_frac": round(simt / bwd_s / 1e12 / fp32_peak, 3),
-            "bound": "the three fp32 CUDA-core products (S and dP run on the tensor cores); at small T, too few CTAs"}
+            "flops": flops, "tflops": round(flops / bwd_s / 1e12, 2), "mma_flops": mma,
+            "mma_tflops": round(mma / bwd_s / 1e12, 2), "peak_bf16_tflops": peak[0],
+            "frac": round(mma / bwd_s / 1e12 / peak[0], 4), "peak_source": peak[1],
+            "bound": "mma.sync chains per 64-key block (legacy tensor path, 8 warps per CTA), the exponentials, "
+                     "fp32 atomics of dK / dV; at small T too few CTAs"}
 
 
 def run_kernels(local: int):

@@ -270,16 +270,25 @@ __global__ void __launch_bounds__(kThreads)
 // ---------------------------------------------------------------------------
 // 16-bit inputs: S = Q K^T and dP = dO V^T on the tensor cores (mma.sync
 // m16n8k16, fp32 accumulators).  A product of two 16-bit values is exact in
-// fp32, so these match the fp32 products above up to accumulation order.  The
-// three products that consume the fp32 P and dS stay fp32 CUDA-core products,
-// reading K, Q and dO from the same 16-bit tiles.  Warp w computes S / dP for
-// rows 16 (w % 4) .. +15 and keys 32 (w / 4) .. +31 of each block; pass 1 keeps
-// separate running statistics per key half, merged once at its end.
+// fp32, so these match the fp32 products above up to accumulation order.  Warp
+// w computes S / dP for rows 16 (w % 4) .. +15 and keys 32 (w / 4) .. +31 of
+// each block; pass 1 keeps separate running statistics per key half, merged
+// once at its end.  The three products that consume P and dS:
+//   * kMma (bf16): on the tensor cores too, with P and dS each split into a
+//     bf16 high part and the bf16 of the remainder (16 significant bits; each
+//     product runs twice and sums in fp32): dQ from dS tiles (ldmatrix) and
+//     K (ldmatrix.trans), dK / dV from dS^T / P^T (ldmatrix.trans) and Q / dO;
+//     warp w owns rows (dQ) or keys (dK, dV) 16 (w % 4) .. and head-dim
+//     columns 32 (w / 4) ..;
+//   * otherwise (f16, whose range could flush a small remainder): fp32
+//     CUDA-core products reading K, Q and dO from the same 16-bit tiles.
 // ---------------------------------------------------------------------------
 constexpr int kLdb = 72;  // 16-bit tile row stride in elements (144 bytes: ldmatrix rows on distinct banks)
 constexpr int kTileB = kQTile * kLdb;
-constexpr size_t kSmemTcBytes =
-    4 * kTileB * 2 + 2 * kTile * sizeof(float) + kQTile * sizeof(int) + 2 * kQTile * 3 * sizeof(float);
+// Q, dO, K, V tiles, then either the P / dS hi / lo tiles (kMma) or fp32 P and
+// dS (the larger of the two), the row flags and the pass-1 statistics
+constexpr size_t kPdBytes = 4 * kTileB * 2 > 2 * kTile * sizeof(float) ? 4 * kTileB * 2 : 2 * kTile * sizeof(float);
+constexpr size_t kSmemTcBytes = 4 * kTileB * 2 + kPdBytes + kQTile * sizeof(int) + 2 * kQTile * 3 * sizeof(float);
 
 // acc[a][b] += sum_x A[row a][x] * B[x][col b], B a 16-bit tile
 template <typename T>
@@ -325,7 +334,7 @@ __device__ __forceinline__ float quad_max(float x) {
   return fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 2));
 }
 
-template <typename T>
+template <typename T, bool kMma>
 __global__ void __launch_bounds__(kThreads, 2)
     prefill_bwd_tc_kernel(const T *__restrict__ q, int64_t q_sb, int64_t q_st, int64_t q_sh, const T *__restrict__ k,
                           const T *__restrict__ v, int64_t c_sb, int64_t c_sh, int64_t c_st,
@@ -338,9 +347,13 @@ __global__ void __launch_bounds__(kThreads, 2)
   T *Gb = Qb + kTileB;                   // dO [row][d]
   T *Kb = Gb + kTileB;                   // k of the block [key][d]
   T *Vb = Kb + kTileB;                   // v of the block [key][d]
-  float *Ps = reinterpret_cast<float *>(Vb + kTileB);  // P  [row][key]
+  float *Ps = reinterpret_cast<float *>(Vb + kTileB);  // P  [row][key] (fp32 products)
   float *Ds = Ps + kTile;                              // dS [row][key]
-  int *s_ok = reinterpret_cast<int *>(Ds + kTile);
+  T *Ph = Vb + kTileB;                                 // P  high / low parts [row][key] (kMma)
+  T *Pl = Ph + kTileB;
+  T *Dh = Pl + kTileB;                                 // dS high / low parts
+  T *Dl = Dh + kTileB;
+  int *s_ok = reinterpret_cast<int *>(smraw + 4 * kTileB * sizeof(T) + kPdBytes);
   float *s_stat = reinterpret_cast<float *>(s_ok + kQTile);  // [key half][row][m, l, pd]
 
   const int qt = blockIdx.x, hq = blockIdx.y, b = blockIdx.z;
@@ -498,7 +511,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
 
   // ---- pass 2: P, dS per block; dQ in registers, dK / dV atomically
-  float gq[4][4] = {};
+  float gq[4][4] = {};  // dQ: CUDA-core 4 x 4 blocks, or (kMma) this warp's MMA fragments
+  const int fg = lane >> 2, fc = lane & 3;  // fragment row group / column pair
   for (int i = 0; i < cnt; ++i) {
     const int j = list[i];
     if (j < 0 || j >= nbk) continue;
@@ -513,44 +527,130 @@ __global__ void __launch_bounds__(kThreads, 2)
     for (int hr = 0; hr < 2; ++hr) {
       const int r = r0 + 8 * hr;
 #pragma unroll
-      for (int nt = 0; nt < 4; ++nt)
+      for (int nt = 0; nt < 4; ++nt) {
+        const int key = kc + 8 * nt;
+        float p[2] = {0.f, 0.f}, ds[2] = {0.f, 0.f};
 #pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          const int key = kc + 8 * nt + e;
-          float p = 0.f, ds = 0.f;
-          if (allowed(r, key, k0)) {
-            p = expf(sa[nt][2 * hr + e] * scale - lse[hr]);
-            ds = p * (pa[nt][2 * hr + e] - delta[hr]);
+        for (int e = 0; e < 2; ++e)
+          if (allowed(r, key + e, k0)) {
+            p[e] = expf(sa[nt][2 * hr + e] * scale - lse[hr]);
+            ds[e] = p[e] * (pa[nt][2 * hr + e] - delta[hr]);
             any = true;
           }
-          Ps[r * kLd + key] = p;
-          Ds[r * kLd + key] = ds;
+        if constexpr (kMma) {
+          const float ph0 = to_f(from_f<T>(p[0])), ph1 = to_f(from_f<T>(p[1]));
+          const float dh0 = to_f(from_f<T>(ds[0])), dh1 = to_f(from_f<T>(ds[1]));
+          *reinterpret_cast<uint32_t *>(Ph + r * kLdb + key) = pack2<T>(ph0, ph1);
+          *reinterpret_cast<uint32_t *>(Pl + r * kLdb + key) = pack2<T>(p[0] - ph0, p[1] - ph1);
+          *reinterpret_cast<uint32_t *>(Dh + r * kLdb + key) = pack2<T>(dh0, dh1);
+          *reinterpret_cast<uint32_t *>(Dl + r * kLdb + key) = pack2<T>(ds[0] - dh0, ds[1] - dh1);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            Ps[r * kLd + key + e] = p[e];
+            Ds[r * kLd + key + e] = ds[e];
+          }
         }
+      }
     }
     if (!__syncthreads_or(any)) continue;  // no allowed pair in this block: nothing to add
-    mm_ab16(Ds, Kb, ti, tj, gq);  // dQ += dS K
-    float gk[4][4] = {}, gv[4][4] = {};
-    mm_atb16(Ds, Qb, ti, tj, gk);  // dK = dS^T Q
-    mm_atb16(Ps, Gb, ti, tj, gv);  // dV = P^T dO
+    if constexpr (kMma) {
+      // B fragments of a row-major [k][n] tile (K, Q or dO) for n-tiles n0, n0 + 8
+      auto ldb = [&](const T *tile, int k0r, int n0, uint32_t (&bf)[4]) {
+        ldsm_x4_t(smem_u32(tile + (k0r + (lane & 7) + ((lane >> 3) & 1) * 8) * kLdb + n0 + (lane >> 4) * 8), bf[0],
+                  bf[1], bf[2], bf[3]);
+      };
+      // dQ (rows 16 rg .., columns 32 kh ..) += (dS_hi + dS_lo) K
 #pragma unroll
-    for (int a = 0; a < 4; ++a) {
-      const int64_t kt = k0 + ti + 16 * a;
-      if (kt >= T_) continue;
-      const int64_t base = ((static_cast<int64_t>(b) * Hkv + h) * T_ + kt) * kHeadDim;
+      for (int ks = 0; ks < kQTile / 16; ++ks) {
+        uint32_t ah[4], al[4];
+        const int arow = 16 * rg + (lane & 15), acol = 16 * ks + (lane >> 4) * 8;
+        ldsm_x4(smem_u32(Dh + arow * kLdb + acol), ah[0], ah[1], ah[2], ah[3]);
+        ldsm_x4(smem_u32(Dl + arow * kLdb + acol), al[0], al[1], al[2], al[3]);
 #pragma unroll
-      for (int bb = 0; bb < 4; ++bb) {
-        atomicAdd(dk + base + tj + 16 * bb, scale * gk[a][bb]);
-        atomicAdd(dv + base + tj + 16 * bb, gv[a][bb]);
+        for (int np = 0; np < 2; ++np) {
+          uint32_t bk[4];
+          ldb(Kb, 16 * ks, 32 * kh + 16 * np, bk);
+          mma16816<T>(gq[2 * np], ah, bk[0], bk[1]);
+          mma16816<T>(gq[2 * np], al, bk[0], bk[1]);
+          mma16816<T>(gq[2 * np + 1], ah, bk[2], bk[3]);
+          mma16816<T>(gq[2 * np + 1], al, bk[2], bk[3]);
+        }
+      }
+      // dK = dS^T Q and dV = P^T dO for keys 16 rg .., columns 32 kh ..
+      float gk[4][4] = {}, gv[4][4] = {};
+#pragma unroll
+      for (int ks = 0; ks < kQTile / 16; ++ks) {
+        uint32_t dh[4], dl[4], phf[4], plf[4];
+        const int trow = 16 * ks + (lane & 7) + ((lane >> 4) << 3), tcol = 16 * rg + ((lane >> 3) & 1) * 8;
+        ldsm_x4_t(smem_u32(Dh + trow * kLdb + tcol), dh[0], dh[1], dh[2], dh[3]);
+        ldsm_x4_t(smem_u32(Dl + trow * kLdb + tcol), dl[0], dl[1], dl[2], dl[3]);
+        ldsm_x4_t(smem_u32(Ph + trow * kLdb + tcol), phf[0], phf[1], phf[2], phf[3]);
+        ldsm_x4_t(smem_u32(Pl + trow * kLdb + tcol), plf[0], plf[1], plf[2], plf[3]);
+#pragma unroll
+        for (int np = 0; np < 2; ++np) {
+          uint32_t bq[4], bg[4];
+          ldb(Qb, 16 * ks, 32 * kh + 16 * np, bq);
+          ldb(Gb, 16 * ks, 32 * kh + 16 * np, bg);
+          mma16816<T>(gk[2 * np], dh, bq[0], bq[1]);
+          mma16816<T>(gk[2 * np], dl, bq[0], bq[1]);
+          mma16816<T>(gk[2 * np + 1], dh, bq[2], bq[3]);
+          mma16816<T>(gk[2 * np + 1], dl, bq[2], bq[3]);
+          mma16816<T>(gv[2 * np], phf, bg[0], bg[1]);
+          mma16816<T>(gv[2 * np], plf, bg[0], bg[1]);
+          mma16816<T>(gv[2 * np + 1], phf, bg[2], bg[3]);
+          mma16816<T>(gv[2 * np + 1], plf, bg[2], bg[3]);
+        }
+      }
+#pragma unroll
+      for (int hr = 0; hr < 2; ++hr) {
+        const int64_t kt = k0 + 16 * rg + fg + 8 * hr;
+        if (kt >= T_) continue;
+        const int64_t base = ((static_cast<int64_t>(b) * Hkv + h) * T_ + kt) * kHeadDim + 32 * kh + 2 * fc;
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) {
+          atomicAdd(reinterpret_cast<float2 *>(dk + base + 8 * nt),
+                    make_float2(scale * gk[nt][2 * hr], scale * gk[nt][2 * hr + 1]));
+          atomicAdd(reinterpret_cast<float2 *>(dv + base + 8 * nt), make_float2(gv[nt][2 * hr], gv[nt][2 * hr + 1]));
+        }
+      }
+    } else {
+      mm_ab16(Ds, Kb, ti, tj, gq);  // dQ += dS K
+      float gk[4][4] = {}, gv[4][4] = {};
+      mm_atb16(Ds, Qb, ti, tj, gk);  // dK = dS^T Q
+      mm_atb16(Ps, Gb, ti, tj, gv);  // dV = P^T dO
+#pragma unroll
+      for (int a = 0; a < 4; ++a) {
+        const int64_t kt = k0 + ti + 16 * a;
+        if (kt >= T_) continue;
+        const int64_t base = ((static_cast<int64_t>(b) * Hkv + h) * T_ + kt) * kHeadDim;
+#pragma unroll
+        for (int bb = 0; bb < 4; ++bb) {
+          atomicAdd(dk + base + tj + 16 * bb, scale * gk[a][bb]);
+          atomicAdd(dv + base + tj + 16 * bb, gv[a][bb]);
+        }
       }
     }
   }
+  if constexpr (kMma) {
 #pragma unroll
-  for (int a = 0; a < 4; ++a) {
-    const int64_t t = t0 + ti + 16 * a;
-    if (t >= T_) continue;
-    float *dst = dq + ((static_cast<int64_t>(b) * T_ + t) * Hq + hq) * kHeadDim;
+    for (int hr = 0; hr < 2; ++hr) {
+      const int64_t t = t0 + 16 * rg + fg + 8 * hr;
+      if (t >= T_) continue;
+      float *dst = dq + ((static_cast<int64_t>(b) * T_ + t) * Hq + hq) * kHeadDim + 32 * kh + 2 * fc;
 #pragma unroll
-    for (int bb = 0; bb < 4; ++bb) dst[tj + 16 * bb] = scale * gq[a][bb];
+      for (int nt = 0; nt < 4; ++nt)
+        *reinterpret_cast<float2 *>(dst + 8 * nt) = make_float2(scale * gq[nt][2 * hr], scale * gq[nt][2 * hr + 1]);
+    }
+  } else {
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+      const int64_t t = t0 + ti + 16 * a;
+      if (t >= T_) continue;
+      float *dst = dq + ((static_cast<int64_t>(b) * T_ + t) * Hq + hq) * kHeadDim;
+#pragma unroll
+      for (int bb = 0; bb < 4; ++bb) dst[tj + 16 * bb] = scale * gq[a][bb];
+    }
   }
 }
 
@@ -594,8 +694,8 @@ extern "C" int sd_prefill_attention_backward(const void *q, const void *k, const
           lists, counts, lcap, topk, kk, causal, scale, dq, dk, dv);
       return sd::check_launch();
     };
-    if (dtype == SD_DTYPE_BF16) return run(sd::bwd::prefill_bwd_tc_kernel<__nv_bfloat16>, __nv_bfloat16());
-    if (dtype == SD_DTYPE_F16) return run(sd::bwd::prefill_bwd_tc_kernel<__half>, __half());
+    if (dtype == SD_DTYPE_BF16) return run(sd::bwd::prefill_bwd_tc_kernel<__nv_bfloat16, true>, __nv_bfloat16());
+    if (dtype == SD_DTYPE_F16) return run(sd::bwd::prefill_bwd_tc_kernel<__half, false>, __half());
   }
   SD_DISPATCH_DTYPE(dtype, E, {
     auto kern = sd::bwd::prefill_bwd_kernel<E>;
