@@ -288,7 +288,15 @@ constexpr int kTileB = kQTile * kLdb;
 // Q, dO, K, V tiles, then either the P / dS hi / lo tiles (kMma) or fp32 P and
 // dS (the larger of the two), the row flags and the pass-1 statistics
 constexpr size_t kPdBytes = 4 * kTileB * 2 > 2 * kTile * sizeof(float) ? 4 * kTileB * 2 : 2 * kTile * sizeof(float);
-constexpr size_t kSmemTcBytes = 4 * kTileB * 2 + kPdBytes + kQTile * sizeof(int) + 2 * kQTile * 3 * sizeof(float);
+constexpr size_t kSmemTcBytes = 6 * kTileB * 2 + kPdBytes + 2 * kQTile * sizeof(int) + 2 * kQTile * 3 * sizeof(float);
+
+// 16-byte asynchronous global -> shared copy; src_bytes = 0 fills zeros
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem)), "l"(gmem), "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 
 // acc[a][b] += sum_x A[row a][x] * B[x][col b], B a 16-bit tile
 template <typename T>
@@ -345,16 +353,17 @@ __global__ void __launch_bounds__(kThreads, 2)
   extern __shared__ __align__(16) char smraw[];
   T *Qb = reinterpret_cast<T *>(smraw);  // q  [row][d]
   T *Gb = Qb + kTileB;                   // dO [row][d]
-  T *Kb = Gb + kTileB;                   // k of the block [key][d]
-  T *Vb = Kb + kTileB;                   // v of the block [key][d]
-  float *Ps = reinterpret_cast<float *>(Vb + kTileB);  // P  [row][key] (fp32 products)
-  float *Ds = Ps + kTile;                              // dS [row][key]
-  T *Ph = Vb + kTileB;                                 // P  high / low parts [row][key] (kMma)
+  T *const Kbuf = Gb + kTileB;           // k, v of a block [key][d], two buffers: K0 V0 K1 V1
+  T *Kb = Kbuf, *Vb = Kbuf + kTileB;     // the buffer of the block being computed
+  float *Ps = reinterpret_cast<float *>(Kbuf + 4 * kTileB);  // P  [row][key] (fp32 products)
+  float *Ds = Ps + kTile;                                    // dS [row][key]
+  T *Ph = Kbuf + 4 * kTileB;                                 // P  high / low parts [row][key] (kMma)
   T *Pl = Ph + kTileB;
-  T *Dh = Pl + kTileB;                                 // dS high / low parts
+  T *Dh = Pl + kTileB;                                       // dS high / low parts
   T *Dl = Dh + kTileB;
-  int *s_ok = reinterpret_cast<int *>(smraw + 4 * kTileB * sizeof(T) + kPdBytes);
-  float *s_stat = reinterpret_cast<float *>(s_ok + kQTile);  // [key half][row][m, l, pd]
+  int *const s_okbuf = reinterpret_cast<int *>(smraw + 6 * kTileB * sizeof(T) + kPdBytes);  // [2][row]
+  int *s_ok = s_okbuf;
+  float *s_stat = reinterpret_cast<float *>(s_okbuf + 2 * kQTile);  // [key half][row][m, l, pd]
 
   const int qt = blockIdx.x, hq = blockIdx.y, b = blockIdx.z;
   const int G = Hq / Hkv, h = hq / G;
@@ -386,19 +395,20 @@ __global__ void __launch_bounds__(kThreads, 2)
   const T *kbase = k + b * c_sb + h * c_sh;
   const T *vbase = v + b * c_sb + h * c_sh;
 
-  auto stage = [&](int j) {
+  // copies block j's K / V rows into buffer `buf` (asynchronously, one
+  // commit group) and writes the rows' permissions for it
+  auto stage = [&](int j, int buf) {
     const int64_t k0 = static_cast<int64_t>(j) * kQTile;
+    T *kd = Kbuf + 2 * buf * kTileB, *vd = kd + kTileB;
     for (int e = tid; e < kQTile * kCh; e += kThreads) {
       const int c = e / kCh, c8 = (e - c * kCh) * 8;
       const int64_t kt = k0 + c;
-      uint4 xk = make_uint4(0u, 0u, 0u, 0u), xv = xk;
-      if (kt < T_) {
-        xk = *reinterpret_cast<const uint4 *>(kbase + kt * c_st + c8);
-        xv = *reinterpret_cast<const uint4 *>(vbase + kt * c_st + c8);
-      }
-      *reinterpret_cast<uint4 *>(Kb + c * kLdb + c8) = xk;
-      *reinterpret_cast<uint4 *>(Vb + c * kLdb + c8) = xv;
+      const bool in = kt < T_;
+      const int64_t src = in ? kt * c_st + c8 : 0;
+      cp_async16(kd + c * kLdb + c8, kbase + src, in ? 16 : 0);
+      cp_async16(vd + c * kLdb + c8, vbase + src, in ? 16 : 0);
     }
+    cp_async_commit();
     if (tid < kQTile) {
       const int64_t t = t0 + tid;
       bool ok = t < T_;
@@ -413,7 +423,35 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         ok = in;
       }
-      s_ok[tid] = ok ? 1 : 0;
+      s_okbuf[buf * kQTile + tid] = ok ? 1 : 0;
+    }
+  };
+  // next listed block at or after list position i (entries outside the cache are skipped)
+  auto next_valid = [&](int i) {
+    while (i < cnt && (list[i] < 0 || list[i] >= nbk)) ++i;
+    return i;
+  };
+  // walks the list with block i + 1's copies in flight while block i is
+  // computed; body(k0) runs with Kb / Vb / s_ok pointing at block i's buffer
+  auto walk = [&](auto &&body) {
+    int i = next_valid(0), buf = 0;
+    if (i < cnt) stage(list[i], 0);
+    while (i < cnt) {
+      const int inext = next_valid(i + 1);
+      __syncthreads();  // every thread is done with the other buffer (the previous block)
+      if (inext < cnt) {
+        stage(list[inext], buf ^ 1);
+      } else {
+        cp_async_commit();  // an empty group keeps the wait below uniform
+      }
+      cp_async_wait1();  // block i's copies (all groups but the newest) have landed
+      __syncthreads();
+      Kb = Kbuf + 2 * buf * kTileB;
+      Vb = Kb + kTileB;
+      s_ok = s_okbuf + buf * kQTile;
+      body(static_cast<int64_t>(list[i]) * kQTile);
+      buf ^= 1;
+      i = inext;
     }
   };
   auto allowed = [&](int r, int key, int64_t k0) {
@@ -453,13 +491,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   // ---- pass 1: per (row, key half) running maximum, sum of exponentials and
   // sum of exp * dP
   float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f}, pd[2] = {0.f, 0.f};
-  for (int i = 0; i < cnt; ++i) {
-    const int j = list[i];
-    if (j < 0 || j >= nbk) continue;  // uniform across the CTA
-    __syncthreads();
-    stage(j);
-    __syncthreads();
-    const int64_t k0 = static_cast<int64_t>(j) * kQTile;
+  walk([&](int64_t k0) {
     float sa[4][4], pa[4][4];
     products(sa, pa);
 #pragma unroll
@@ -488,7 +520,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       pd[hr] = fmaf(pd[hr], alpha, quad_sum(lp));
       m[hr] = mn;
     }
-  }
+  });
   // merge the two key halves of every row
   if ((lane & 3) == 0)
 #pragma unroll
@@ -513,13 +545,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   // ---- pass 2: P, dS per block; dQ in registers, dK / dV atomically
   float gq[4][4] = {};  // dQ: CUDA-core 4 x 4 blocks, or (kMma) this warp's MMA fragments
   const int fg = lane >> 2, fc = lane & 3;  // fragment row group / column pair
-  for (int i = 0; i < cnt; ++i) {
-    const int j = list[i];
-    if (j < 0 || j >= nbk) continue;
-    __syncthreads();
-    stage(j);
-    __syncthreads();
-    const int64_t k0 = static_cast<int64_t>(j) * kQTile;
+  walk([&](int64_t k0) {
     float sa[4][4], pa[4][4];
     products(sa, pa);
     bool any = false;
@@ -553,7 +579,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
       }
     }
-    if (!__syncthreads_or(any)) continue;  // no allowed pair in this block: nothing to add
+    if (!__syncthreads_or(any)) return;  // no allowed pair in this block: nothing to add
     if constexpr (kMma) {
       // B fragments of a row-major [k][n] tile (K, Q or dO) for n-tiles n0, n0 + 8
       auto ldb = [&](const T *tile, int k0r, int n0, uint32_t (&bf)[4]) {
@@ -631,7 +657,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
       }
     }
-  }
+  });
   if constexpr (kMma) {
 #pragma unroll
     for (int hr = 0; hr < 2; ++hr) {
