@@ -274,8 +274,10 @@ SD_API int sd_prefill_attention(const void *q, int dtype, int64_t B, int64_t T, 
  * dout [B,T,Hq,D] (element strides g_sb, g_st, g_sh) is the gradient of the
  * output, all four in `dtype`.  Writes fp32 dq [B,T,Hq,D] and dk, dv
  * [B,Hkv,T,D], all contiguous; dk and dv are zeroed on the stream first.  The
- * softmax is recomputed exactly in fp32 (no forward statistics needed).
- * D == 64, block_size == 64. */
+ * softmax is recomputed in fp32 (no forward statistics needed).  16-bit inputs
+ * with 16-byte aligned rows run the products on the tensor cores (bf16: P and
+ * dS split into high and low bf16 parts), fp32 inputs on CUDA cores; all
+ * paths give fp32-level gradients.  D == 64, block_size == 64. */
 SD_API int sd_prefill_attention_backward(const void *q, const void *k, const void *v, const void *dout,
                                          int dtype, int64_t B, int64_t T, int64_t Hq, int64_t Hkv, int64_t D,
                                          int64_t q_sb, int64_t q_st, int64_t q_sh, int64_t c_sb, int64_t c_sh,

@@ -19,8 +19,8 @@
 // are stored; dK and dV of a key block collect contributions from every query
 // block and head that lists it and are added with fp32 atomics into buffers
 // the entry point zeroes first.  16-bit inputs with 16-byte aligned rows take
-// prefill_bwd_tc_kernel below instead, which computes S and dP on the tensor
-// cores; this kernel serves fp32 inputs and other strides.
+// prefill_bwd_tc_kernel below instead (tensor-core products: all seven for
+// bf16, S and dP for f16); this kernel serves fp32 inputs and other strides.
 #include "sd_prefill.cuh"
 #include "sd_tma.cuh"
 
