@@ -457,3 +457,23 @@ def test_attention_backward_finite_differences():
             fd = (up - loss(*args)) / (2 * eps)
             assert abs(fd - gx[ix]) <= 1e-6 * max(1.0, abs(fd)), (which, ix, fd, gx[ix])
     assert np.all(dq[:, 2:4, 3] == 0)  # query heads 2, 3 use kv head 1's empty row
+
+
+def test_mask_helpers_match_the_oracle_paths():
+    """masked_allowed_from_topk equals masked_allowed's mask for the same top-k,
+    and attention over chunked_allowed equals chunked_attention on the same
+    lists: the two helpers the GPU backward tests build their masks with."""
+    b, t = 2, 300
+    q, k, v = normal((b, 12, t, 64), seed=901), normal((b, 4, t, 64), seed=902), normal((b, 4, t, 64), seed=903)
+    f = normal((b, t, 4, 64), seed=904)
+    reps = O.compress_blocks(k.transpose(0, 2, 1, 3), 64)
+    _, topk = O.select_blocks(f, reps, 3, 64, True)
+    for causal in (True, False):
+        want, _, _ = O.masked_allowed(f, k, t, 64, 3, 1, "forecast", causal)
+        _, topk_c = O.select_blocks(f, reps, 3, 64, causal)
+        assert np.array_equal(O.masked_allowed_from_topk(topk_c, t, 64, causal), want)
+    dense, _, _ = O.masked_allowed(None, k, t, 64, 3, 0, "forecast", True)
+    assert np.array_equal(O.masked_allowed_from_topk(None, t, 64, True), dense)
+    sel, cnt, _ = O.chunked_select(f, reps, t, 64, 3, b, 4, "forecast")
+    np.testing.assert_allclose(O.attention_forward(q, k, v, O.chunked_allowed(sel, cnt, t, 64)),
+                               O.chunked_attention(q, k, v, sel, cnt, 64), rtol=0, atol=1e-12)
