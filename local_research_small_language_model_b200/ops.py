@@ -402,12 +402,39 @@ def prefill_lists(mode: str, batch: int, n_kv_head: int, seq_len: int, block_siz
     return lists, counts
 
 
+def _check_prefill_shapes(q, k, v, lists, counts, topk, block_size, dout=None):
+    """Shapes the prefill kernels index by, checked before any launch: q (and
+    dout) [B,T,Hq,D]; k, v [>=B, Hkv, >=T, D] (cache views may hold more
+    sequences or positions); lists [B,Hkv,NQ,cap] and counts [B,Hkv,NQ] int32
+    contiguous (NQ = ceil(T / block_size)); topk [B,Hkv,T,k]."""
+    if q.dim() != 4:
+        raise ValueError(f"q must be [B, T, Hq, D], got {tuple(q.shape)}")
+    b, t, hq, d = q.shape
+    if dout is not None and tuple(dout.shape) != tuple(q.shape):
+        raise ValueError(f"dout must have q's shape {tuple(q.shape)}, got {tuple(dout.shape)}")
+    if k.dim() != 4 or tuple(k.shape) != tuple(v.shape) or k.shape[0] < b or k.shape[2] < t or k.shape[3] != d:
+        raise ValueError(f"k and v must be [>={b}, Hkv, >={t}, {d}], got {tuple(k.shape)} and {tuple(v.shape)}")
+    hkv = k.shape[1]
+    if hq % hkv:
+        raise ValueError(f"query heads ({hq}) must be a multiple of kv heads ({hkv})")
+    nq = num_blocks(t, block_size)
+    if lists.dim() != 4 or tuple(lists.shape[:3]) != (b, hkv, nq) or tuple(counts.shape) != (b, hkv, nq):
+        raise ValueError(f"lists must be [{b}, {hkv}, {nq}, cap] and counts [{b}, {hkv}, {nq}], got "
+                         f"{tuple(lists.shape)} and {tuple(counts.shape)}")
+    if lists.dtype != torch.int32 or counts.dtype != torch.int32 or not lists.is_contiguous() \
+            or not counts.is_contiguous():
+        raise ValueError("lists and counts must be contiguous int32 (as prefill_lists returns them)")
+    if topk is not None and (topk.dim() != 4 or tuple(topk.shape[:3]) != (b, hkv, t)):
+        raise ValueError(f"topk must be [{b}, {hkv}, {t}, k], got {tuple(topk.shape)}")
+
+
 def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, lists: torch.Tensor, counts: torch.Tensor,
                       block_size: int, topk: Optional[torch.Tensor] = None, causal: bool = True,
                       scale: Optional[float] = None) -> torch.Tensor:
     """Block-sparse GQA prefill attention over prefill_lists' lists.
     q [B,T,Hq,D]; k, v [B,Hkv,T,D] views (same strides); topk [B,H,T,k] for
     per-row membership (masked forecast mode).  Returns [B,T,Hq,D]."""
+    _check_prefill_shapes(q, k, v, lists, counts, topk, block_size)
     _cuda(q, k, v, lists, counts, topk)
     b, t, hq, d = q.shape
     hkv = k.shape[1]
@@ -437,6 +464,7 @@ def prefill_attention_backward(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor
     (the backward of the reference's masked / chunked SDPA, sparse.py:185-364):
     same q, k, v, lists and topk as the forward.  Returns fp32 (dq [B,T,Hq,D],
     dk [B,Hkv,T,D], dv [B,Hkv,T,D])."""
+    _check_prefill_shapes(q, k, v, lists, counts, topk, block_size, dout)
     _cuda(q, k, v, dout, lists, counts, topk)
     b, t, hq, d = q.shape
     hkv = k.shape[1]

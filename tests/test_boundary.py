@@ -122,3 +122,42 @@ def test_rope_tables_stay_fp32_under_module_cast():
     with pytest.raises(ValueError):
         ops._rope_tables(rot.cos, rot.sin, 64, 1024)
     ops._rope_tables(rot.cos, rot.sin, 64, 256)
+
+
+def test_prefill_wrappers_reject_mismatched_shapes_before_launch():
+    """ops.prefill_attention / prefill_attention_backward check every shape the
+    kernels index by before anything reaches the device (so a wrong list or
+    gradient tensor cannot make a kernel read out of bounds); correctly shaped
+    CPU tensors get as far as the CUDA check."""
+    import pytest
+    import torch
+    from local_research_small_language_model_b200 import ops
+
+    b, t, hq, hkv, d = 2, 130, 6, 2, 64
+    q = torch.zeros(b, t, hq, d)
+    k = torch.zeros(b, hkv, t, d)
+    lists = torch.zeros(b, hkv, 3, 10, dtype=torch.int32)
+    counts = torch.zeros(b, hkv, 3, dtype=torch.int32)
+    topk = torch.zeros(b, hkv, t, 8, dtype=torch.int64)
+    bad = {
+        "k and v must be": dict(k=torch.zeros(b, hkv, t - 1, d)),
+        "multiple of kv heads": dict(k=torch.zeros(b, 4, t, d)),
+        "lists must be": dict(lists=torch.zeros(b, hkv, 2, 10, dtype=torch.int32)),
+        "contiguous int32": dict(counts=torch.zeros(b, hkv, 3, dtype=torch.int64)),
+        "topk must be": dict(topk=torch.zeros(b, hkv, t - 1, 8, dtype=torch.int64)),
+    }
+    for msg, over in bad.items():
+        a = dict(q=q, k=k, v=k, lists=lists, counts=counts, topk=topk)
+        a.update(over)
+        if "k" in over:
+            a["v"] = a["k"]
+        with pytest.raises(ValueError, match=msg):
+            ops.prefill_attention(a["q"], a["k"], a["v"], a["lists"], a["counts"], 64, a["topk"])
+    with pytest.raises(ValueError, match="dout must have"):
+        ops.prefill_attention_backward(q, k, k, torch.zeros(b, t, hq, d - 1), lists, counts, 64, topk)
+    # a cache view holding more sequences and positions than the prompt is fine
+    big = torch.zeros(b + 1, hkv, t + 64, d)[:, :, :t + 10]
+    for call in (lambda: ops.prefill_attention(q, big, big, lists, counts, 64, topk),
+                 lambda: ops.prefill_attention_backward(q, big, big, q, lists, counts, 64, topk)):
+        with pytest.raises(ValueError, match="need CUDA tensors"):
+            call()
