@@ -186,9 +186,17 @@ def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     """Block-sparse GQA decode attention (model/attention/sparse.py:156-181).
     q [B,Hq,D]; caches [B,Hkv,Tcap,D] views (any strides with inner 1, same for K
     and V); sel/cnt from decode_select.  Returns [B,Hq,D] in q's dtype."""
-    _cuda(q, k_cache, v_cache, sel, cnt)
+    if q.dim() != 3 or k_cache.dim() != 4 or tuple(k_cache.shape) != tuple(v_cache.shape):
+        raise ValueError(f"q must be [B, Hq, D] and the caches [B, Hkv, Tcap, D] alike, got {tuple(q.shape)}, "
+                         f"{tuple(k_cache.shape)}, {tuple(v_cache.shape)}")
     b, hq, d = q.shape
     hkv, tcap = k_cache.shape[1], k_cache.shape[2]
+    if k_cache.shape[0] < b or k_cache.shape[3] != d or hq % hkv or not 0 < seq_len_k <= tcap:
+        raise ValueError(f"caches {tuple(k_cache.shape)} do not fit q {tuple(q.shape)} at length {seq_len_k}")
+    if sel.dim() != 3 or tuple(sel.shape[:2]) != (b, hkv) or tuple(cnt.shape) != (b, hkv):
+        raise ValueError(f"sel must be [{b}, {hkv}, ms] and cnt [{b}, {hkv}], got {tuple(sel.shape)}, "
+                         f"{tuple(cnt.shape)}")
+    _cuda(q, k_cache, v_cache, sel, cnt)
     if k_cache.stride() != v_cache.stride():
         raise ValueError("K and V caches must share strides")
     q = _inner1(q)
@@ -209,6 +217,17 @@ def kv_append(xk: torch.Tensor, xv: torch.Tensor, k_store: torch.Tensor, v_store
               proto_sum: torch.Tensor, start: int, block_size: int) -> None:
     """Writes xk, xv [B,T,H,D] into the head-major stores [B,H,Tcap,D] at
     positions start.. and refreshes the block sums [B,H,NBcap,D] they touch."""
+    if xk.dim() != 4 or tuple(xk.shape) != tuple(xv.shape) or tuple(k_store.shape) != tuple(v_store.shape) \
+            or k_store.dim() != 4 or proto_sum.dim() != 4:
+        raise ValueError(f"xk, xv must be [B, T, H, D] alike and the stores [B, H, Tcap, D] alike, got "
+                         f"{tuple(xk.shape)}, {tuple(xv.shape)}, {tuple(k_store.shape)}, {tuple(v_store.shape)}")
+    b_, t_, h_, d_ = xk.shape
+    if k_store.shape[0] < b_ or k_store.shape[1] != h_ or k_store.shape[3] != d_ or \
+            proto_sum.shape[0] < b_ or proto_sum.shape[1] != h_ or proto_sum.shape[3] != d_ or \
+            proto_sum.dtype != torch.float32 or not (proto_sum.is_contiguous() and k_store.is_contiguous()
+                                                     and v_store.is_contiguous()):
+        raise ValueError(f"stores {tuple(k_store.shape)} / sums {tuple(proto_sum.shape)} do not fit "
+                         f"[{b_}, {t_}, {h_}, {d_}] rows (contiguous stores, fp32 sums)")
     _cuda(xk, xv, k_store, v_store, proto_sum)
     xk, xv = _inner1(xk.to(k_store.dtype)), _inner1(xv.to(v_store.dtype))
     b, t, h, d = xk.shape

@@ -161,3 +161,35 @@ def test_prefill_wrappers_reject_mismatched_shapes_before_launch():
                  lambda: ops.prefill_attention_backward(q, big, big, q, lists, counts, 64, topk)):
         with pytest.raises(ValueError, match="need CUDA tensors"):
             call()
+
+
+def test_decode_and_append_wrappers_reject_mismatched_shapes():
+    """ops.decode_attention and ops.kv_append check the shapes their kernels
+    index by before the CUDA check (the stores and sums may be sized for more
+    sequences than the call uses)."""
+    import pytest
+    import torch
+    from local_research_small_language_model_b200 import ops
+
+    q = torch.zeros(2, 12, 64)
+    kc = torch.zeros(2, 4, 256, 64)
+    sel, cnt = torch.zeros(2, 4, 10, dtype=torch.int32), torch.zeros(2, 4, dtype=torch.int32)
+    with pytest.raises(ValueError, match="do not fit"):
+        ops.decode_attention(q, kc[:1], kc[:1], sel, cnt, 100, 64)
+    with pytest.raises(ValueError, match="do not fit"):
+        ops.decode_attention(q, kc, kc, sel, cnt, 300, 64)
+    with pytest.raises(ValueError, match="sel must be"):
+        ops.decode_attention(q, kc, kc, sel[:, :3], cnt, 100, 64)
+    with pytest.raises(ValueError, match="need CUDA tensors"):
+        ops.decode_attention(q, kc, kc, sel, cnt, 100, 64)
+    xk = torch.zeros(2, 70, 4, 64)
+    store = torch.zeros(3, 4, 256, 64)
+    sums = torch.zeros(3, 4, 4, 64)
+    with pytest.raises(ValueError, match="do not fit"):
+        ops.kv_append(xk, xk, store[:, :2].contiguous(), store[:, :2].contiguous(), sums, 0, 64)
+    with pytest.raises(ValueError, match="do not fit"):
+        ops.kv_append(xk, xk, store, store, sums.double(), 0, 64)
+    with pytest.raises(ValueError, match="alike"):
+        ops.kv_append(xk, xk[:, :69], store, store, sums, 0, 64)
+    with pytest.raises(ValueError, match="need CUDA tensors"):
+        ops.kv_append(xk, xk, store[:2], store[:2], sums, 0, 64)
