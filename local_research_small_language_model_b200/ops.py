@@ -128,6 +128,10 @@ def gather_kv_blocks(k: torch.Tensor, v: torch.Tensor, block_indices: torch.Tens
     indices [B,H,S] -> [B,H,S*block_size,D].  k and v may also be pinned host
     tensors (an offloaded cache): the kernel on ``device`` then reads the
     selected rows straight from host memory."""
+    if k.dim() != 4 or tuple(k.shape) != tuple(v.shape) or block_indices.dim() != 3 \
+            or tuple(block_indices.shape[:2]) != tuple(k.shape[:2]):
+        raise ValueError(f"k, v must be [B, H, T, D] alike and the indices [B, H, S], got {tuple(k.shape)}, "
+                         f"{tuple(v.shape)}, {tuple(block_indices.shape)}")
     if not k.is_cuda or not v.is_cuda:
         if not (k.is_pinned() and v.is_pinned()) or device is None:
             raise ValueError("host K/V must be pinned, and the gather needs a target device")
@@ -163,6 +167,12 @@ def decode_select(forecast: Optional[torch.Tensor], reps: Optional[torch.Tensor]
     Returns sel int32 [B,H,MS] (ascending, -1 padded) and cnt int32 [B,H]."""
     nb = num_blocks(seq_len_k, block_size)
     ms = min(nb, top_k + 2)
+    if forecast is not None:
+        if reps is None or reps.dim() != 4 or reps.shape[0] < batch or reps.shape[1] < nb \
+                or tuple(reps.shape[2:]) != (n_kv_head, head_dim) or forecast.numel() != batch * n_kv_head * head_dim:
+            raise ValueError(f"forecast must hold [{batch}, {n_kv_head}, {head_dim}] and reps be "
+                             f"[>={batch}, >={nb}, {n_kv_head}, {head_dim}], got "
+                             f"{tuple(forecast.shape)} and {None if reps is None else tuple(reps.shape)}")
     dev = forecast.device if forecast is not None else (reps.device if reps is not None else device)
     _cuda(forecast, reps)
     sel = torch.empty(batch, n_kv_head, ms, dtype=torch.int32, device=dev)

@@ -193,3 +193,20 @@ def test_decode_and_append_wrappers_reject_mismatched_shapes():
         ops.kv_append(xk, xk[:, :69], store, store, sums, 0, 64)
     with pytest.raises(ValueError, match="need CUDA tensors"):
         ops.kv_append(xk, xk, store[:2], store[:2], sums, 0, 64)
+
+
+def test_gather_and_select_wrappers_reject_mismatched_shapes():
+    import pytest
+    import torch
+    from local_research_small_language_model_b200 import ops
+
+    k = torch.zeros(2, 4, 640, 64)
+    with pytest.raises(ValueError, match="indices"):
+        ops.gather_kv_blocks(k, k, torch.zeros(1, 4, 10, dtype=torch.int64), 64)
+    with pytest.raises(ValueError, match="pinned"):  # well-shaped host K/V: the pinned-host rule applies next
+        ops.gather_kv_blocks(k, k, torch.zeros(2, 4, 10, dtype=torch.int64), 64)
+    f = torch.zeros(2, 1, 4, 64)
+    with pytest.raises(ValueError, match="reps be"):
+        ops.decode_select(f, torch.zeros(2, 9, 4, 64), 600, 2, 4, 64, 64, 8)  # 600 tokens = 10 blocks
+    with pytest.raises(ValueError, match="need CUDA tensors"):
+        ops.decode_select(f, torch.zeros(2, 10, 4, 64), 600, 2, 4, 64, 64, 8)
