@@ -210,3 +210,24 @@ def test_gather_and_select_wrappers_reject_mismatched_shapes():
         ops.decode_select(f, torch.zeros(2, 9, 4, 64), 600, 2, 4, 64, 64, 8)  # 600 tokens = 10 blocks
     with pytest.raises(ValueError, match="need CUDA tensors"):
         ops.decode_select(f, torch.zeros(2, 10, 4, 64), 600, 2, 4, 64, 64, 8)
+
+
+def test_rope_transpose_is_rope_with_negated_sin():
+    """The backward of RoPE that the training path uses (_RopeQK: the same
+    rotation with -sin) equals autograd's gradient through the reference-order
+    rotation (apply_rotary_emb, fp32, CPU)."""
+    import torch
+    from local_research_small_language_model_b200.rope import apply_rotary_emb, precompute_rope_freqs
+
+    torch.manual_seed(0)
+    cos, sin = precompute_rope_freqs(64, 200)
+    q = torch.randn(2, 37, 12, 64, dtype=torch.float64, requires_grad=True)
+    k = torch.randn(2, 37, 4, 64, dtype=torch.float64, requires_grad=True)
+    gq, gk = torch.randn(2, 37, 12, 64, dtype=torch.float64), torch.randn(2, 37, 4, 64, dtype=torch.float64)
+    c64, s64 = cos.double(), sin.double()
+    for offset in (0, 100):
+        qr, kr = apply_rotary_emb(q, k, c64, s64, offset)
+        dq, dk = torch.autograd.grad((qr * gq).sum() + (kr * gk).sum(), (q, k))
+        tq, tk = apply_rotary_emb(gq, gk, c64, -s64, offset)
+        torch.testing.assert_close(tq, dq, rtol=0, atol=1e-12)
+        torch.testing.assert_close(tk, dk, rtol=0, atol=1e-12)
